@@ -1,0 +1,75 @@
+"""Build the native libraries in-tree (``python -m commux_b200.build``).
+
+Runs CMake + Ninja into ``<repo>/build`` and places the outputs inside the
+package: ``commux_b200/lib/libcommux{,_io,_cuda}.so``, ``commux_b200/_C*.so``
+and the C++ test driver ``commux_b200/lib/test_commux``. CUDA code is compiled
+for sm_100a only (``-gencode arch=compute_100a,code=sm_100a``); nvcc
+cross-compiles, so no GPU is needed to build.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(PKG_DIR)
+
+
+def _has_cuda_sources() -> bool:
+    d = os.path.join(PKG_DIR, "csrc", "cuda")
+    return os.path.isdir(d) and any(f.endswith(".cu") for f in os.listdir(d))
+
+
+def build(build_dir: str | None = None, jobs: int | None = None, verbose: bool = False,
+          sanitize: str = "", device_checks: bool = False, cuda: bool | None = None) -> None:
+    build_dir = build_dir or os.path.join(REPO, "build" if not sanitize else f"build-{sanitize}")
+    os.makedirs(build_dir, exist_ok=True)
+    if cuda is None:
+        cuda = _has_cuda_sources() and os.path.exists("/usr/local/cuda/bin/nvcc")
+    gen = ["-G", "Ninja"] if shutil.which("ninja") else []
+    cfg = ["cmake", "-S", REPO, "-B", build_dir, *gen,
+           f"-DPython3_EXECUTABLE={sys.executable}",
+           f"-DCOMMUX_CUDA={'ON' if cuda else 'OFF'}",
+           f"-DCOMMUX_DEVICE_CHECKS={'ON' if device_checks else 'OFF'}",
+           "-DCMAKE_BUILD_TYPE=Release"]
+    if sanitize:
+        cfg.append(f"-DCOMMUX_SANITIZE={sanitize}")
+    env = dict(os.environ)
+    env.setdefault("CUDACXX", "/usr/local/cuda/bin/nvcc")
+    out = None if verbose else subprocess.PIPE
+    r = subprocess.run(cfg, env=env, stdout=out, stderr=subprocess.STDOUT, text=True)
+    if r.returncode != 0:
+        sys.stderr.write(r.stdout or "")
+        raise RuntimeError("commux: cmake configure failed")
+    cmd = ["cmake", "--build", build_dir, "-j", str(jobs or os.cpu_count() or 4)]
+    r = subprocess.run(cmd, env=env, stdout=out, stderr=subprocess.STDOUT, text=True)
+    if r.returncode != 0:
+        sys.stderr.write(r.stdout or "")
+        raise RuntimeError("commux: native build failed")
+    if not verbose and r.stdout:
+        # keep the ptxas register/spill report around for inspection
+        with open(os.path.join(build_dir, "build.log"), "w") as f:
+            f.write(r.stdout)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--build-dir")
+    ap.add_argument("-j", "--jobs", type=int)
+    ap.add_argument("-v", "--verbose", action="store_true")
+    ap.add_argument("--sanitize", default="", help="thread or address (host code)")
+    ap.add_argument("--device-checks", action="store_true",
+                    help="kernels bounds-check descriptors and report instead of faulting")
+    ap.add_argument("--no-cuda", action="store_true")
+    a = ap.parse_args()
+    build(a.build_dir, a.jobs, a.verbose, a.sanitize, a.device_checks,
+          cuda=False if a.no_cuda else None)
+    print("commux: build ok")
+
+
+if __name__ == "__main__":
+    main()

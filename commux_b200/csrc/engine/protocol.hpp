@@ -1,0 +1,92 @@
+#pragma once
+
+// Records exchanged over the shared-memory rings. Every record starts with a
+// shm::WireHdr; the producing rank is implicit (ring index).
+//
+// Host (CPU tensor) messages:
+//   EAGER  first fragment of a message <= eager limit: key, total, msg id
+//   FRAG   continuation bytes of an EAGER message or of a rendezvous DATA
+//          stream (msg id in the sender's id space for EAGER, recv id with
+//          kDataBit for DATA)
+//   RTS    request-to-send for a large host message (no payload)
+//   CTS    clear-to-send: receiver matched an RTS, names its recv id
+// Device (CUDA tensor) messages:
+//   DRTS   device request-to-send: sender's IPC descriptors and flag slot;
+//          the receiver pulls the bytes with a kernel
+//   FIN    receiver -> sender: the transfer of send id is complete
+// Control:
+//   ABORT  the producer aborts the group (code, reason)
+
+#include <cstdint>
+
+#include "shm.hpp"
+
+namespace commux {
+namespace proto {
+
+enum : std::uint16_t {
+  kEager = 1,
+  kFrag = 2,
+  kRts = 3,
+  kCts = 4,
+  kDrts = 5,
+  kFin = 6,
+  kAbort = 7,
+};
+
+constexpr std::uint64_t kDataBit = 1ull << 63;
+
+struct EagerRec {
+  shm::WireHdr h;
+  std::uint64_t key;     // match key (tag without the rank field)
+  std::uint64_t total;   // message bytes
+  std::uint64_t msg_id;  // sender id of this message
+  std::uint64_t nbytes;  // payload bytes in this record
+  // payload follows
+};
+
+struct FragRec {
+  shm::WireHdr h;
+  std::uint64_t msg_id;
+  std::uint64_t offset;
+  std::uint64_t nbytes;
+  // payload follows
+};
+
+struct RtsRec {
+  shm::WireHdr h;
+  std::uint64_t key;
+  std::uint64_t total;
+  std::uint64_t send_id;
+};
+
+struct CtsRec {
+  shm::WireHdr h;
+  std::uint64_t send_id;
+  std::uint64_t recv_id;
+};
+
+struct DrtsRec {
+  shm::WireHdr h;
+  std::uint64_t key;
+  std::uint64_t total;
+  std::uint64_t send_id;
+  std::uint32_t blob_bytes;  // device descriptor blob (opaque to the engine)
+  std::uint32_t pad;
+  // blob follows
+};
+
+struct FinRec {
+  shm::WireHdr h;
+  std::uint64_t send_id;
+  std::int64_t status;  // 0 ok, else error code
+};
+
+struct AbortRec {
+  shm::WireHdr h;
+  std::int64_t code;
+  char reason[112];
+};
+
+}  // namespace proto
+}  // namespace commux
