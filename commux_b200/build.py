@@ -40,6 +40,17 @@ def build(build_dir: str | None = None, jobs: int | None = None, verbose: bool =
         cfg.append(f"-DCOMMUX_SANITIZE={sanitize}")
     env = dict(os.environ)
     env.setdefault("CUDACXX", "/usr/local/cuda/bin/nvcc")
+    # Use the system compiler, which links the shared libstdc++ that torch
+    # uses. A toolchain that links libstdc++ statically gives each library
+    # private iostream/locale state, and that crashes as soon as one of them
+    # formats an exception message coming from torch.
+    cxx = os.environ.get("COMMUX_CXX", "/usr/bin/g++")
+    cc = os.environ.get("COMMUX_CC", "/usr/bin/gcc")
+    if os.path.exists(cxx):
+        env["CXX"] = cxx
+        cfg.append(f"-DCMAKE_CUDA_HOST_COMPILER={cxx}")
+    if os.path.exists(cc):
+        env["CC"] = cc
     out = None if verbose else subprocess.PIPE
     r = subprocess.run(cfg, env=env, stdout=out, stderr=subprocess.STDOUT, text=True)
     if r.returncode != 0:

@@ -112,6 +112,12 @@ class CommuxWork : public c10d::Work {
     std::lock_guard<std::mutex> lk(mu_);
     dev_.push_back(std::move(d));
   }
+  // CPU receive into a strided view: the bytes land in `tmp`, copied into
+  // `view` once the receive completed.
+  void add_unpack(at::Tensor tmp, at::Tensor view) {
+    std::lock_guard<std::mutex> lk(mu_);
+    unpack_.push_back({std::move(tmp), std::move(view)});
+  }
   void set_source(int s) { source_rank_ = s; }
 
   bool isCompleted() override {
@@ -130,6 +136,7 @@ class CommuxWork : public c10d::Work {
     }
     for (auto& d : dev_)
       if (!d->query()) return false;
+    unpack_locked();
     return true;
   }
 
@@ -161,8 +168,10 @@ class CommuxWork : public c10d::Work {
     auto to = timeout == kNoTimeout ? std::chrono::milliseconds(0) : timeout;
     try {
       for (auto& r : reqs) eng_->wait(r, to);
+      std::vector<ReqPtr> dev_reqs;
       for (auto& r : reqs)
-        if (r->device) eng_->device()->stream_wait(r);
+        if (r->device) dev_reqs.push_back(r);
+      if (!dev_reqs.empty()) eng_->device()->stream_wait_all(dev_reqs);
       for (auto& d : devs) {
         std::string e = d->error();
         if (!e.empty()) throw_backend(e);
@@ -177,6 +186,8 @@ class CommuxWork : public c10d::Work {
       if (!err_) err_ = std::current_exception();
       throw;
     }
+    std::lock_guard<std::mutex> lk(mu_);
+    unpack_locked();
     return true;
   }
 
@@ -232,6 +243,11 @@ class CommuxWork : public c10d::Work {
   }
 
  private:
+  void unpack_locked() {
+    for (auto& tv : unpack_) tv.second.copy_(tv.first.view(tv.second.sizes()));
+    unpack_.clear();
+  }
+
   void record_error(const std::string& e) {
     if (!err_) err_ = std::make_exception_ptr(c10::DistBackendError(
                    c10::SourceLocation{__func__, __FILE__, static_cast<uint32_t>(__LINE__)}, e));
@@ -242,6 +258,7 @@ class CommuxWork : public c10d::Work {
   std::vector<ReqPtr> reqs_;
   std::vector<DevCollPtr> dev_;
   std::vector<at::Tensor> outs_;
+  std::vector<std::pair<at::Tensor, at::Tensor>> unpack_;
   int source_rank_;
   std::exception_ptr err_;
   c10::intrusive_ptr<c10::ivalue::Future> future_;
@@ -476,6 +493,22 @@ ProcessGroupUCX::~ProcessGroupUCX() {
 
 void ProcessGroupUCX::setTimeout(std::chrono::milliseconds timeout) { engine_->set_timeout(timeout); }
 
+bool ProcessGroupUCX::device_coll(const at::Tensor& t) {
+  return engine_->device()->device_collectives(t.device().index());
+}
+
+std::vector<at::Tensor> ProcessGroupUCX::to_host(const std::vector<at::Tensor>& ts) {
+  // Host staging for ranks that share a GPU: the device collectives would
+  // need kernels of two processes to wait on each other on one GPU.
+  std::vector<at::Tensor> h;
+  for (auto& t : ts) h.push_back(t.cpu().contiguous());
+  return h;
+}
+
+void ProcessGroupUCX::from_host(std::vector<at::Tensor>& ts, const std::vector<at::Tensor>& h) {
+  for (std::size_t i = 0; i < ts.size(); ++i) ts[i].copy_(h[i]);
+}
+
 c10::intrusive_ptr<c10d::Backend::Options> ProcessGroupUCX::getBackendOptions() {
   return c10::make_intrusive<c10d::Backend::Options>("ucx", engine_->timeout());
 }
@@ -530,11 +563,14 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::post_p2p(std::vector<at::Tensor>
     d.peer = peer;
     d.tag = tag;
     for (auto& t : tensors) {
-      if (is_send)
+      if (is_send) {
         d.keep.push_back(t.is_contiguous() || t.is_cuda() ? t : t.contiguous());
-      else {
-        TORCH_CHECK(t.is_contiguous() || t.is_cuda(), "commux recv: destination tensor must be contiguous");
+      } else if (t.is_cuda() || t.is_contiguous()) {
         d.keep.push_back(t);
+      } else {
+        at::Tensor tmp = at::empty(t.sizes(), t.options());
+        g.pending->add_unpack(tmp, t);
+        d.keep.push_back(tmp);
       }
     }
     g.deferred.push_back(std::move(d));
@@ -543,15 +579,24 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::post_p2p(std::vector<at::Tensor>
   glk.unlock();
 
   std::vector<at::Tensor> keep;
+  std::vector<std::pair<at::Tensor, at::Tensor>> unpack;
   keep.reserve(tensors.size());
   for (auto& t : tensors) {
     // CPU sends go from a contiguous copy (the reference does the same,
-    // :586-588); CUDA sends and receives may be strided views: the device
-    // transport packs and unpacks inside its copy kernel.
-    if (is_send && !t.is_cuda())
-      keep.push_back(t.contiguous());
-    else
+    // :586-588); CPU receives into strided views land in a contiguous temp.
+    // CUDA sends and receives may be strided views: the device transport
+    // gathers and scatters inside its copy kernel.
+    if (t.is_cuda()) {
       keep.push_back(t);
+    } else if (is_send) {
+      keep.push_back(t.contiguous());
+    } else if (t.is_contiguous()) {
+      keep.push_back(t);
+    } else {
+      at::Tensor tmp = at::empty(t.sizes(), t.options());
+      unpack.push_back({tmp, t});
+      keep.push_back(tmp);
+    }
   }
   std::vector<ReqPtr> reqs;
   const std::uint32_t ut = static_cast<std::uint32_t>(tag);
@@ -569,8 +614,12 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::post_p2p(std::vector<at::Tensor>
   }
   auto work = c10::make_intrusive<CommuxWork>(engine_.get(), is_send ? c10d::OpType::SEND : c10d::OpType::RECV,
                                               reqs, is_send ? std::vector<at::Tensor>{} : tensors);
+  for (auto& tv : unpack) work->add_unpack(tv.first, tv.second);
   glk.lock();
-  if (g.open && g.pending) g.pending->add(reqs, {});
+  if (g.open && g.pending) {
+    g.pending->add(reqs, {});
+    for (auto& tv : unpack) g.pending->add_unpack(tv.first, tv.second);
+  }
   return work;
 }
 
@@ -672,9 +721,16 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::allreduce(std::vector<at::Tensor
   check_same_device_kind(tensors, "allreduce");
   RedOp op = validate_op(opts.reduceOp, tensors, "allreduce");
   if (tensors[0].is_cuda()) {
+    if (getSize() == 1) return completed_work(engine_.get(), c10d::OpType::ALLREDUCE, tensors);
+    if (!device_coll(tensors[0])) {
+      std::vector<at::Tensor> h = to_host(tensors);
+      allreduce(h, opts);
+      from_host(tensors, h);
+      return completed_work(engine_.get(), c10d::OpType::ALLREDUCE, tensors);
+    }
     auto w = c10::make_intrusive<CommuxWork>(engine_.get(), c10d::OpType::ALLREDUCE,
                                              std::vector<ReqPtr>{}, tensors);
-    if (getSize() > 1 || op == RedOp::Avg) w->add_device(engine_->device()->allreduce(tensors, op));
+    w->add_device(engine_->device()->allreduce(tensors, op));
     return w;
   }
   if (getSize() > 1) {
@@ -703,9 +759,16 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::reduce(std::vector<at::Tensor>& 
   int root = static_cast<int>(opts.rootRank);
   TORCH_CHECK(root >= 0 && root < getSize(), "commux reduce: root out of range");
   if (tensors[0].is_cuda()) {
+    if (getSize() == 1) return completed_work(engine_.get(), c10d::OpType::REDUCE, tensors);
+    if (!device_coll(tensors[0])) {
+      std::vector<at::Tensor> h = to_host(tensors);
+      reduce(h, opts);
+      if (getRank() == root) from_host(tensors, h);
+      return completed_work(engine_.get(), c10d::OpType::REDUCE, tensors);
+    }
     auto w = c10::make_intrusive<CommuxWork>(engine_.get(), c10d::OpType::REDUCE,
                                              std::vector<ReqPtr>{}, tensors);
-    if (getSize() > 1 || op == RedOp::Avg) w->add_device(engine_->device()->reduce(tensors, op, root));
+    w->add_device(engine_->device()->reduce(tensors, op, root));
     return w;
   }
   if (getSize() > 1) {
@@ -725,9 +788,16 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::broadcast(std::vector<at::Tensor
   int root = static_cast<int>(opts.rootRank);
   TORCH_CHECK(root >= 0 && root < getSize(), "commux broadcast: root out of range");
   if (tensors[0].is_cuda()) {
+    if (getSize() == 1) return completed_work(engine_.get(), c10d::OpType::BROADCAST, tensors);
+    if (!device_coll(tensors[0])) {
+      std::vector<at::Tensor> h = to_host(tensors);
+      broadcast(h, opts);
+      from_host(tensors, h);
+      return completed_work(engine_.get(), c10d::OpType::BROADCAST, tensors);
+    }
     auto w = c10::make_intrusive<CommuxWork>(engine_.get(), c10d::OpType::BROADCAST,
                                              std::vector<ReqPtr>{}, tensors);
-    if (getSize() > 1) w->add_device(engine_->device()->broadcast(tensors, root));
+    w->add_device(engine_->device()->broadcast(tensors, root));
     return w;
   }
   if (getSize() > 1) {
@@ -758,6 +828,13 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::allgather(
     TORCH_CHECK(o.numel() == in.numel() && o.scalar_type() == in.scalar_type(),
                 "commux allgather: output tensors must match the input's numel and dtype");
   if (in.is_cuda()) {
+    if (getSize() > 1 && !device_coll(in)) {
+      std::vector<std::vector<at::Tensor>> ho{to_host(outs)};
+      std::vector<at::Tensor> hi = to_host(inputTensors);
+      allgather(ho, hi, c10d::AllgatherOptions());
+      from_host(outs, ho[0]);
+      return completed_work(engine_.get(), c10d::OpType::ALLGATHER, outs);
+    }
     // gather into one flat buffer on the device, then split into the list
     at::Tensor flat = at::empty({getSize() * in.numel()}, in.options());
     at::Tensor src = in.contiguous().view({-1});
@@ -795,6 +872,12 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::_allgather_base(at::Tensor& outp
   at::Tensor flat = outputBuffer.view({-1});
   at::Tensor src = inputBuffer.contiguous().view({-1});
   if (inputBuffer.is_cuda()) {
+    if (getSize() > 1 && !device_coll(inputBuffer)) {
+      at::Tensor ho = outputBuffer.cpu(), hi = inputBuffer.cpu();
+      _allgather_base(ho, hi, c10d::AllgatherOptions());
+      outputBuffer.copy_(ho);
+      return completed_work(engine_.get(), c10d::OpType::_ALLGATHER_BASE, {outputBuffer});
+    }
     auto w = c10::make_intrusive<CommuxWork>(engine_.get(), c10d::OpType::_ALLGATHER_BASE,
                                              std::vector<ReqPtr>{}, std::vector<at::Tensor>{outputBuffer});
     if (getSize() > 1)
@@ -878,6 +961,13 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::reduce_scatter(
   TORCH_CHECK(static_cast<int>(inputTensors[0].size()) == getSize(),
               "commux reduce_scatter: needs world_size inputs");
   if (out.is_cuda()) {
+    if (getSize() == 1 || !device_coll(out)) {
+      std::vector<at::Tensor> ho = to_host(outputTensors);
+      std::vector<std::vector<at::Tensor>> hi{to_host(inputTensors[0])};
+      reduce_scatter(ho, hi, opts);
+      from_host(outputTensors, ho);
+      return completed_work(engine_.get(), c10d::OpType::REDUCE_SCATTER, outputTensors);
+    }
     at::Tensor flat = at::empty({getSize() * out.numel()}, out.options());
     for (int p = 0; p < getSize(); ++p)
       flat.narrow(0, p * out.numel(), out.numel()).copy_(inputTensors[0][p].reshape({-1}));
@@ -909,6 +999,12 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::_reduce_scatter_base(at::Tensor&
   TORCH_CHECK(inputBuffer.numel() == outputBuffer.numel() * getSize(),
               "commux _reduce_scatter_base: input must hold world_size * output elements");
   RedOp op = validate_op(opts.reduceOp, {outputBuffer}, "reduce_scatter");
+  if (outputBuffer.is_cuda() && (getSize() == 1 || !device_coll(outputBuffer))) {
+    at::Tensor ho = outputBuffer.cpu(), hi = inputBuffer.cpu();
+    _reduce_scatter_base(ho, hi, opts);
+    outputBuffer.copy_(ho);
+    return completed_work(engine_.get(), c10d::OpType::_REDUCE_SCATTER_BASE, {outputBuffer});
+  }
   if (outputBuffer.is_cuda()) {
     TORCH_CHECK(outputBuffer.is_contiguous(), "commux _reduce_scatter_base: output must be contiguous");
     at::Tensor o = outputBuffer.view({-1});

@@ -1,0 +1,312 @@
+#include "coll.hpp"
+
+#include <ATen/core/ivalue.h>
+#include <c10/cuda/CUDACachingAllocator.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <unistd.h>
+
+#include <cstring>
+
+namespace commux {
+namespace cuda {
+
+namespace {
+
+cudaStream_t current_stream(int dev) {
+  return c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(dev)).stream();
+}
+
+int dtype_code(at::ScalarType t) {
+  switch (t) {
+    case at::kFloat:
+      return kF32;
+    case at::kDouble:
+      return kF64;
+    case at::kHalf:
+      return kF16;
+    case at::kBFloat16:
+      return kBF16;
+    case at::kInt:
+      return kI32;
+    case at::kLong:
+      return kI64;
+    case at::kByte:
+    case at::kBool:
+      return kU8;
+    case at::kChar:
+      return kI8;
+    default:
+      throw std::runtime_error(std::string("commux: unsupported dtype for a CUDA collective: ") +
+                               c10::toString(t));
+  }
+}
+
+int op_code(RedOp op) { return static_cast<int>(op); }
+
+struct ExchangeRecord {
+  std::int32_t pid;
+  unsigned char uuid[16];
+  cudaIpcMemHandle_t handle;
+};
+
+class CollResult final : public DevCollResult {
+ public:
+  CollResult(CudaTransport* tr, int dev, cudaStream_t s, EventPtr done)
+      : tr_(tr), dev_(dev), stream_(s), done_(std::move(done)) {}
+  void stream_wait() override {
+    c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev_));
+    CMX_CUDA(cudaStreamWaitEvent(current_stream(dev_), done_->ev, 0));
+  }
+  bool query() override { return cudaEventQuery(done_->ev) == cudaSuccess; }
+  void host_wait() override { CMX_CUDA(cudaEventSynchronize(done_->ev)); }
+  std::string error() override { return tr_->device_error(); }
+  void mark_future(void* fut, void* value) override {
+    c10::cuda::CUDAStreamGuard g(
+        c10::cuda::getStreamFromExternal(stream_, static_cast<c10::DeviceIndex>(dev_)));
+    static_cast<c10::ivalue::Future*>(fut)->markCompleted(*static_cast<c10::IValue*>(value));
+  }
+
+ private:
+  CudaTransport* tr_;
+  int dev_;
+  cudaStream_t stream_;
+  EventPtr done_;
+};
+
+}  // namespace
+
+CollImpl::CollImpl(CudaTransport* tr, int dev)
+    : tr_(tr), eng_(tr->engine()), ctx_(tr->ctx(dev)), dev_(dev), P_(tr->engine()->size()),
+      me_(tr->engine()->rank()) {
+  TORCH_CHECK(P_ <= kMaxCollRanks, "commux: CUDA collectives support up to ", kMaxCollRanks,
+              " ranks per group (one NVLink domain)");
+  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev));
+  region_bytes_ = env_int("COMMUX_CUDA_WS_BYTES", 64ll << 20);
+  region_bytes_ = std::max<std::int64_t>(region_bytes_ & ~std::int64_t(4095), 1 << 20);
+  oneshot_bytes_ = env_int("COMMUX_ONESHOT_BYTES", 256 << 10);
+  int lo = 0, hi = 0;
+  CMX_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+  CMX_CUDA(cudaStreamCreateWithPriority(&stream_, cudaStreamNonBlocking, hi));
+  const std::size_t total = kFlagBytes + 2 * static_cast<std::size_t>(region_bytes_);
+  CMX_CUDA(cudaMalloc(reinterpret_cast<void**>(&ws_), total));
+  CMX_CUDA(cudaMemsetAsync(ws_, 0, kFlagBytes, stream_));
+  CMX_CUDA(cudaStreamSynchronize(stream_));
+
+  // exchange workspace handles (collective: every rank creates its workspace
+  // at its first CUDA collective, in the same order)
+  ExchangeRecord mine;
+  std::memset(&mine, 0, sizeof(mine));
+  mine.pid = static_cast<std::int32_t>(::getpid());
+  std::memcpy(mine.uuid, ctx_->uuid, 16);
+  CMX_CUDA(cudaIpcGetMemHandle(&mine.handle, ws_));
+  const std::string key = eng_->store_prefix() + "cws/";
+  std::vector<std::uint8_t> blob(reinterpret_cast<std::uint8_t*>(&mine),
+                                 reinterpret_cast<std::uint8_t*>(&mine) + sizeof(mine));
+  eng_->store().set(key + std::to_string(me_), blob);
+  data_.assign(P_, nullptr);
+  flags_.assign(P_, nullptr);
+  std::vector<ExchangeRecord> recs(P_);
+  for (int p = 0; p < P_; ++p) {
+    if (p == me_) {
+      recs[p] = mine;
+      continue;
+    }
+    eng_->store().wait({key + std::to_string(p)}, eng_->timeout());
+    auto v = eng_->store().get(key + std::to_string(p));
+    TORCH_CHECK(v.size() == sizeof(ExchangeRecord), "commux: malformed workspace record");
+    std::memcpy(&recs[p], v.data(), sizeof(ExchangeRecord));
+    if (std::memcmp(recs[p].uuid, ctx_->uuid, 16) == 0) shared_gpu_ = true;
+  }
+  if (shared_gpu_) return;  // kernels of two processes on one GPU must not wait on each other
+  for (int p = 0; p < P_; ++p) {
+    char* base = ws_;
+    if (p != me_) {
+      void* q = nullptr;
+      CMX_CUDA(cudaIpcOpenMemHandle(&q, recs[p].handle, cudaIpcMemLazyEnablePeerAccess));
+      base = static_cast<char*>(q);
+    }
+    flags_[p] = reinterpret_cast<std::uint64_t*>(base);
+    data_[p] = base + kFlagBytes;
+  }
+}
+
+CollImpl::~CollImpl() {
+  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev_));
+  if (stream_) cudaStreamSynchronize(stream_);
+  for (int p = 0; p < P_; ++p)
+    if (p != me_ && flags_[p]) cudaIpcCloseMemHandle(flags_[p]);
+  if (ws_) cudaFree(ws_);
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+int CollImpl::choose_ctas(int mode, int algo, std::int64_t bytes) const {
+  static const std::int64_t forced = env_int("COMMUX_COLL_CTAS", 0);
+  if (forced > 0) return static_cast<int>(std::min<std::int64_t>(forced, kMaxCollCtas));
+  const int cap = std::min(ctx_->sm_count, kMaxCollCtas);
+  if (mode == kModeAllreduce || mode == kModeReduce || mode == kModeReduceScatter) {
+    if (algo == kAlgoOneShot)
+      return static_cast<int>(std::max<std::int64_t>(1, std::min<std::int64_t>(cap / 2, bytes / (16 << 10))));
+    return cap;
+  }
+  return static_cast<int>(std::max<std::int64_t>(1, std::min<std::int64_t>(cap, bytes / (16 << 10))));
+}
+
+void CollImpl::fill(CollArgs& a, const Launch& l, const at::Tensor& in, const at::Tensor& out) {
+  std::memset(&a, 0, sizeof(a));
+  a.P = P_;
+  a.me = me_;
+  a.root = l.root;
+  a.mode = l.mode;
+  a.op = l.op;
+  a.dtype = dtype_code(in.scalar_type());
+  a.elem_bytes = static_cast<int>(in.element_size());
+  a.n = l.n;
+  a.in = in.data_ptr();
+  a.out = out.data_ptr();
+  for (int p = 0; p < P_; ++p) {
+    a.data[p] = data_[p];
+    a.flags[p] = flags_[p];
+  }
+  a.region_bytes = region_bytes_;
+  ++epoch_;
+  a.half_off = (epoch_ & 1) ? region_bytes_ / 2 : 0;
+  a.seq_base = epoch_ << 20;
+  a.timeout_ns = tr_->device_timeout_ns();
+  a.status = ctx_->status_d;
+}
+
+DevCollPtr CollImpl::run(const std::vector<Launch>& launches) {
+  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev_));
+  cudaStream_t cur = current_stream(dev_);
+  auto c10s = c10::cuda::getStreamFromExternal(stream_, static_cast<c10::DeviceIndex>(dev_));
+  // contiguous, 16B-aligned inputs and outputs (copies made on the caller's
+  // stream so they are ordered before the collective)
+  std::vector<at::Tensor> ins, outs;
+  for (auto& l : launches) {
+    at::Tensor i = *l.in, o = *l.out;
+    auto good = [](const at::Tensor& t) {
+      return t.is_contiguous() && (reinterpret_cast<std::uintptr_t>(t.data_ptr()) & 15u) == 0;
+    };
+    if (!good(i)) i = i.contiguous().clone();
+    if (l.in == l.out)
+      o = i;
+    else if (!good(o))
+      o = at::empty(o.sizes(), o.options());
+    ins.push_back(i);
+    outs.push_back(o);
+  }
+  auto ready = ctx_->event();
+  CMX_CUDA(cudaEventRecord(ready->ev, cur));
+  CMX_CUDA(cudaStreamWaitEvent(stream_, ready->ev, 0));
+  for (std::size_t k = 0; k < launches.size(); ++k) {
+    const Launch& l = launches[k];
+    CollArgs a;
+    fill(a, l, ins[k], outs[k]);
+    std::int64_t bytes = l.n * a.elem_bytes;
+    int algo = kAlgoTwoShot;
+    if ((l.mode == kModeAllreduce || l.mode == kModeReduce) && bytes <= oneshot_bytes_ &&
+        l.n * a.elem_bytes * P_ <= region_bytes_ / 2)
+      algo = kAlgoOneShot;
+    a.algo = algo;
+    int ctas = choose_ctas(l.mode, algo, bytes);
+    CMX_CUDA(launch_coll(a, ctas, stream_));
+    tr_->kernel_launches++;
+    st_calls_++;
+    st_bytes_ += bytes;
+    if (l.mode == kModeAllgather || l.mode == kModeBroadcast)
+      st_gather_++;
+    else if (algo == kAlgoOneShot)
+      st_oneshot_++;
+    else
+      st_twoshot_++;
+  }
+  // copy back results that went through a temporary
+  {
+    c10::cuda::CUDAStreamGuard sg(c10s);
+    for (std::size_t k = 0; k < launches.size(); ++k) {
+      at::Tensor& user_out = *launches[k].out;
+      if (!outs[k].is_same(user_out) && outs[k].data_ptr() != user_out.data_ptr())
+        user_out.copy_(outs[k].view(user_out.sizes()));
+    }
+  }
+  for (std::size_t k = 0; k < launches.size(); ++k) {
+    c10::cuda::CUDACachingAllocator::recordStream(ins[k].storage().data_ptr(), c10s);
+    c10::cuda::CUDACachingAllocator::recordStream(outs[k].storage().data_ptr(), c10s);
+    c10::cuda::CUDACachingAllocator::recordStream(launches[k].out->storage().data_ptr(), c10s);
+  }
+  auto done = ctx_->event();
+  CMX_CUDA(cudaEventRecord(done->ev, stream_));
+  return std::make_shared<CollResult>(tr_, dev_, stream_, done);
+}
+
+DevCollPtr CollImpl::allreduce(std::vector<at::Tensor>& ts, RedOp op) {
+  std::vector<Launch> ls;
+  for (auto& t : ts) ls.push_back({kModeAllreduce, op_code(op), 0, &t, &t, t.numel()});
+  return run(ls);
+}
+
+DevCollPtr CollImpl::reduce(std::vector<at::Tensor>& ts, RedOp op, int root) {
+  std::vector<Launch> ls;
+  for (auto& t : ts) ls.push_back({kModeReduce, op_code(op), root, &t, &t, t.numel()});
+  return run(ls);
+}
+
+DevCollPtr CollImpl::broadcast(std::vector<at::Tensor>& ts, int root) {
+  std::vector<Launch> ls;
+  for (auto& t : ts) ls.push_back({kModeBroadcast, 0, root, &t, &t, t.numel()});
+  return run(ls);
+}
+
+DevCollPtr CollImpl::allgather(at::Tensor& out, const at::Tensor& in) {
+  std::vector<Launch> ls{{kModeAllgather, 0, 0, &in, &out, in.numel()}};
+  return run(ls);
+}
+
+DevCollPtr CollImpl::reduce_scatter(at::Tensor& out, const at::Tensor& in, RedOp op) {
+  std::vector<Launch> ls{{kModeReduceScatter, op_code(op), 0, &in, &out, out.numel()}};
+  return run(ls);
+}
+
+std::vector<std::pair<std::string, std::int64_t>> CollImpl::stats() const {
+  return {{"coll_calls", st_calls_},   {"coll_oneshot", st_oneshot_}, {"coll_twoshot", st_twoshot_},
+          {"coll_gather", st_gather_}, {"coll_bytes", st_bytes_},     {"coll_shared_gpu", shared_gpu_ ? 1 : 0}};
+}
+
+// ---------------------------------------------------------------------------
+// transport entry points
+// ---------------------------------------------------------------------------
+
+bool CudaTransport::device_collectives(int dev) {
+  if (!coll_) coll_ = std::make_unique<CollImpl>(this, dev);
+  TORCH_CHECK(coll_->device() == dev, "commux: CUDA collectives of one group must use one device "
+              "per rank (got device ", dev, " after ", coll_->device(), ")");
+  return !coll_->shared_gpu();
+}
+
+DevCollPtr CudaTransport::allreduce(std::vector<at::Tensor>& ts, RedOp op) {
+  device_collectives(ts[0].device().index());
+  return coll_->allreduce(ts, op);
+}
+DevCollPtr CudaTransport::reduce(std::vector<at::Tensor>& ts, RedOp op, int root) {
+  device_collectives(ts[0].device().index());
+  return coll_->reduce(ts, op, root);
+}
+DevCollPtr CudaTransport::broadcast(std::vector<at::Tensor>& ts, int root) {
+  device_collectives(ts[0].device().index());
+  return coll_->broadcast(ts, root);
+}
+DevCollPtr CudaTransport::allgather(at::Tensor& out, const at::Tensor& in) {
+  device_collectives(in.device().index());
+  return coll_->allgather(out, in);
+}
+DevCollPtr CudaTransport::reduce_scatter(at::Tensor& out, const at::Tensor& in, RedOp op) {
+  device_collectives(in.device().index());
+  return coll_->reduce_scatter(out, in, op);
+}
+DevCollPtr CudaTransport::barrier() {
+  throw std::runtime_error("commux: the device barrier is not used (barrier runs on the host)");
+}
+
+}  // namespace cuda
+}  // namespace commux

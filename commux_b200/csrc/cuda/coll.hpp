@@ -1,0 +1,64 @@
+#pragma once
+
+// Host side of the device collectives: symmetric workspace bootstrap over the
+// c10d Store, algorithm choice per message size, stream ordering, results.
+
+#include <ATen/ATen.h>
+
+#include <memory>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "coll_args.hpp"
+#include "transport.hpp"
+
+namespace commux {
+namespace cuda {
+
+class CollImpl {
+ public:
+  CollImpl(CudaTransport* tr, int dev);
+  ~CollImpl();
+
+  bool shared_gpu() const { return shared_gpu_; }
+  DevCollPtr allreduce(std::vector<at::Tensor>& ts, RedOp op);
+  DevCollPtr reduce(std::vector<at::Tensor>& ts, RedOp op, int root);
+  DevCollPtr broadcast(std::vector<at::Tensor>& ts, int root);
+  DevCollPtr allgather(at::Tensor& out, const at::Tensor& in);
+  DevCollPtr reduce_scatter(at::Tensor& out, const at::Tensor& in, RedOp op);
+  std::vector<std::pair<std::string, std::int64_t>> stats() const;
+  int device() const { return dev_; }
+
+ private:
+  struct Launch {
+    int mode;
+    int op;
+    int root;
+    const at::Tensor* in;
+    at::Tensor* out;
+    std::int64_t n;
+  };
+  DevCollPtr run(const std::vector<Launch>& launches);
+  void fill(CollArgs& a, const Launch& l, const at::Tensor& in, const at::Tensor& out);
+  int choose_ctas(int mode, int algo, std::int64_t bytes) const;
+
+  CudaTransport* tr_;
+  Engine* eng_;
+  DevCtx* ctx_;
+  int dev_;
+  int P_;
+  int me_;
+  bool shared_gpu_ = false;
+  cudaStream_t stream_ = nullptr;  // collectives run here, ordered per group
+  char* ws_ = nullptr;
+  std::int64_t region_bytes_ = 0;
+  std::int64_t oneshot_bytes_ = 0;
+  std::vector<char*> data_;
+  std::vector<std::uint64_t*> flags_;
+  std::uint64_t epoch_ = 0;
+  std::int64_t st_calls_ = 0, st_oneshot_ = 0, st_twoshot_ = 0, st_gather_ = 0, st_bytes_ = 0;
+};
+
+}  // namespace cuda
+}  // namespace commux

@@ -1,0 +1,430 @@
+// Device collectives on sm_100a over symmetric CUDA-IPC workspaces.
+//
+// Every rank owns one workspace (flags + regions A and B) mapped into every
+// peer. All data crosses NVLink as plain 16-byte stores into a peer's
+// workspace (posted writes: a CTA never stalls on a remote round trip); every
+// reduction then reads local HBM. Synchronisation is per CTA: CTA b of each
+// rank exchanges flags only with CTA b of the others, so there is no grid-wide
+// barrier and ranks pipeline freely. Flags are monotonically increasing
+// sequence numbers (epoch << 20 | chunk), stored with release and polled with
+// acquire at system scope; every wait gives up after a timeout, records the
+// failure in a host-mapped status word and returns (no trap, no endless spin).
+//
+// Reuse rules: a call with epoch e only touches half (e & 1) of A and B, and
+// every call contains an all-to-all flag round, so a peer has finished call
+// e-2 before call e writes into the same half (see coll_args.hpp). Inside a
+// call, each chunk has two flag rounds, so chunk c+1 never overwrites what a
+// peer still reads from chunk c.
+//
+// The reduction folds ranks in rank order 0..P-1 with fp32 accumulation for
+// bf16/fp16, so all ranks hold bit-identical results that the CPU fold of the
+// host backend reproduces exactly. (The reference reduces with ATen ops along
+// a binomial tree of whole-tensor messages, reference:
+// src/process_group_ucx.cpp:214-232, :734-792.)
+//
+// Kernels:
+//   oneshot  (small allreduce/reduce): push my data into slot[me] of every
+//            rank's A, one flag round, fold the P slots locally.
+//   twoshot  (large allreduce/reduce/reduce_scatter), chunked: push segment s
+//            of the chunk into slot[me] of rank s's A (reduce-scatter by
+//            writes), flag round, rank s folds its segment and pushes it into
+//            slot[s] of B on every rank that needs it, flag round, copy out.
+//   gather   (allgather/broadcast), chunked: push my block into slot[me] of
+//            every rank's B (broadcast: the root's block into slot 0), flag
+//            round, copy out, flag round.
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "coll_args.hpp"
+#include "cuda_common.hpp"
+#include "device_utils.cuh"
+
+namespace commux {
+namespace cuda {
+
+namespace {
+
+constexpr int kCollThreads = 512;
+
+template <typename T>
+struct AccT {
+  using type = T;
+};
+template <>
+struct AccT<__half> {
+  using type = float;
+};
+template <>
+struct AccT<__nv_bfloat16> {
+  using type = float;
+};
+
+template <typename A, typename T>
+__device__ __forceinline__ A to_acc(T v) {
+  return static_cast<A>(v);
+}
+template <>
+__device__ __forceinline__ float to_acc<float, __half>(__half v) {
+  return __half2float(v);
+}
+template <>
+__device__ __forceinline__ float to_acc<float, __nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <typename T, typename A>
+__device__ __forceinline__ T from_acc(A v) {
+  return static_cast<T>(v);
+}
+template <>
+__device__ __forceinline__ __half from_acc<__half, float>(float v) {
+  return __float2half_rn(v);
+}
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_acc<__nv_bfloat16, float>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+template <int OP, typename A>
+__device__ __forceinline__ A combine(A a, A b) {
+  if constexpr (OP == kOpSum || OP == kOpAvg) {
+    return a + b;
+  } else if constexpr (OP == kOpProd) {
+    return a * b;
+  } else if constexpr (OP == kOpMin) {
+    return b < a ? b : a;
+  } else {
+    return b > a ? b : a;
+  }
+}
+
+// ---- flag rounds -------------------------------------------------------------
+
+__device__ __forceinline__ std::uint64_t* flag_at(std::uint64_t* base, int phase, int src, int b) {
+  return base + (static_cast<std::size_t>(phase) * kMaxCollRanks + src) * kMaxCollCtas + b;
+}
+
+// After all threads' stores, thread p stores the flag into rank p's area
+// (every rank when `only` < 0, else only rank `only`).
+__device__ __forceinline__ void signal(const CollArgs& a, int phase, std::uint64_t seq, int only = -1) {
+  __syncthreads();
+  const int p = threadIdx.x;
+  if (p < a.P && (only < 0 || p == only)) {
+    fence_acq_rel_sys();
+    st_release_sys(flag_at(a.flags[p], phase, a.me, blockIdx.x), seq);
+  }
+}
+
+// Thread p waits for rank p's flag (every rank when `only` < 0). Returns false
+// after recording a status if a wait timed out.
+__device__ __forceinline__ bool await(const CollArgs& a, int phase, std::uint64_t seq, int only = -1) {
+  __shared__ int timed_out;
+  if (threadIdx.x == 0) timed_out = 0;
+  __syncthreads();
+  const int p = threadIdx.x;
+  if (p < a.P && (only < 0 || p == only)) {
+    const std::uint64_t* f = flag_at(a.flags[a.me], phase, p, blockIdx.x);
+    const std::uint64_t t0 = globaltimer_ns();
+    std::uint32_t spins = 0;
+    while (ld_acquire_sys(f) < seq) {
+      if ((++spins & 31u) == 0u && globaltimer_ns() - t0 > a.timeout_ns) {
+        report_status(a.status, kStatusCollTimeout, static_cast<unsigned long long>(p), seq >> 20,
+                      ld_acquire_sys(f));
+        atomicExch(&timed_out, 1);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  return timed_out == 0;
+}
+
+// ---- packed copies and folds -----------------------------------------------
+
+template <typename T>
+struct Packs {
+  static constexpr int N = 16 / sizeof(T);
+};
+
+__device__ __forceinline__ bool aligned16(const void* p) {
+  return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0;
+}
+
+// dst[i] = src[i], i in [lo, hi); lo is a multiple of the pack size.
+template <typename T>
+__device__ __forceinline__ void copy_range(T* dst, const T* src, std::int64_t lo, std::int64_t hi) {
+  constexpr int N = Packs<T>::N;
+  if (lo >= hi) return;
+  std::int64_t full_hi = (aligned16(dst + lo) && aligned16(src + lo)) ? lo + ((hi - lo) / N) * N : lo;
+  for (std::int64_t i = lo + static_cast<std::int64_t>(threadIdx.x) * N; i < full_hi;
+       i += static_cast<std::int64_t>(blockDim.x) * N)
+    *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<const uint4*>(src + i);
+  for (std::int64_t i = full_hi + threadIdx.x; i < hi; i += blockDim.x) dst[i] = src[i];
+}
+
+// out[i] = fold over p of base[p*stride + i], i in [lo, hi).
+template <typename T, int OP>
+__device__ __forceinline__ void fold_range(T* out, const T* base, std::int64_t stride, int P,
+                                           std::int64_t lo, std::int64_t hi) {
+  using A = typename AccT<T>::type;
+  constexpr int N = Packs<T>::N;
+  if (lo >= hi) return;
+  const bool vec = aligned16(out + lo) && aligned16(base + lo) && (stride % N) == 0;
+  std::int64_t full_hi = vec ? lo + ((hi - lo) / N) * N : lo;
+  for (std::int64_t i = lo + static_cast<std::int64_t>(threadIdx.x) * N; i < full_hi;
+       i += static_cast<std::int64_t>(blockDim.x) * N) {
+    A acc[N];
+    {
+      uint4 raw = *reinterpret_cast<const uint4*>(base + i);
+      const T* v = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int k = 0; k < N; ++k) acc[k] = to_acc<A>(v[k]);
+    }
+    for (int p = 1; p < P; ++p) {
+      uint4 raw = *reinterpret_cast<const uint4*>(base + p * stride + i);
+      const T* v = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int k = 0; k < N; ++k) acc[k] = combine<OP>(acc[k], to_acc<A>(v[k]));
+    }
+    uint4 outraw;
+    T* o = reinterpret_cast<T*>(&outraw);
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+      A r = acc[k];
+      if constexpr (OP == kOpAvg) r = r / static_cast<A>(P);
+      o[k] = from_acc<T>(r);
+    }
+    *reinterpret_cast<uint4*>(out + i) = outraw;
+  }
+  for (std::int64_t i = full_hi + threadIdx.x; i < hi; i += blockDim.x) {
+    A acc = to_acc<A>(base[i]);
+    for (int p = 1; p < P; ++p) acc = combine<OP>(acc, to_acc<A>(base[p * stride + i]));
+    if constexpr (OP == kOpAvg) acc = acc / static_cast<A>(P);
+    out[i] = from_acc<T>(acc);
+  }
+}
+
+// Piece k of `parts` of [0, n), cut on pack boundaries.
+template <typename T>
+__device__ __forceinline__ void piece(std::int64_t n, int parts, int k, std::int64_t& lo,
+                                      std::int64_t& hi) {
+  constexpr int N = Packs<T>::N;
+  std::int64_t packs = (n + N - 1) / N;
+  std::int64_t per = (packs + parts - 1) / parts;
+  lo = min(n, static_cast<std::int64_t>(k) * per * N);
+  hi = min(n, lo + per * N);
+}
+
+template <typename T>
+__device__ __forceinline__ T* region_a(const CollArgs& a, int p) {
+  return reinterpret_cast<T*>(a.data[p] + a.half_off);
+}
+template <typename T>
+__device__ __forceinline__ T* region_b(const CollArgs& a, int p) {
+  return reinterpret_cast<T*>(a.data[p] + a.region_bytes + a.half_off);
+}
+template <typename T>
+__device__ __forceinline__ std::int64_t slot_elems(const CollArgs& a, int nslots) {
+  constexpr int N = Packs<T>::N;
+  std::int64_t e = (a.region_bytes / 2) / static_cast<std::int64_t>(sizeof(T)) / nslots;
+  return (e / N) * N;
+}
+
+// ---- oneshot -------------------------------------------------------------------
+
+template <typename T, int OP>
+__global__ void __launch_bounds__(kCollThreads) oneshot_kernel(const __grid_constant__ CollArgs a) {
+  const T* in = static_cast<const T*>(a.in);
+  T* out = static_cast<T*>(a.out);
+  std::int64_t lo, hi;
+  piece<T>(a.n, gridDim.x, blockIdx.x, lo, hi);
+  const std::int64_t slot = slot_elems<T>(a, a.P);
+  for (int q = 0; q < a.P; ++q) {
+    const int p = (a.me + q) % a.P;  // stagger destinations across ranks
+    copy_range(region_a<T>(a, p) + a.me * slot, in, lo, hi);
+  }
+  const std::uint64_t seq = a.seq_base + 1;
+  signal(a, 0, seq);
+  if (!await(a, 0, seq)) return;
+  if (a.mode == kModeReduce && a.me != a.root) return;
+  fold_range<T, OP>(out, region_a<T>(a, a.me), slot, a.P, lo, hi);
+}
+
+// ---- twoshot -------------------------------------------------------------------
+
+template <typename T, int OP>
+__global__ void __launch_bounds__(kCollThreads) twoshot_kernel(const __grid_constant__ CollArgs a) {
+  constexpr int N = Packs<T>::N;
+  const T* in = static_cast<const T*>(a.in);
+  T* out = static_cast<T*>(a.out);
+  const int P = a.P;
+  const bool rs = a.mode == kModeReduceScatter;
+  const std::int64_t seg_cap = slot_elems<T>(a, P);
+  const std::int64_t total = rs ? a.n * P : a.n;
+  // segment s of the tensor: [s*seg, s*seg + seg) (reduce_scatter: block s)
+  const std::int64_t seg = rs ? a.n : (((total + P - 1) / P + N - 1) / N) * N;
+  const std::int64_t nchunks = (seg + seg_cap - 1) / seg_cap;
+  T* a_me = region_a<T>(a, a.me);
+  T* b_me = region_b<T>(a, a.me);
+  for (std::int64_t c = 0; c < nchunks; ++c) {
+    const std::int64_t s0 = c * seg_cap;
+    const std::int64_t slen = min(seg_cap, seg - s0);
+    std::int64_t lo, hi;
+    piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
+    const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
+    // phase 0: my part of segment s -> slot[me] of rank s's A
+    for (int q = 0; q < P; ++q) {
+      const int s = (a.me + q) % P;
+      const std::int64_t g = static_cast<std::int64_t>(s) * seg + s0;
+      const std::int64_t ghi = rs ? g + hi : min(g + hi, total);
+      copy_range(region_a<T>(a, s) + a.me * seg_cap - g, in, g + lo, ghi);
+    }
+    signal(a, 0, seq);
+    if (!await(a, 0, seq)) return;
+    // fold my segment
+    const std::int64_t mine = static_cast<std::int64_t>(a.me) * seg + s0;
+    const std::int64_t mhi = rs ? hi : min(hi, total - mine);
+    if (rs) {
+      fold_range<T, OP>(out + s0, a_me, seg_cap, P, lo, mhi);
+    } else {
+      fold_range<T, OP>(b_me + a.me * seg_cap, a_me, seg_cap, P, lo, mhi);
+      __syncthreads();
+      // phase 1: my folded segment -> slot[me] of B on every rank that needs it
+      for (int q = 1; q < P; ++q) {
+        const int p = (a.me + q) % P;
+        if (a.mode == kModeReduce && p != a.root) continue;
+        copy_range(region_b<T>(a, p) + a.me * seg_cap, b_me + a.me * seg_cap, lo, mhi);
+      }
+    }
+    signal(a, 1, seq);
+    if (!await(a, 1, seq)) return;
+    if (rs || (a.mode == kModeReduce && a.me != a.root)) continue;
+    for (int p = 0; p < P; ++p) {
+      const std::int64_t g = static_cast<std::int64_t>(p) * seg + s0;
+      const std::int64_t phi = min(hi, total - g);
+      copy_range(out + g, b_me + p * seg_cap - 0, lo, phi);
+    }
+  }
+}
+
+// ---- gather (allgather / broadcast) ------------------------------------------
+
+template <typename T>
+__global__ void __launch_bounds__(kCollThreads) gather_kernel(const __grid_constant__ CollArgs a) {
+  const T* in = static_cast<const T*>(a.in);
+  T* out = static_cast<T*>(a.out);
+  const int P = a.P;
+  const bool bcast = a.mode == kModeBroadcast;
+  const std::int64_t slot = slot_elems<T>(a, bcast ? 1 : P);
+  const std::int64_t nchunks = (a.n + slot - 1) / slot;
+  T* b_me = region_b<T>(a, a.me);
+  for (std::int64_t c = 0; c < nchunks; ++c) {
+    const std::int64_t c0 = c * slot;
+    const std::int64_t clen = min(slot, a.n - c0);
+    std::int64_t lo, hi;
+    piece<T>(clen, gridDim.x, blockIdx.x, lo, hi);
+    const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
+    if (bcast) {
+      if (a.me == a.root) {
+        for (int q = 1; q < P; ++q) {
+          const int p = (a.me + q) % P;
+          copy_range(region_b<T>(a, p) - c0, in, c0 + lo, c0 + hi);
+        }
+        if (out != in) copy_range(out, in, c0 + lo, c0 + hi);
+        signal(a, 0, seq);
+      } else {
+        if (!await(a, 0, seq, a.root)) return;
+        copy_range(out, b_me - c0, c0 + lo, c0 + hi);
+      }
+    } else {
+      for (int q = 1; q < P; ++q) {
+        const int p = (a.me + q) % P;
+        copy_range(region_b<T>(a, p) + a.me * slot - c0, in, c0 + lo, c0 + hi);
+      }
+      copy_range(out + static_cast<std::int64_t>(a.me) * a.n, in, c0 + lo, c0 + hi);
+      signal(a, 0, seq);
+      if (!await(a, 0, seq)) return;
+      for (int q = 1; q < P; ++q) {
+        const int p = (a.me + q) % P;
+        copy_range(out + static_cast<std::int64_t>(p) * a.n, b_me + p * slot - c0, c0 + lo, c0 + hi);
+      }
+    }
+    // everyone has consumed this chunk before anyone refills the slots
+    signal(a, 1, seq);
+    if (!await(a, 1, seq)) return;
+  }
+}
+
+template <typename T, int OP>
+cudaError_t launch_reduce_family(const CollArgs& a, int ctas, cudaStream_t s) {
+  if (a.algo == kAlgoOneShot)
+    oneshot_kernel<T, OP><<<ctas, kCollThreads, 0, s>>>(a);
+  else
+    twoshot_kernel<T, OP><<<ctas, kCollThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t dispatch_op(const CollArgs& a, int ctas, cudaStream_t s) {
+  switch (a.op) {
+    case kOpSum:
+      return launch_reduce_family<T, kOpSum>(a, ctas, s);
+    case kOpProd:
+      return launch_reduce_family<T, kOpProd>(a, ctas, s);
+    case kOpMin:
+      return launch_reduce_family<T, kOpMin>(a, ctas, s);
+    case kOpMax:
+      return launch_reduce_family<T, kOpMax>(a, ctas, s);
+    case kOpAvg:
+      return launch_reduce_family<T, kOpAvg>(a, ctas, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+cudaError_t launch_coll(const CollArgs& a, int ctas, cudaStream_t s) {
+  if (ctas < 1 || ctas > kMaxCollCtas || a.P > kMaxCollRanks) return cudaErrorInvalidValue;
+  if (a.mode == kModeAllgather || a.mode == kModeBroadcast) {
+    switch (a.elem_bytes) {
+      case 1:
+        gather_kernel<std::uint8_t><<<ctas, kCollThreads, 0, s>>>(a);
+        break;
+      case 2:
+        gather_kernel<std::uint16_t><<<ctas, kCollThreads, 0, s>>>(a);
+        break;
+      case 4:
+        gather_kernel<std::uint32_t><<<ctas, kCollThreads, 0, s>>>(a);
+        break;
+      case 8:
+        gather_kernel<std::uint64_t><<<ctas, kCollThreads, 0, s>>>(a);
+        break;
+      default:
+        return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+  }
+  switch (a.dtype) {
+    case kF32:
+      return dispatch_op<float>(a, ctas, s);
+    case kF64:
+      return dispatch_op<double>(a, ctas, s);
+    case kF16:
+      return dispatch_op<__half>(a, ctas, s);
+    case kBF16:
+      return dispatch_op<__nv_bfloat16>(a, ctas, s);
+    case kI32:
+      return dispatch_op<std::int32_t>(a, ctas, s);
+    case kI64:
+      return dispatch_op<std::int64_t>(a, ctas, s);
+    case kU8:
+      return dispatch_op<std::uint8_t>(a, ctas, s);
+    case kI8:
+      return dispatch_op<std::int8_t>(a, ctas, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace cuda
+}  // namespace commux

@@ -1,0 +1,93 @@
+#pragma once
+
+// Structures shared by the host side of the CUDA transport and its sm_100a
+// kernels.
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace commux {
+namespace cuda {
+
+constexpr int kMaxPullDims = 4;      // dims of a pull descriptor after merging
+constexpr int kMaxBatch = 128;       // descriptors per pull launch (by value)
+constexpr int kMaxWaitFlags = 32;    // flags per wait launch (one warp)
+constexpr std::uint32_t kCounterSlots = 1024;  // per-stream message counters
+constexpr std::uint32_t kChunkUnits = 4096;  // units per CTA work item
+
+// 32-bit division by an invariant divisor through a multiply-high and a shift
+// (Granlund & Montgomery, "Division by invariant integers using
+// multiplication", PLDI 1994, round-up variant). Valid for n < 2^31.
+struct FastDiv {
+  std::uint32_t d = 1, mul = 0, shr = 0;
+  FastDiv() = default;
+  explicit FastDiv(std::uint32_t div) : d(div) {
+    if (div <= 1) {
+      mul = 0;
+      shr = 0;
+      return;
+    }
+    std::uint32_t l = 0;
+    while ((1ull << l) < div) ++l;  // l = ceil(log2 div)
+    std::uint64_t p = 31 + l;
+    mul = static_cast<std::uint32_t>(((1ull << p) + div - 1) / div);
+    shr = static_cast<std::uint32_t>(p - 32);
+  }
+#if defined(__CUDACC__)
+  __device__ __forceinline__ std::uint32_t div(std::uint32_t n) const {
+    return d == 1 ? n : (__umulhi(n, mul) >> shr);
+  }
+#endif
+};
+
+// One strided copy: units of `unit` bytes, dims outermost first.
+struct PullDesc {
+  const char* src;
+  char* dst;
+  std::int64_t sst[kMaxPullDims];   // src stride per dim, bytes
+  std::int64_t dstr[kMaxPullDims];  // dst stride per dim, bytes
+  FastDiv div[kMaxPullDims];        // divisors = sizes per dim
+  std::uint32_t ndim;
+  std::uint32_t unit;               // 16, 8, 4, 2 or 1 bytes
+  std::uint32_t units;              // total units (< 2^31)
+  std::uint32_t chunk0;             // first chunk index of this descriptor
+  std::uint32_t nchunks;            // chunks of this descriptor
+  std::uint32_t msg_chunks;         // chunks of its whole message
+  std::uint32_t counter_idx;        // per-message completion counter (scratch)
+  std::uint64_t* done;              // flag to set once copied (may be remote)
+  std::uint64_t done_val;
+};
+
+struct PullBatch {
+  std::uint32_t n;
+  std::uint32_t total_chunks;
+  std::uint32_t* counters;          // per-stream scratch, zero between launches
+  unsigned long long* status;       // host-mapped status word (4 x u64)
+  PullDesc d[kMaxBatch];
+};
+
+// Flags a wait kernel polls (all in this GPU's own memory, written remotely).
+struct WaitBatch {
+  std::uint32_t n;
+  std::uint64_t timeout_ns;
+  unsigned long long* status;
+  const std::uint64_t* flag[kMaxWaitFlags];
+  std::uint64_t val[kMaxWaitFlags];
+};
+
+// Device error codes written to the status word.
+enum : unsigned long long {
+  kStatusOk = 0,
+  kStatusWaitTimeout = 1,     // a flag wait gave up
+  kStatusBadDescriptor = 2,   // bounds check failed (COMMUX_DEVICE_CHECKS)
+  kStatusCollTimeout = 3,     // collective barrier gave up
+};
+
+// Launchers (p2p_kernels.cu).
+cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStream_t s);
+cudaError_t launch_wait(const WaitBatch& b, cudaStream_t s);
+cudaError_t launch_signal(std::uint64_t* flag, std::uint64_t val, cudaStream_t s);
+
+}  // namespace cuda
+}  // namespace commux

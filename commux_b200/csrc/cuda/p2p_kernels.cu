@@ -1,0 +1,160 @@
+// Tagged p2p data movement on sm_100a.
+//
+// pull_kernel: one launch moves a batch of matched messages. Each descriptor
+// is a strided copy from the sender's buffer (mapped into this GPU through
+// CUDA IPC, so the loads cross NVLink; or local for self-sends) into the
+// receiver's buffer, both with arbitrary strides: the halo face/edge/corner
+// gather on the sender side and the ghost-region scatter on the receiver side
+// happen inside this one copy, with no pack/unpack buffers. The reference
+// moves bytes inside UCX's cuda_ipc transport after `.contiguous()` copies and
+// a host stream sync (reference: src/process_group_ucx.cpp:581-591, :490).
+//
+// Work split: each descriptor is cut into chunks of kChunkUnits units; CTAs
+// stride over the global chunk list. The CTA that finishes the last chunk of
+// a descriptor stores the descriptor's completion flag with release
+// semantics at system scope (the sender polls it from its own stream), after
+// which it zeroes the descriptor's counter so the scratch is clean for the
+// next launch on that stream.
+
+#include "cuda_common.hpp"
+#include "device_utils.cuh"
+
+namespace commux {
+namespace cuda {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;
+
+__device__ __forceinline__ void unit_offsets(const PullDesc& d, std::uint32_t u, std::int64_t& so,
+                                             std::int64_t& dof) {
+  if (d.ndim == 1) {
+    so = static_cast<std::int64_t>(u) * d.sst[kMaxPullDims - 1];
+    dof = static_cast<std::int64_t>(u) * d.dstr[kMaxPullDims - 1];
+    return;
+  }
+  so = 0;
+  dof = 0;
+  std::uint32_t rem = u;
+#pragma unroll
+  for (int i = kMaxPullDims - 1; i >= 1; --i) {
+    std::uint32_t q = d.div[i].div(rem);
+    std::uint32_t r = rem - q * d.div[i].d;
+    so += static_cast<std::int64_t>(r) * d.sst[i];
+    dof += static_cast<std::int64_t>(r) * d.dstr[i];
+    rem = q;
+  }
+  so += static_cast<std::int64_t>(rem) * d.sst[0];
+  dof += static_cast<std::int64_t>(rem) * d.dstr[0];
+}
+
+template <int U>
+__device__ __forceinline__ void copy_units(const PullDesc& d, std::uint32_t u0, std::uint32_t u1) {
+  using V = typename VecT<U>::T;
+  const std::uint32_t step = blockDim.x;
+  for (std::uint32_t base = u0 + threadIdx.x; base < u1; base += step * kUnroll) {
+    V v[kUnroll];
+    std::int64_t dofs[kUnroll];
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) {
+      std::uint32_t u = base + k * step;
+      if (u < u1) {
+        std::int64_t so;
+        unit_offsets(d, u, so, dofs[k]);
+        v[k] = *reinterpret_cast<const V*>(d.src + so);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) {
+      std::uint32_t u = base + k * step;
+      if (u < u1) *reinterpret_cast<V*>(d.dst + dofs[k]) = v[k];
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) pull_kernel(const __grid_constant__ PullBatch b) {
+  for (std::uint32_t c = blockIdx.x; c < b.total_chunks; c += gridDim.x) {
+    std::uint32_t di = 0;
+    while (di + 1 < b.n && c >= b.d[di + 1].chunk0) ++di;
+    const PullDesc& d = b.d[di];
+    const std::uint32_t u0 = (c - d.chunk0) * kChunkUnits;
+    const std::uint32_t u1 = min(u0 + kChunkUnits, d.units);
+    switch (d.unit) {
+      case 16:
+        copy_units<16>(d, u0, u1);
+        break;
+      case 8:
+        copy_units<8>(d, u0, u1);
+        break;
+      case 4:
+        copy_units<4>(d, u0, u1);
+        break;
+      case 2:
+        copy_units<2>(d, u0, u1);
+        break;
+      default:
+        copy_units<1>(d, u0, u1);
+        break;
+    }
+    __syncthreads();  // every load of this chunk has returned
+    if (threadIdx.x == 0) {
+      __threadfence();
+      std::uint32_t prev = atomicAdd(&b.counters[d.counter_idx], 1u);
+      if (prev + 1 == d.msg_chunks) {
+        b.counters[d.counter_idx] = 0u;
+        if (d.done != nullptr) {
+          fence_acq_rel_sys();
+          st_release_sys(d.done, d.done_val);
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// One warp: lane i waits until *flag[i] >= val[i], giving up after the
+// timeout (status word set, kernel returns; never traps).
+__global__ void wait_kernel(const __grid_constant__ WaitBatch b) {
+  const std::uint32_t i = threadIdx.x;
+  if (i >= b.n) return;
+  const std::uint64_t t0 = globaltimer_ns();
+  std::uint32_t spins = 0;
+  while (ld_acquire_sys(b.flag[i]) < b.val[i]) {
+    if ((++spins & 63u) == 0u && globaltimer_ns() - t0 > b.timeout_ns) {
+      report_status(b.status, kStatusWaitTimeout, reinterpret_cast<unsigned long long>(b.flag[i]),
+                    b.val[i], ld_acquire_sys(b.flag[i]));
+      return;
+    }
+    __nanosleep(128);
+  }
+}
+
+__global__ void signal_kernel(std::uint64_t* flag, std::uint64_t val) {
+  fence_acq_rel_sys();
+  st_release_sys(flag, val);
+}
+
+}  // namespace
+
+cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStream_t s) {
+  if (b.n == 0 || b.total_chunks == 0) return cudaSuccess;
+  int grid = static_cast<int>(b.total_chunks < static_cast<std::uint32_t>(max_ctas) ? b.total_chunks : max_ctas);
+  (void)threads;
+  pull_kernel<<<grid, kThreads, 0, s>>>(b);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_wait(const WaitBatch& b, cudaStream_t s) {
+  if (b.n == 0) return cudaSuccess;
+  wait_kernel<<<1, 32, 0, s>>>(b);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_signal(std::uint64_t* flag, std::uint64_t val, cudaStream_t s) {
+  signal_kernel<<<1, 1, 0, s>>>(flag, val);
+  return cudaGetLastError();
+}
+
+}  // namespace cuda
+}  // namespace commux

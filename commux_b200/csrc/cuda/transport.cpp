@@ -1,0 +1,980 @@
+#include "transport.hpp"
+
+#include <c10/cuda/CUDACachingAllocator.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <cuda.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <sstream>
+
+#include "coll.hpp"
+
+namespace commux {
+namespace cuda {
+
+namespace {
+
+constexpr std::uint32_t kWireMagic = 0x54524443u;
+constexpr int kWireDims = 8;
+constexpr std::uint64_t kSlots = 1ull << 16;  // consumed-flag slots per device
+constexpr std::uint64_t kMaxUnitsPerDesc = 1ull << 30;
+
+// One tensor of a device message, as the sender describes it.
+struct SegWire {
+  std::uint64_t buffer_id;  // allocation id in the sender process (0: local)
+  std::uint64_t base;       // allocation base address in the sender process
+  std::uint64_t alloc_size;
+  std::uint64_t offset;     // first element, bytes from base
+  cudaIpcMemHandle_t handle;
+  std::uint32_t elem;
+  std::int32_t ndim;
+  std::int64_t sizes[kWireDims];
+  std::int64_t strides[kWireDims];  // elements
+};
+
+struct DrtsWire {
+  std::uint32_t magic;
+  std::uint32_t nseg;
+  std::int32_t pid;
+  std::int32_t device;
+  unsigned char uuid[16];
+  std::uint32_t sender_waits_on_device;
+  std::uint32_t pad;
+  std::uint64_t mbox_id;
+  std::uint64_t mbox_base;
+  cudaIpcMemHandle_t mbox_handle;
+  std::uint64_t slot;
+  std::uint64_t value;
+};
+
+cudaStream_t current_stream(int dev) {
+  return c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(dev)).stream();
+}
+
+void cu_check(CUresult r, const char* what) {
+  if (r == CUDA_SUCCESS) return;
+  const char* s = nullptr;
+  cuGetErrorString(r, &s);
+  throw std::runtime_error(std::string("commux CUDA driver error in ") + what + ": " +
+                           (s ? s : "unknown"));
+}
+
+template <typename T>
+std::shared_ptr<T> state(const ReqPtr& r) {
+  return std::static_pointer_cast<T>(r->dev);
+}
+
+// A tensor dimension as (size, src stride, dst stride), strides in elements
+// or bytes depending on the stage.
+struct Dim {
+  std::int64_t size, ss, ds;
+};
+
+// Refine two shapes with equal element counts into one common shape (split
+// dims where they differ) so a single index walks both. Returns false when no
+// common refinement exists (e.g. sizes 6 and 4 facing each other).
+bool refine(const std::vector<std::pair<std::int64_t, std::int64_t>>& a,
+            const std::vector<std::pair<std::int64_t, std::int64_t>>& b, std::vector<Dim>& out) {
+  out.clear();
+  int i = static_cast<int>(a.size()) - 1, j = static_cast<int>(b.size()) - 1;
+  if (i < 0 || j < 0) return false;
+  std::int64_t ra = a[i].first, rb = b[j].first, sa = a[i].second, sb = b[j].second;
+  while (i >= 0 && j >= 0) {
+    std::int64_t m = std::min(ra, rb);
+    if (m <= 0 || ra % m || rb % m) return false;
+    out.push_back({m, sa, sb});
+    if (ra == m) {
+      if (--i >= 0) {
+        ra = a[i].first;
+        sa = a[i].second;
+      }
+    } else {
+      ra /= m;
+      sa *= m;
+    }
+    if (rb == m) {
+      if (--j >= 0) {
+        rb = b[j].first;
+        sb = b[j].second;
+      }
+    } else {
+      rb /= m;
+      sb *= m;
+    }
+  }
+  if (i >= 0 || j >= 0) return false;
+  std::reverse(out.begin(), out.end());
+  // merge dims that are contiguous in both
+  std::vector<Dim> m;
+  for (auto& d : out) {
+    if (!m.empty() && m.back().ss == d.size * d.ss && m.back().ds == d.size * d.ds) {
+      m.back().size *= d.size;
+      m.back().ss = d.ss;
+      m.back().ds = d.ds;
+    } else {
+      m.push_back(d);
+    }
+  }
+  out.swap(m);
+  return true;
+}
+
+std::vector<std::pair<std::int64_t, std::int64_t>> dims_of(const std::int64_t* sizes,
+                                                           const std::int64_t* strides, int nd) {
+  std::vector<std::pair<std::int64_t, std::int64_t>> v;
+  for (int k = 0; k < nd; ++k)
+    if (sizes[k] != 1) v.push_back({sizes[k], strides[k]});
+  if (v.empty()) v.push_back({1, 1});
+  return v;
+}
+
+// Turn common dims (element strides) into pull descriptors with the widest
+// vector unit the alignment allows; appends to `out`.
+void emit_descs(const char* sp, char* dp, std::vector<Dim> dims, std::int64_t elem,
+                std::vector<PullDesc>& out) {
+  // element strides -> byte strides
+  for (auto& d : dims) {
+    d.ss *= elem;
+    d.ds *= elem;
+  }
+  std::int64_t unit = elem;
+  Dim& in = dims.back();
+  if (in.ss == elem && in.ds == elem) {
+    std::int64_t inner_bytes = in.size * elem;
+    for (std::int64_t u : {16, 8, 4, 2, 1}) {
+      bool ok = inner_bytes % u == 0 && reinterpret_cast<std::uintptr_t>(sp) % u == 0 &&
+                reinterpret_cast<std::uintptr_t>(dp) % u == 0;
+      for (std::size_t k = 0; ok && k + 1 < dims.size(); ++k)
+        ok = dims[k].ss % u == 0 && dims[k].ds % u == 0;
+      if (ok) {
+        unit = u;
+        break;
+      }
+    }
+    in.size = inner_bytes / unit;
+    in.ss = unit;
+    in.ds = unit;
+  } else if (!(elem == 1 || elem == 2 || elem == 4 || elem == 8 || elem == 16)) {
+    throw std::runtime_error("commux: unsupported element size for a strided device copy");
+  }
+  if (dims.size() > static_cast<std::size_t>(kMaxPullDims))
+    throw std::runtime_error("layout");
+  // split along the outermost dim so every descriptor has < 2^30 units
+  std::int64_t per0 = 1;
+  for (std::size_t k = 1; k < dims.size(); ++k) per0 *= dims[k].size;
+  if (per0 > static_cast<std::int64_t>(kMaxUnitsPerDesc))
+    throw std::runtime_error("commux: device message row too large");
+  std::int64_t step0 = std::max<std::int64_t>(1, static_cast<std::int64_t>(kMaxUnitsPerDesc) / per0);
+  for (std::int64_t s0 = 0; s0 < dims[0].size; s0 += step0) {
+    std::int64_t n0 = std::min(step0, dims[0].size - s0);
+    PullDesc d;
+    std::memset(&d, 0, sizeof(d));
+    d.src = sp + s0 * dims[0].ss;
+    d.dst = dp + s0 * dims[0].ds;
+    d.ndim = static_cast<std::uint32_t>(dims.size());
+    d.unit = static_cast<std::uint32_t>(unit);
+    const int off = kMaxPullDims - static_cast<int>(dims.size());
+    for (int k = 0; k < kMaxPullDims; ++k) {
+      d.div[k] = FastDiv(1);
+      d.sst[k] = 0;
+      d.dstr[k] = 0;
+    }
+    std::int64_t units = 1;
+    for (std::size_t k = 0; k < dims.size(); ++k) {
+      std::int64_t sz = k == 0 ? n0 : dims[k].size;
+      d.div[off + k] = FastDiv(static_cast<std::uint32_t>(sz));
+      d.sst[off + k] = dims[k].ss;
+      d.dstr[off + k] = dims[k].ds;
+      units *= sz;
+    }
+    d.units = static_cast<std::uint32_t>(units);
+    d.nchunks = static_cast<std::uint32_t>(std::max<std::int64_t>(1, (units + kChunkUnits - 1) / kChunkUnits));
+    out.push_back(d);
+  }
+}
+
+bool contiguous_wire(const SegWire& s) {
+  std::int64_t expect = 1;
+  for (int k = s.ndim - 1; k >= 0; --k) {
+    if (s.sizes[k] != 1 && s.strides[k] != expect) return false;
+    expect *= s.sizes[k];
+  }
+  return true;
+}
+
+std::int64_t numel_wire(const SegWire& s) {
+  std::int64_t n = 1;
+  for (int k = 0; k < s.ndim; ++k) n *= s.sizes[k];
+  return n;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// device context
+// ---------------------------------------------------------------------------
+
+EventRef::~EventRef() {
+  if (ctx != nullptr && ev != nullptr) ctx->release(ev);
+}
+
+DevCtx::DevCtx(int d) : dev(d) {
+  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(d));
+  cudaDeviceProp prop;
+  CMX_CUDA(cudaGetDeviceProperties(&prop, d));
+  std::memcpy(uuid, prop.uuid.bytes, 16);
+  sm_count = prop.multiProcessorCount;
+  int lo = 0, hi = 0;
+  CMX_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+  CMX_CUDA(cudaStreamCreateWithPriority(&comm, cudaStreamNonBlocking, hi));
+  CMX_CUDA(cudaMalloc(reinterpret_cast<void**>(&mbox), kSlots * sizeof(std::uint64_t)));
+  CMX_CUDA(cudaMemsetAsync(mbox, 0, kSlots * sizeof(std::uint64_t), comm));
+  CMX_CUDA(cudaStreamSynchronize(comm));
+  CMX_CUDA(cudaIpcGetMemHandle(&mbox_handle, mbox));
+  unsigned long long id = 0;
+  cu_check(cuPointerGetAttribute(&id, CU_POINTER_ATTRIBUTE_BUFFER_ID,
+                                 reinterpret_cast<CUdeviceptr>(mbox)),
+           "cuPointerGetAttribute(mailbox)");
+  mbox_id = id;
+  mbox_base = reinterpret_cast<std::uint64_t>(mbox);
+  CMX_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&status_h), 64,
+                         cudaHostAllocMapped | cudaHostAllocPortable));
+  std::memset(status_h, 0, 64);
+  CMX_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&status_d), status_h, 0));
+}
+
+DevCtx::~DevCtx() {
+  // Process teardown may already have destroyed the context; ignore errors.
+  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev));
+  cudaStreamSynchronize(comm);
+  for (auto e : free_) cudaEventDestroy(e);
+  for (auto& kv : scratch_) cudaFree(kv.second);
+  if (mbox) cudaFree(mbox);
+  if (status_h) cudaFreeHost(status_h);
+  if (comm) cudaStreamDestroy(comm);
+}
+
+EventPtr DevCtx::event() {
+  cudaEvent_t e = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!free_.empty()) {
+      e = free_.back();
+      free_.pop_back();
+    }
+  }
+  if (e == nullptr) {
+    c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev));
+    CMX_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  }
+  auto p = std::make_shared<EventRef>();
+  p->ev = e;
+  p->ctx = this;
+  return p;
+}
+
+void DevCtx::release(cudaEvent_t e) {
+  std::lock_guard<std::mutex> lk(mu_);
+  free_.push_back(e);
+}
+
+std::uint32_t* DevCtx::scratch(cudaStream_t s) {
+  std::lock_guard<std::mutex> lk(mu_);
+  auto it = scratch_.find(s);
+  if (it != scratch_.end()) return it->second;
+  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev));
+  std::uint32_t* p = nullptr;
+  CMX_CUDA(cudaMalloc(reinterpret_cast<void**>(&p), kCounterSlots * sizeof(std::uint32_t)));
+  CMX_CUDA(cudaMemsetAsync(p, 0, kCounterSlots * sizeof(std::uint32_t), s));
+  scratch_[s] = p;
+  return p;
+}
+
+std::uint32_t DevCtx::take_slots(cudaStream_t s, std::uint32_t n) {
+  std::lock_guard<std::mutex> lk(mu_);
+  std::uint32_t& next = next_slot_[s];
+  std::uint32_t first = next;
+  next = (next + n) % kCounterSlots;
+  return first;
+}
+
+// ---------------------------------------------------------------------------
+// transport
+// ---------------------------------------------------------------------------
+
+CudaTransport::CudaTransport(Engine* e) : eng_(e) {
+  std::int64_t ms = env_int("COMMUX_DEVICE_TIMEOUT_MS", 60000);
+  std::int64_t host_ms = e->timeout().count();
+  if (host_ms > 0) ms = std::min(ms, host_ms);
+  timeout_ns_ = static_cast<std::uint64_t>(std::max<std::int64_t>(ms, 1)) * 1000000ull;
+}
+
+CudaTransport::~CudaTransport() { shutdown(); }
+
+void CudaTransport::shutdown() {
+  coll_.reset();
+  {
+    std::lock_guard<std::mutex> lk(pend_mu_);
+    pending_.clear();
+  }
+  flights_.clear();
+  std::lock_guard<std::mutex> lk(ipc_mu_);
+  for (auto& kv : opened_) cudaIpcCloseMemHandle(kv.second);
+  opened_.clear();
+}
+
+DevCtx* CudaTransport::ctx(int dev) {
+  std::lock_guard<std::mutex> lk(ctx_mu_);
+  auto& p = ctx_[dev];
+  if (!p) p = std::make_unique<DevCtx>(dev);
+  return p.get();
+}
+
+void CudaTransport::publish_uuid(DevCtx* c) {
+  if (uuid_published_) return;
+  auto* h = eng_->my_header();
+  std::memcpy(h->cuda_uuid, c->uuid, 16);
+  h->cuda_uuid_valid.store(1, std::memory_order_release);
+  uuid_published_ = true;
+}
+
+int CudaTransport::pull_ctas(DevCtx* c) const {
+  static const std::int64_t v = env_int("COMMUX_P2P_CTAS", 0);
+  return v > 0 ? static_cast<int>(v) : c->sm_count * 4;
+}
+
+void CudaTransport::ipc_export(const void* ptr, std::uint64_t* buffer_id, std::uint64_t* base,
+                               std::uint64_t* size, cudaIpcMemHandle_t* handle) {
+  CUpointer_attribute attrs[3] = {CU_POINTER_ATTRIBUTE_BUFFER_ID,
+                                  CU_POINTER_ATTRIBUTE_RANGE_START_ADDR,
+                                  CU_POINTER_ATTRIBUTE_RANGE_SIZE};
+  unsigned long long id = 0;
+  CUdeviceptr start = 0;
+  std::size_t sz = 0;
+  void* data[3] = {&id, &start, &sz};
+  cu_check(cuPointerGetAttributes(3, attrs, data, reinterpret_cast<CUdeviceptr>(ptr)),
+           "cuPointerGetAttributes");
+  *buffer_id = id;
+  *base = static_cast<std::uint64_t>(start);
+  *size = sz;
+  std::lock_guard<std::mutex> lk(ipc_mu_);
+  auto it = exported_.find(id);
+  if (it != exported_.end()) {
+    *handle = it->second;
+    return;
+  }
+  cudaError_t e = cudaIpcGetMemHandle(handle, reinterpret_cast<void*>(start));
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("commux: this CUDA tensor cannot be exported through CUDA IPC (") +
+                             cudaGetErrorString(e) +
+                             "); allocations made with PYTORCH_CUDA_ALLOC_CONF=expandable_segments:True "
+                             "are not exportable");
+  exported_[id] = *handle;
+  st_ipc_exports_++;
+}
+
+void* CudaTransport::ipc_open(int src, std::uint64_t buffer_id, const cudaIpcMemHandle_t& h,
+                              DevCtx* c) {
+  std::lock_guard<std::mutex> lk(ipc_mu_);
+  auto key = std::make_pair(src, buffer_id);
+  auto it = opened_.find(key);
+  if (it != opened_.end()) return it->second;
+  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(c->dev));
+  void* p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("commux: cudaIpcOpenMemHandle for rank ") +
+                             std::to_string(src) + " failed: " + cudaGetErrorString(e));
+  opened_[key] = p;
+  opened_lru_.push_back(key);
+  st_ipc_opens_++;
+  return p;
+}
+
+EventPtr ready_event_for(DevCtx* c, cudaStream_t s, int batch_depth,
+                         std::map<int, EventPtr>& batch_events) {
+  if (batch_depth > 0) {
+    auto it = batch_events.find(c->dev);
+    if (it != batch_events.end()) return it->second;
+  }
+  auto ev = c->event();
+  CMX_CUDA(cudaEventRecord(ev->ev, s));
+  if (batch_depth > 0) batch_events[c->dev] = ev;
+  return ev;
+}
+
+void CudaTransport::prepare_send(const ReqPtr& s, int dst, std::vector<char>& blob, bool* gate,
+                                 bool* complete_on_post) {
+  const int dev = s->tensors[0].device().index();
+  for (auto& t : s->tensors)
+    TORCH_CHECK(t.device().index() == dev, "commux send: a coalesced CUDA message spans devices");
+  DevCtx* c = ctx(dev);
+  publish_uuid(c);
+  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev));
+  auto st = std::make_shared<SendState>();
+  st->device = dev;
+  st->stream = current_stream(dev);
+  st->local = dst == eng_->rank();
+
+  std::vector<at::Tensor> wire_t;
+  for (auto& t : s->tensors) {
+    bool ok = t.dim() <= kWireDims;
+    for (int k = 0; ok && k < t.dim(); ++k) ok = t.stride(k) >= 0;
+    if (ok) {
+      wire_t.push_back(t);
+    } else {
+      st->staged.push_back(t.contiguous());
+      wire_t.push_back(st->staged.back());
+      st_staged_++;
+    }
+  }
+  {
+    std::lock_guard<std::mutex> lk(batch_mu_);
+    st->ready = ready_event_for(c, st->stream, batch_depth_, batch_event_);
+  }
+
+  blob.assign(sizeof(DrtsWire) + wire_t.size() * sizeof(SegWire), 0);
+  auto* w = reinterpret_cast<DrtsWire*>(blob.data());
+  w->magic = kWireMagic;
+  w->nseg = static_cast<std::uint32_t>(wire_t.size());
+  w->pid = static_cast<std::int32_t>(::getpid());
+  w->device = dev;
+  std::memcpy(w->uuid, c->uuid, 16);
+  if (!st->local) {
+    st->value = c->next_value.fetch_add(1) + 1;
+    st->slot = st->value % kSlots;
+    w->slot = st->slot;
+    w->value = st->value;
+    w->mbox_id = c->mbox_id;
+    w->mbox_base = c->mbox_base;
+    w->mbox_handle = c->mbox_handle;
+    const auto* ph = eng_->peer_header(dst);
+    bool known = ph->cuda_uuid_valid.load(std::memory_order_acquire) != 0;
+    bool same = known && std::memcmp(ph->cuda_uuid, c->uuid, 16) == 0;
+    st->device_wait = known && !same;
+  }
+  w->sender_waits_on_device = st->device_wait ? 1u : 0u;
+  auto* segs = reinterpret_cast<SegWire*>(blob.data() + sizeof(DrtsWire));
+  for (std::size_t i = 0; i < wire_t.size(); ++i) {
+    const at::Tensor& t = wire_t[i];
+    SegWire& sw = segs[i];
+    sw.elem = static_cast<std::uint32_t>(t.element_size());
+    sw.ndim = static_cast<std::int32_t>(t.dim());
+    for (int k = 0; k < t.dim(); ++k) {
+      sw.sizes[k] = t.size(k);
+      sw.strides[k] = t.stride(k);
+    }
+    if (t.numel() == 0) continue;
+    const char* p = static_cast<const char*>(t.data_ptr());
+    if (st->local) {
+      sw.base = reinterpret_cast<std::uint64_t>(p);
+      sw.offset = 0;
+    } else {
+      ipc_export(p, &sw.buffer_id, &sw.base, &sw.alloc_size, &sw.handle);
+      sw.offset = reinterpret_cast<std::uint64_t>(p) - sw.base;
+    }
+  }
+  s->dev = st;
+  *gate = !st->local;
+  *complete_on_post = st->device_wait;
+  if (st->local) {
+    std::lock_guard<std::mutex> lk(local_mu_);
+    local_sends_[s->id] = s;
+  }
+}
+
+bool CudaTransport::send_gate_open(const ReqPtr& s) {
+  auto st = state<SendState>(s);
+  if (!st || st->local) return true;
+  cudaError_t e = cudaEventQuery(st->ready->ev);
+  if (e == cudaSuccess) return true;
+  if (e == cudaErrorNotReady) return false;
+  cudaGetLastError();
+  std::lock_guard<std::mutex> lk(pend_mu_);
+  dev_error_ = std::string("commux: CUDA error while waiting for send data: ") + cudaGetErrorString(e);
+  return true;
+}
+
+void CudaTransport::prepare_recv(const ReqPtr& r) {
+  const int dev = r->tensors[0].device().index();
+  for (auto& t : r->tensors)
+    TORCH_CHECK(t.device().index() == dev, "commux recv: a coalesced CUDA message spans devices");
+  DevCtx* c = ctx(dev);
+  publish_uuid(c);
+  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev));
+  auto st = std::make_shared<RecvState>();
+  st->device = dev;
+  st->stream = current_stream(dev);
+  {
+    std::lock_guard<std::mutex> lk(batch_mu_);
+    st->ready = ready_event_for(c, st->stream, batch_depth_, batch_event_);
+  }
+  r->dev = st;
+}
+
+void CudaTransport::build_descs(const ReqPtr& r, const char* blob, std::size_t len, bool local,
+                                PendingPull& pp) {
+  auto* w = reinterpret_cast<const DrtsWire*>(blob);
+  if (len < sizeof(DrtsWire) || w->magic != kWireMagic ||
+      len < sizeof(DrtsWire) + w->nseg * sizeof(SegWire))
+    throw std::runtime_error("commux: malformed device message descriptor");
+  auto* segs = reinterpret_cast<const SegWire*>(blob + sizeof(DrtsWire));
+  auto rs = state<RecvState>(r);
+  DevCtx* c = pp.ctx;
+  std::uint64_t* done = nullptr;
+  std::uint64_t done_val = 0;
+  if (!local) {
+    auto* mb = static_cast<std::uint64_t*>(ipc_open(pp.src, w->mbox_id, w->mbox_handle, c));
+    done = mb + w->slot;
+    done_val = w->value;
+  }
+  std::uint64_t sbytes = 0;
+  for (std::uint32_t i = 0; i < w->nseg; ++i)
+    sbytes += static_cast<std::uint64_t>(numel_wire(segs[i])) * segs[i].elem;
+  if (sbytes > r->total)
+    throw std::runtime_error("commux recv: message of " + std::to_string(sbytes) +
+                             " bytes does not fit the " + std::to_string(r->total) + "-byte buffer");
+
+  auto src_ptr = [&](const SegWire& sw) -> const char* {
+    if (numel_wire(sw) == 0) return nullptr;
+    if (local) return reinterpret_cast<const char*>(sw.base + sw.offset);
+    auto* base = static_cast<const char*>(ipc_open(pp.src, sw.buffer_id, sw.handle, c));
+    return base + sw.offset;
+  };
+
+  std::vector<PullDesc> out;
+  bool paired = w->nseg == r->tensors.size();
+  for (std::uint32_t i = 0; paired && i < w->nseg; ++i)
+    paired = numel_wire(segs[i]) == r->tensors[i].numel() &&
+             segs[i].elem == static_cast<std::uint32_t>(r->tensors[i].element_size());
+  if (paired) {
+    for (std::uint32_t i = 0; i < w->nseg; ++i) {
+      const SegWire& sw = segs[i];
+      at::Tensor dt = r->tensors[i];
+      if (dt.numel() == 0) continue;
+      const char* sp = src_ptr(sw);
+      char* dp = static_cast<char*>(dt.data_ptr());
+      auto a = dims_of(sw.sizes, sw.strides, sw.ndim);
+      std::vector<std::int64_t> dsz(dt.sizes().begin(), dt.sizes().end());
+      std::vector<std::int64_t> dst(dt.strides().begin(), dt.strides().end());
+      auto b = dims_of(dsz.data(), dst.data(), static_cast<int>(dsz.size()));
+      std::vector<Dim> dims;
+      bool ok = refine(a, b, dims) && dims.size() <= static_cast<std::size_t>(kMaxPullDims);
+      if (ok) {
+        emit_descs(sp, dp, dims, sw.elem, out);
+        continue;
+      }
+      // No common <=4-dim walk: land in a contiguous temp laid out like the
+      // source, then scatter with a torch copy on the same stream.
+      std::vector<std::int64_t> ssz(sw.sizes, sw.sizes + sw.ndim);
+      at::Tensor tmp = at::empty(ssz, dt.options());
+      std::vector<std::int64_t> tstr(tmp.strides().begin(), tmp.strides().end());
+      auto tb = dims_of(ssz.data(), tstr.data(), sw.ndim);
+      if (!refine(a, tb, dims) || dims.size() > static_cast<std::size_t>(kMaxPullDims))
+        throw std::runtime_error("commux: the sender's tensor layout has more than 4 "
+                                 "non-mergeable dimensions; send a contiguous tensor");
+      emit_descs(sp, static_cast<char*>(tmp.data_ptr()), dims, sw.elem, out);
+      rs->unpack.push_back({tmp, dt});
+    }
+  } else {
+    // Byte-stream semantics (different tensor counts or element types): both
+    // sides must be contiguous; the bytes are concatenated in order.
+    std::vector<std::pair<const char*, std::uint64_t>> src_ranges;
+    for (std::uint32_t i = 0; i < w->nseg; ++i) {
+      if (!contiguous_wire(segs[i]))
+        throw std::runtime_error("commux recv: sender and receiver tensors differ in count or "
+                                 "dtype, which needs contiguous tensors on both sides");
+      std::uint64_t nb = static_cast<std::uint64_t>(numel_wire(segs[i])) * segs[i].elem;
+      if (nb) src_ranges.push_back({src_ptr(segs[i]), nb});
+    }
+    std::size_t di = 0;
+    std::uint64_t doff = 0;
+    for (auto& sr : src_ranges) {
+      std::uint64_t soff = 0;
+      while (soff < sr.second) {
+        while (di < r->tensors.size() &&
+               doff >= static_cast<std::uint64_t>(r->tensors[di].numel()) * r->tensors[di].element_size()) {
+          ++di;
+          doff = 0;
+        }
+        TORCH_CHECK(di < r->tensors.size(), "commux recv: receive buffers too small");
+        at::Tensor& dt = r->tensors[di];
+        TORCH_CHECK(dt.is_contiguous(), "commux recv: byte-stream receive needs contiguous tensors");
+        std::uint64_t dcap = static_cast<std::uint64_t>(dt.numel()) * dt.element_size() - doff;
+        std::uint64_t n = std::min(dcap, sr.second - soff);
+        std::vector<Dim> dims{{static_cast<std::int64_t>(n), 1, 1}};
+        emit_descs(sr.first + soff, static_cast<char*>(dt.data_ptr()) + doff, dims, 1, out);
+        soff += n;
+        doff += n;
+      }
+    }
+  }
+  if (out.empty()) {
+    PullDesc d;
+    std::memset(&d, 0, sizeof(d));
+    for (int k = 0; k < kMaxPullDims; ++k) d.div[k] = FastDiv(1);
+    d.ndim = 1;
+    d.unit = 1;
+    d.units = 0;
+    d.nchunks = 1;
+    out.push_back(d);
+  }
+  std::uint32_t chunks = 0;
+  for (auto& d : out) {
+    d.done = done;
+    d.done_val = done_val;
+    chunks += d.nchunks;
+    st_pull_bytes_ += static_cast<std::int64_t>(d.units) * d.unit;
+  }
+  pp.descs = std::move(out);
+  pp.msg_chunks = chunks;
+}
+
+void CudaTransport::on_match(const ReqPtr& r, int src, std::uint64_t send_id, const char* blob,
+                             std::size_t len) {
+  auto rs = state<RecvState>(r);
+  const bool local = src == eng_->rank();
+  DevCtx* c = ctx(rs->device);
+  ReqPtr s;
+  if (local) {
+    std::lock_guard<std::mutex> lk(local_mu_);
+    auto it = local_sends_.find(send_id);
+    if (it != local_sends_.end()) {
+      s = it->second;
+      local_sends_.erase(it);
+    }
+  }
+  auto* w = reinterpret_cast<const DrtsWire*>(blob);
+  if (!local && len >= sizeof(DrtsWire) && w->sender_waits_on_device &&
+      std::memcmp(w->uuid, c->uuid, 16) == 0) {
+    eng_->send_fin(src, send_id, -3);
+    eng_->fail(r, "commux: rank " + std::to_string(src) +
+                      " sends from the GPU this receive lives on while it expected another "
+                      "GPU; drive CUDA p2p from one device per rank");
+    return;
+  }
+  PendingPull pp;
+  pp.r = r;
+  pp.src = src;
+  pp.send_id = send_id;
+  pp.ctx = c;
+  try {
+    build_descs(r, blob, len, local, pp);
+  } catch (const std::exception& e) {
+    if (!local) eng_->send_fin(src, send_id, -4);
+    if (s) eng_->fail(s, e.what());
+    eng_->fail(r, e.what());
+    return;
+  }
+  st_pulls_++;
+  if (!local) {
+    {
+      std::lock_guard<std::mutex> lk(pend_mu_);
+      pending_.push_back(std::move(pp));
+      inflight_.fetch_add(1);
+    }
+    eng_->wake_progress();
+    return;
+  }
+  TORCH_CHECK(s, "commux: internal error, self-send state missing");
+  auto ss = state<SendState>(s);
+  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(c->dev));
+  cudaStream_t cur = current_stream(c->dev);
+  if (ss->stream != cur) CMX_CUDA(cudaStreamWaitEvent(cur, ss->ready->ev, 0));
+  if (rs->stream != cur) CMX_CUDA(cudaStreamWaitEvent(cur, rs->ready->ev, 0));
+  pp.descs.shrink_to_fit();
+  {
+    std::lock_guard<std::mutex> lk(batch_mu_);
+    if (batch_depth_ > 0) {
+      // launched together with the rest of the window at end_batch
+      batch_local_.push_back({std::move(pp), cur});
+      batch_local_sends_.push_back(s);
+      return;
+    }
+  }
+  std::vector<PendingPull> one;
+  one.push_back(std::move(pp));
+  launch_batch(c, one, cur);
+  ss->local_done = rs->done;
+  eng_->complete(s);
+}
+
+void CudaTransport::launch_batch(DevCtx* c, std::vector<PendingPull>& pulls, cudaStream_t stream) {
+  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(c->dev));
+  std::uint32_t* counters = c->scratch(stream);
+  std::uint32_t nmsg = static_cast<std::uint32_t>(pulls.size());
+  std::uint32_t next = c->take_slots(stream, nmsg);
+  PullBatch b;
+  std::memset(&b, 0, sizeof(b));
+  b.counters = counters;
+  b.status = c->status_d;
+  const int ctas = pull_ctas(c);
+  auto flush = [&]() {
+    if (b.n == 0) return;
+    CMX_CUDA(launch_pull(b, ctas, 256, stream));
+    kernel_launches++;
+    b.n = 0;
+    b.total_chunks = 0;
+  };
+  for (auto& p : pulls) {
+    std::uint32_t slot = next++ % kCounterSlots;
+    for (auto& d : p.descs) {
+      if (b.n == static_cast<std::uint32_t>(kMaxBatch)) flush();
+      d.chunk0 = b.total_chunks;
+      d.counter_idx = slot;
+      d.msg_chunks = p.msg_chunks;
+      b.d[b.n++] = d;
+      b.total_chunks += d.nchunks;
+    }
+  }
+  flush();
+  // receives that could not be walked directly land in a temp: scatter now
+  bool any_unpack = false;
+  for (auto& p : pulls) any_unpack |= !state<RecvState>(p.r)->unpack.empty();
+  if (any_unpack) {
+    c10::cuda::CUDAStreamGuard sg(c10::cuda::getStreamFromExternal(stream, static_cast<c10::DeviceIndex>(c->dev)));
+    for (auto& p : pulls)
+      for (auto& tv : state<RecvState>(p.r)->unpack) tv.second.copy_(tv.first.view(tv.second.sizes()));
+  }
+  auto done = c->event();
+  CMX_CUDA(cudaEventRecord(done->ev, stream));
+  const bool foreign = stream == c->comm;
+  for (auto& p : pulls) {
+    auto rs = state<RecvState>(p.r);
+    rs->done = done;
+    if (foreign)
+      for (auto& t : p.r->tensors)
+        if (t.numel() > 0)
+          c10::cuda::CUDACachingAllocator::recordStream(
+              t.storage().data_ptr(), c10::cuda::getStreamFromExternal(stream, static_cast<c10::DeviceIndex>(c->dev)));
+    eng_->complete(p.r);
+  }
+}
+
+bool CudaTransport::poll() {
+  bool busy = false;
+  std::vector<PendingPull> ready;
+  {
+    std::lock_guard<std::mutex> lk(pend_mu_);
+    for (auto it = pending_.begin(); it != pending_.end();) {
+      auto rs = state<RecvState>(it->r);
+      cudaError_t e = cudaEventQuery(rs->ready->ev);
+      if (e == cudaSuccess) {
+        ready.push_back(std::move(*it));
+        it = pending_.erase(it);
+      } else {
+        if (e != cudaErrorNotReady) {
+          cudaGetLastError();
+          dev_error_ = std::string("commux: CUDA error on a receive's stream: ") + cudaGetErrorString(e);
+        }
+        ++it;
+      }
+    }
+  }
+  if (!ready.empty()) {
+    busy = true;
+    std::map<DevCtx*, std::vector<PendingPull>> by_ctx;
+    for (auto& p : ready) by_ctx[p.ctx].push_back(std::move(p));
+    for (auto& kv : by_ctx) {
+      Flight f;
+      for (auto& p : kv.second) {
+        f.fins.push_back({p.src, p.send_id});
+        f.reqs.push_back(p.r);
+      }
+      launch_batch(kv.first, kv.second, kv.first->comm);
+      f.done = state<RecvState>(f.reqs.front())->done;
+      flights_.push_back(std::move(f));
+    }
+  }
+  while (!flights_.empty()) {
+    Flight& f = flights_.front();
+    cudaError_t e = cudaEventQuery(f.done->ev);
+    if (e == cudaErrorNotReady) break;
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      std::lock_guard<std::mutex> lk(pend_mu_);
+      dev_error_ = std::string("commux: CUDA error in a pull: ") + cudaGetErrorString(e);
+    }
+    for (auto& fin : f.fins) {
+      eng_->send_fin(fin.first, fin.second, e == cudaSuccess ? 0 : -5);
+      st_fins_++;
+    }
+    inflight_.fetch_sub(static_cast<int>(f.fins.size()));
+    flights_.pop_front();
+    busy = true;
+  }
+  return busy;
+}
+
+void CudaTransport::on_fin(const ReqPtr& s, std::int64_t status) {
+  auto st = state<SendState>(s);
+  if (st) st->fin.store(true, std::memory_order_release);
+  if (status != 0) {
+    const char* why = status == -3   ? "the receiver shares this GPU but the send expected a peer GPU"
+                      : status == -4 ? "the receiver could not describe the copy (layout/size mismatch)"
+                      : status == -5 ? "the receiver's copy kernel failed"
+                                     : "the receiver rejected the message";
+    eng_->fail(s, std::string("commux send: ") + why);
+    return;
+  }
+  if (st && !st->device_wait) eng_->complete(s);
+}
+
+void CudaTransport::wait_sends_on_stream(const std::vector<ReqPtr>& sends) {
+  // group the device-side waits per device into one-warp launches
+  std::map<int, std::vector<std::shared_ptr<SendState>>> by_dev;
+  for (auto& s : sends) {
+    auto st = state<SendState>(s);
+    if (st->fin.load(std::memory_order_acquire)) continue;  // consumed already
+    by_dev[st->device].push_back(st);
+  }
+  for (auto& kv : by_dev) {
+    DevCtx* c = ctx(kv.first);
+    c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(c->dev));
+    cudaStream_t cur = current_stream(c->dev);
+    WaitBatch b;
+    std::memset(&b, 0, sizeof(b));
+    b.timeout_ns = timeout_ns_;
+    b.status = c->status_d;
+    for (auto& st : kv.second) {
+      if (b.n == static_cast<std::uint32_t>(kMaxWaitFlags)) {
+        CMX_CUDA(launch_wait(b, cur));
+        kernel_launches++;
+        st_wait_kernels_++;
+        b.n = 0;
+      }
+      b.flag[b.n] = c->mbox + st->slot;
+      b.val[b.n] = st->value;
+      ++b.n;
+    }
+    if (b.n) {
+      CMX_CUDA(launch_wait(b, cur));
+      kernel_launches++;
+      st_wait_kernels_++;
+    }
+  }
+}
+
+void CudaTransport::stream_wait(const ReqPtr& r) { stream_wait_all({r}); }
+
+void CudaTransport::stream_wait_all(const std::vector<ReqPtr>& rs) {
+  std::vector<ReqPtr> dev_sends;
+  for (auto& r : rs) {
+    if (!r->dev || r->state.load() != kDone) continue;
+    if (r->kind == ReqKind::Recv) {
+      auto st = state<RecvState>(r);
+      if (!st->done) continue;
+      c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(st->device));
+      CMX_CUDA(cudaStreamWaitEvent(current_stream(st->device), st->done->ev, 0));
+    } else {
+      auto st = state<SendState>(r);
+      if (st->local) {
+        if (st->local_done) {
+          c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(st->device));
+          CMX_CUDA(cudaStreamWaitEvent(current_stream(st->device), st->local_done->ev, 0));
+        }
+      } else if (st->device_wait) {
+        dev_sends.push_back(r);
+      }
+    }
+  }
+  if (!dev_sends.empty()) wait_sends_on_stream(dev_sends);
+}
+
+bool CudaTransport::query(const ReqPtr& r) {
+  if (!r->dev) return true;
+  if (r->kind == ReqKind::Recv) {
+    auto st = state<RecvState>(r);
+    return st->done && cudaEventQuery(st->done->ev) == cudaSuccess;
+  }
+  auto st = state<SendState>(r);
+  if (st->local) return st->local_done && cudaEventQuery(st->local_done->ev) == cudaSuccess;
+  return st->fin.load(std::memory_order_acquire);
+}
+
+std::string CudaTransport::device_error() {
+  {
+    std::lock_guard<std::mutex> lk(pend_mu_);
+    if (!dev_error_.empty()) return dev_error_;
+  }
+  std::lock_guard<std::mutex> lk(ctx_mu_);
+  for (auto& kv : ctx_) {
+    volatile unsigned long long* st = kv.second->status_h;
+    unsigned long long code = st[0];
+    if (code == kStatusOk) continue;
+    std::ostringstream os;
+    if (code == kStatusWaitTimeout)
+      os << "commux: a device-side wait on GPU " << kv.first << " gave up after "
+         << timeout_ns_ / 1000000 << " ms (flag 0x" << std::hex << st[1] << std::dec
+         << " wanted " << st[2] << ", saw " << st[3] << "); the peer never completed its side";
+    else if (code == kStatusCollTimeout)
+      os << "commux: a device collective on GPU " << kv.first << " timed out waiting for rank "
+         << st[1] << " (barrier epoch " << st[2] << ")";
+    else
+      os << "commux: device error code " << code << " on GPU " << kv.first;
+    return os.str();
+  }
+  return "";
+}
+
+int CudaTransport::inflight() { return inflight_.load(); }
+
+void CudaTransport::begin_batch() {
+  std::lock_guard<std::mutex> lk(batch_mu_);
+  ++batch_depth_;
+}
+
+void CudaTransport::end_batch() {
+  std::vector<std::pair<PendingPull, cudaStream_t>> todo;
+  std::vector<ReqPtr> sends;
+  {
+    std::lock_guard<std::mutex> lk(batch_mu_);
+    if (batch_depth_ == 0 || --batch_depth_ > 0) return;
+    todo.swap(batch_local_);
+    sends.swap(batch_local_sends_);
+    batch_event_.clear();
+  }
+  if (todo.empty()) return;
+  std::map<std::pair<DevCtx*, cudaStream_t>, std::vector<PendingPull>> groups;
+  std::map<std::pair<DevCtx*, cudaStream_t>, std::vector<ReqPtr>> group_sends;
+  for (std::size_t i = 0; i < todo.size(); ++i) {
+    auto key = std::make_pair(todo[i].first.ctx, todo[i].second);
+    groups[key].push_back(std::move(todo[i].first));
+    group_sends[key].push_back(sends[i]);
+  }
+  for (auto& kv : groups) {
+    launch_batch(kv.first.first, kv.second, kv.first.second);
+    EventPtr done = state<RecvState>(kv.second.front().r)->done;
+    for (auto& s : group_sends[kv.first]) {
+      state<SendState>(s)->local_done = done;
+      eng_->complete(s);
+    }
+  }
+}
+
+std::vector<std::pair<std::string, std::int64_t>> CudaTransport::stats() {
+  std::vector<std::pair<std::string, std::int64_t>> v = {
+      {"cuda_pulls", st_pulls_.load()},
+      {"cuda_pull_bytes", st_pull_bytes_.load()},
+      {"cuda_kernel_launches", kernel_launches.load()},
+      {"cuda_wait_kernels", st_wait_kernels_.load()},
+      {"cuda_fins", st_fins_.load()},
+      {"cuda_ipc_opens", st_ipc_opens_.load()},
+      {"cuda_ipc_exports", st_ipc_exports_.load()},
+      {"cuda_staged_sends", st_staged_.load()},
+  };
+  if (coll_)
+    for (auto& kv : coll_->stats()) v.push_back(kv);
+  return v;
+}
+
+}  // namespace cuda
+}  // namespace commux
+
+extern "C" commux::DeviceTransport* commux_create_device_transport(commux::Engine* e) {
+  return new commux::cuda::CudaTransport(e);
+}

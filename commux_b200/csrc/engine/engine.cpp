@@ -71,6 +71,24 @@ std::string from_bytes(const std::vector<std::uint8_t>& v) {
   C10_THROW_ERROR(DistBackendError, msg);
 }
 
+// A process that exited but was not reaped yet (a zombie) still answers
+// kill(pid, 0); its /proc state says Z (or X) though.
+bool pid_alive(pid_t pid) {
+  if (::kill(pid, 0) != 0 && errno == ESRCH) return false;
+  char path[64];
+  std::snprintf(path, sizeof(path), "/proc/%d/stat", static_cast<int>(pid));
+  FILE* f = std::fopen(path, "r");
+  if (f == nullptr) return true;  // no procfs view: trust kill()
+  char buf[512];
+  std::size_t n = std::fread(buf, 1, sizeof(buf) - 1, f);
+  std::fclose(f);
+  buf[n] = '\0';
+  const char* rp = std::strrchr(buf, ')');  // "pid (comm) S ..."
+  if (rp == nullptr || rp[1] == '\0' || rp[2] == '\0') return true;
+  char state = rp[2];
+  return state != 'Z' && state != 'X';
+}
+
 }  // namespace
 
 FaultSpec FaultSpec::from_env() {
@@ -156,6 +174,7 @@ void Engine::bootstrap() {
   auto v = store_->add("commux/join", 1);
   std::int64_t gen = (v - 1) / size_;
   std::string pfx = "commux/" + std::to_string(gen) + "/";
+  prefix_ = pfx;
 
   std::uint64_t instance = 0;
   if (rank_ == 0) {
@@ -261,13 +280,47 @@ ReqPtr Engine::post_send(std::vector<at::Tensor> tensors, int dst, tag_t tag) {
     stats_.device_msgs++;
     DeviceTransport* d = device();
     std::vector<char> blob;
-    bool gate = false;
+    bool gate = false, complete_on_post = false;
+    if (dst == rank_) {
+      // Self-send: matched here, in the posting thread, so the copy can be
+      // launched on the caller's stream (no ring, no progress thread).
+      d->prepare_send(r, dst, blob, &gate, &complete_on_post);
+      ReqPtr rr;
+      {
+        std::lock_guard<std::mutex> lk(mu_);
+        rr = match_posted(rank_, r->key);
+        if (rr) {
+          rr->source = rank_;
+        } else {
+          auto u = std::make_shared<Unexpected>();
+          u->src = rank_;
+          u->key = r->key;
+          u->type = proto::kDrts;
+          u->total = r->total;
+          u->msg_id = r->id;
+          u->data = std::move(blob);
+          unexpected_[r->key].push_back(u);
+          ++unexpected_count_;
+          stats_.unexpected_msgs++;
+          return r;
+        }
+      }
+      if (!rr->device) {
+        fail(rr, "commux recv: a CUDA tensor was sent to a CPU receive buffer; "
+                 "send and receive tensors must live on the same kind of device");
+        fail(r, "commux send: the matching receive buffer is a CPU tensor");
+        return r;
+      }
+      d->on_match(rr, rank_, r->id, blob.data(), blob.size());
+      return r;
+    }
     {
       std::lock_guard<std::mutex> lk(mu_);
       sends_waiting_[r->id] = r;
     }
-    d->prepare_send(r, dst, blob, &gate);
+    d->prepare_send(r, dst, blob, &gate, &complete_on_post);
     auto job = std::make_unique<OutJob>();
+    job->complete_req_when_done = complete_on_post;
     job->type = proto::kDrts;
     job->head.resize(sizeof(proto::DrtsRec) + blob.size());
     auto* rec = reinterpret_cast<proto::DrtsRec*>(job->head.data());
@@ -277,17 +330,12 @@ ReqPtr Engine::post_send(std::vector<at::Tensor> tensors, int dst, tag_t tag) {
     rec->blob_bytes = static_cast<std::uint32_t>(blob.size());
     rec->pad = 0;
     std::memcpy(job->head.data() + sizeof(proto::DrtsRec), blob.data(), blob.size());
-    if (gate) {
-      // Sent by the progress thread once the device says the data is ready.
-      job->req = r;
-      std::lock_guard<std::mutex> lk(out_[dst]->mu);
-      out_[dst]->jobs.push_back(std::move(job));
-      out_[dst]->pending.fetch_add(1);
-      wake_progress();
-      return r;
-    }
+    job->req = r;
     enqueue(dst, std::move(job));
-    flush_out(dst, false);
+    if (gate)
+      wake_progress();  // the progress thread sends it once the data is ready
+    else
+      flush_out(dst, false);
     return r;
   }
 
@@ -581,7 +629,9 @@ void Engine::wake_progress() {
 void Engine::enqueue(int dst, std::unique_ptr<OutJob> job) {
   auto& po = *out_[dst];
   std::lock_guard<std::mutex> lk(po.mu);
-  po.jobs.push_back(std::move(job));
+  const bool control = job->type == proto::kFin || job->type == proto::kCts ||
+                       job->type == proto::kAbort;
+  (control ? po.ctrl : po.jobs).push_back(std::move(job));
   po.pending.fetch_add(1);
 }
 
@@ -670,7 +720,18 @@ bool Engine::flush_out(int dst, bool blocking_lock) {
     return false;
   bool wrote = false;
   std::vector<std::unique_ptr<OutJob>> finished;
-  while (!po.jobs.empty()) {
+  while (!po.ctrl.empty()) {
+    bool done = write_job(dst, po, *po.ctrl.front());
+    if (!done) {
+      stats_.ring_full_stalls++;
+      break;
+    }
+    wrote = true;
+    finished.push_back(std::move(po.ctrl.front()));
+    po.ctrl.pop_front();
+    po.pending.fetch_sub(1);
+  }
+  while (po.ctrl.empty() && !po.jobs.empty()) {
     OutJob& job = *po.jobs.front();
     if (job.type == proto::kDrts && job.req && dev_ && !dev_->send_gate_open(job.req)) break;
     bool done = write_job(dst, po, job);
@@ -1074,7 +1135,7 @@ void Engine::check_liveness() {
     if (p == rank_ || dead_[p].load()) continue;
     auto* h = segs_[p]->header();
     if (h->closed.load() != 0) continue;
-    if (::kill(static_cast<pid_t>(h->pid), 0) != 0 && errno == ESRCH) {
+    if (!pid_alive(static_cast<pid_t>(h->pid))) {
       fail_peer(p, "commux: peer rank " + std::to_string(p) + " (pid " +
                        std::to_string(h->pid) + ") exited without closing the group");
     }

@@ -113,7 +113,8 @@ struct OutJob {
 struct PeerOut {
   std::mutex mu;                  // serialises writers of this ring
   shm::RingWriter ring;
-  std::deque<std::unique_ptr<OutJob>> jobs;
+  std::deque<std::unique_ptr<OutJob>> ctrl;  // FIN/CTS/ABORT: never wait
+  std::deque<std::unique_ptr<OutJob>> jobs;  // matched messages, FIFO
   std::atomic<int> pending{0};
 };
 
@@ -141,6 +142,8 @@ class Engine {
   std::chrono::milliseconds timeout() const { return timeout_; }
   void set_timeout(std::chrono::milliseconds t) { timeout_ = t; }
   c10d::Store& store() { return *store_; }
+  // Store key prefix unique to this group ("commux/<generation>/").
+  const std::string& store_prefix() const { return prefix_; }
 
   // Post a send / receive of the given tensors. `iov` sends the vector as one
   // message (COMMUX_COALESCE); otherwise the caller passes one tensor.
@@ -209,6 +212,7 @@ class Engine {
                std::uint64_t n);
 
   c10::intrusive_ptr<c10d::Store> store_;
+  std::string prefix_;
   int rank_;
   int size_;
   std::chrono::milliseconds timeout_;
@@ -283,9 +287,12 @@ class DeviceTransport {
  public:
   virtual ~DeviceTransport() = default;
   // Sender: prepare a CUDA send; fills the descriptor blob carried by DRTS.
-  // Sets *gate when the DRTS may only go out once send_gate_open() is true.
+  // Sets *gate when the DRTS may only go out once send_gate_open() is true,
+  // and *complete_on_post when the send's host part is complete as soon as
+  // the DRTS is written (its device completion is then awaited on a stream).
+  // For dst == own rank the blob never leaves the process.
   virtual void prepare_send(const ReqPtr& s, int dst, std::vector<char>& blob,
-                            bool* gate) = 0;
+                            bool* gate, bool* complete_on_post) = 0;
   virtual bool send_gate_open(const ReqPtr& s) = 0;
   // Receiver: record the point on the consumer stream where the buffer may
   // be overwritten.
@@ -302,6 +309,8 @@ class DeviceTransport {
   virtual bool poll() = 0;
   // Order the caller's current stream after the request's device work.
   virtual void stream_wait(const ReqPtr& r) = 0;
+  // Same for a set of requests (one wait launch covers many sends).
+  virtual void stream_wait_all(const std::vector<ReqPtr>& rs) = 0;
   // Non-blocking: has the device work of `r` finished?
   virtual bool query(const ReqPtr& r) = 0;
   // Device-side error (timeout of a flag wait, ...) recorded so far.
@@ -324,6 +333,12 @@ class DeviceTransport {
   virtual DevCollPtr allgather(at::Tensor& out, const at::Tensor& in) = 0;
   virtual DevCollPtr reduce_scatter(at::Tensor& out, const at::Tensor& in, RedOp op) = 0;
   virtual DevCollPtr barrier() = 0;
+  // True if the device collectives can run on `dev` (every rank drives its
+  // own GPU). False when ranks share a GPU: kernels of different processes
+  // must never wait on each other on one GPU, so the caller stages through
+  // the host collectives instead. The first call is collective (workspace
+  // exchange): all ranks make it in the same order.
+  virtual bool device_collectives(int dev) = 0;
 };
 
 using DeviceTransportFactory = DeviceTransport* (*)(Engine*);

@@ -95,6 +95,7 @@ void Segment::create(const std::string& name, int nranks, int rank,
   hdr_->abort_rank.store(-1);
   hdr_->heartbeat.store(0);
   hdr_->closed.store(0);
+  hdr_->cuda_uuid_valid.store(0);
   for (int p = 0; p < nranks; ++p) {
     RingCtl* c = ring_ctl(p);
     new (c) RingCtl();

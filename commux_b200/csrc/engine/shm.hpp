@@ -24,7 +24,7 @@ namespace commux {
 namespace shm {
 
 constexpr std::uint64_t kSegMagic = 0x31584d4d4f434d53ull;  // "SMCOMMX1"
-constexpr std::uint32_t kSegVersion = 3;
+constexpr std::uint32_t kSegVersion = 4;
 
 // Record header; `len` covers header + payload and is a multiple of 8.
 struct WireHdr {
@@ -58,6 +58,10 @@ struct alignas(64) SegHeader {
   std::atomic<std::int32_t> abort_rank;
   alignas(64) std::atomic<std::uint64_t> heartbeat;  // bumped by progress
   alignas(64) std::atomic<std::uint32_t> closed;     // rank shut down cleanly
+  // CUDA device this rank drives p2p from (published on first CUDA use), so
+  // a sender knows whether its peer shares its GPU.
+  alignas(64) std::atomic<std::uint32_t> cuda_uuid_valid;
+  unsigned char cuda_uuid[16];
 };
 
 inline std::uint64_t align8(std::uint64_t n) { return (n + 7) & ~7ull; }

@@ -1,0 +1,121 @@
+// commux_b200._ops: compute kernels of the halo-exchange workload (sm_100a).
+//
+// jacobi7: one 7-point Jacobi sweep of a halo-padded 3-D fp64/fp32 field,
+//   v[z,y,x] = (u[z±1,y,x] + u[z,y±1,x] + u[z,y,x±1]) / 6   (interior only),
+// fused with the residual sum((v-u)^2) (atomically accumulated per block).
+// HBM-bound: each CTA owns a 32x8 (x,y) column tile and marches along z with
+// the z-1/z/z+1 values in registers and the current plane (with its x/y halo)
+// in shared memory, so every input element is read from DRAM about once.
+// The ghost shell of v is not written (the halo exchange fills it).
+
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+
+#include <atomic>
+#include <cstdint>
+
+namespace {
+
+constexpr int kTX = 32;
+constexpr int kTY = 8;
+constexpr int kZB = 16;  // planes per CTA
+
+std::atomic<std::int64_t> g_launches{0};
+
+template <typename T>
+__global__ void __launch_bounds__(kTX* kTY)
+    jacobi7_kernel(const T* __restrict__ u, T* __restrict__ v, int nz, int ny, int nx, int h,
+                   int iz, int iy, int ix, double* __restrict__ residual) {
+  __shared__ T plane[kTY + 2][kTX + 2];
+  __shared__ double red[kTX * kTY / 32];
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int x = h + blockIdx.x * kTX + tx;  // interior coordinates offset by the halo
+  const int y = h + blockIdx.y * kTY + ty;
+  const int z0 = h + blockIdx.z * kZB;
+  const int z1 = min(z0 + kZB, h + iz);
+  const bool active = x < h + ix && y < h + iy;
+  const std::int64_t sy = nx, sz = static_cast<std::int64_t>(ny) * nx;
+  const std::int64_t col = static_cast<std::int64_t>(y) * sy + x;
+  double acc = 0.0;
+  T below = active ? u[(z0 - 1) * sz + col] : T(0);
+  T cur = active ? u[z0 * sz + col] : T(0);
+  for (int z = z0; z < z1; ++z) {
+    const std::int64_t zo = z * sz;
+    T above = active ? u[zo + sz + col] : T(0);
+    plane[ty + 1][tx + 1] = cur;
+    if (active) {
+      if (tx == 0) plane[ty + 1][0] = u[zo + col - 1];
+      if (tx == kTX - 1 || x == h + ix - 1) plane[ty + 1][tx + 2] = u[zo + col + 1];
+      if (ty == 0) plane[0][tx + 1] = u[zo + col - sy];
+      if (ty == kTY - 1 || y == h + iy - 1) plane[ty + 2][tx + 1] = u[zo + col + sy];
+    }
+    __syncthreads();
+    if (active) {
+      T s = below + above + plane[ty + 1][tx] + plane[ty + 1][tx + 2] + plane[ty][tx + 1] +
+            plane[ty + 2][tx + 1];
+      T nv = s / T(6);
+      v[zo + col] = nv;
+      double d = static_cast<double>(nv) - static_cast<double>(cur);
+      acc += d * d;
+    }
+    __syncthreads();
+    below = cur;
+    cur = above;
+  }
+  if (residual != nullptr) {
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
+    const int lane = (ty * kTX + tx) & 31, warp = (ty * kTX + tx) >> 5;
+    if (lane == 0) red[warp] = acc;
+    __syncthreads();
+    if (warp == 0) {
+      acc = lane < kTX * kTY / 32 ? red[lane] : 0.0;
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
+      if (lane == 0) atomicAdd(residual, acc);
+    }
+  }
+}
+
+// v[interior] = jacobi(u); residual (optional, fp64 scalar on the device) += sum (v-u)^2
+void jacobi7(const at::Tensor& u, at::Tensor& v, int64_t halo, c10::optional<at::Tensor> residual) {
+  TORCH_CHECK(u.is_cuda() && v.is_cuda(), "jacobi7: CUDA tensors");
+  TORCH_CHECK(u.dim() == 3 && u.sizes() == v.sizes(), "jacobi7: matching 3-D fields");
+  TORCH_CHECK(u.is_contiguous() && v.is_contiguous(), "jacobi7: contiguous fields");
+  TORCH_CHECK(u.scalar_type() == v.scalar_type(), "jacobi7: same dtype");
+  TORCH_CHECK(halo >= 1, "jacobi7: halo >= 1");
+  const int nz = u.size(0), ny = u.size(1), nx = u.size(2), h = static_cast<int>(halo);
+  const int iz = nz - 2 * h, iy = ny - 2 * h, ix = nx - 2 * h;
+  TORCH_CHECK(iz > 0 && iy > 0 && ix > 0, "jacobi7: field smaller than its halo");
+  double* res = nullptr;
+  if (residual.has_value()) {
+    TORCH_CHECK(residual->is_cuda() && residual->scalar_type() == at::kDouble && residual->numel() >= 1,
+                "jacobi7: residual must be a CUDA float64 tensor");
+    res = residual->data_ptr<double>();
+  }
+  c10::cuda::CUDAGuard g(u.device());
+  auto stream = c10::cuda::getCurrentCUDAStream(u.device().index()).stream();
+  dim3 block(kTX, kTY);
+  dim3 grid((ix + kTX - 1) / kTX, (iy + kTY - 1) / kTY, (iz + kZB - 1) / kZB);
+  if (u.scalar_type() == at::kDouble)
+    jacobi7_kernel<double><<<grid, block, 0, stream>>>(u.data_ptr<double>(), v.data_ptr<double>(), nz, ny,
+                                                       nx, h, iz, iy, ix, res);
+  else if (u.scalar_type() == at::kFloat)
+    jacobi7_kernel<float><<<grid, block, 0, stream>>>(u.data_ptr<float>(), v.data_ptr<float>(), nz, ny, nx,
+                                                      h, iz, iy, ix, res);
+  else
+    TORCH_CHECK(false, "jacobi7: float32 or float64 fields");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  g_launches++;
+}
+
+int64_t launches() { return g_launches.load(); }
+
+}  // namespace
+
+PYBIND11_MODULE(_ops, m) {
+  m.doc() = "commux_b200 compute kernels (sm_100a)";
+  m.def("jacobi7", &jacobi7, py::arg("u"), py::arg("v"), py::arg("halo"), py::arg("residual") = py::none());
+  m.def("launches", &launches);
+}

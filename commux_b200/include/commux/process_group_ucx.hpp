@@ -142,6 +142,10 @@ class ProcessGroupUCX : public c10d::Backend {
  private:
   c10::intrusive_ptr<c10d::Work> post_p2p(std::vector<at::Tensor>& tensors,
                                           int peer, int tag, bool is_send);
+  bool device_coll(const at::Tensor& t);
+  static std::vector<at::Tensor> to_host(const std::vector<at::Tensor>& ts);
+  static void from_host(std::vector<at::Tensor>& ts,
+                        const std::vector<at::Tensor>& h);
 
   c10::intrusive_ptr<c10d::Store> store_;
   std::unique_ptr<Engine> engine_;
