@@ -48,6 +48,7 @@ def parse_args():
     ap.add_argument("--halo", type=int, default=2)
     ap.add_argument("--dtype", choices=["fp64", "fp32"], default="fp64")
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--clocks-raw", default=None, help="save the raw nvidia-smi samples here")
     ap.add_argument("--per-gpu-n", type=int, default=512,
                     help="interior points per GPU and axis (weak scaling); the global size is "
                          "per-gpu-n times the process grid")
@@ -119,7 +120,7 @@ def main() -> None:
     K = args.steps
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
     uuid = gpu_uuid(local_rank)
-    sampler = ClockSampler([uuid] if uuid else []).start()
+    sampler = ClockSampler([uuid] if uuid else [], raw_path=args.clocks_raw).start()
     launches0 = cuda_launches()
     torch.cuda.synchronize()
     dist.barrier()
@@ -151,6 +152,7 @@ def main() -> None:
     dist.barrier()
     e2e_wall = 0.0
     for k in range(Ke):
+        torch.cuda.current_stream().synchronize()  # previous update finished (not timed)
         t0 = time.perf_counter()
         forcing_d.copy_(forcing_h, non_blocking=True)
         model.inject(forcing_d)

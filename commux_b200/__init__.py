@@ -119,6 +119,32 @@ def reset_stats(group=None, device=None) -> None:
     _C.reset_stats(_backend_of(group, device))
 
 
+def batch_p2p(sends=(), recvs=(), group=None):
+    """Post tagged sends and receives as one batch and return one Work.
+
+    ``sends`` and ``recvs`` are sequences of ``(tensor, peer, tag)`` with peer
+    ranks of ``group`` (default group if None). Receives are posted first. This
+    is the native form of ``torch.distributed.batch_isend_irecv``: one call
+    into the backend for the whole exchange, one readiness event and (for
+    messages to self) one copy launch on CUDA.
+    """
+    group = group if group is not None else dist.distributed_c10d._get_default_group()
+    first = (list(recvs) + list(sends))[0][0]
+    backend = group._get_backend(first.device)
+    r = list(recvs)
+    s = list(sends)
+    return _C.batch_p2p(backend, [t for t, _, _ in r], [int(p) for _, p, _ in r], [int(g) for _, _, g in r],
+                        [t for t, _, _ in s], [int(p) for _, p, _ in s], [int(g) for _, _, g in s])
+
+
+def is_commux(group=None, device="cpu") -> bool:
+    """True if ``group`` runs on the commux backend."""
+    try:
+        return bool(_C.is_commux(_backend_of(group, device)))
+    except Exception:
+        return False
+
+
 def library_paths() -> list[str]:
     """Paths of the native libraries this package loads."""
     lib = os.path.join(_PKG, "lib")

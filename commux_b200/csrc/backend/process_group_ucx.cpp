@@ -578,8 +578,63 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::post_p2p(std::vector<at::Tensor>
   }
   glk.unlock();
 
-  std::vector<at::Tensor> keep;
+  std::vector<ReqPtr> reqs;
   std::vector<std::pair<at::Tensor, at::Tensor>> unpack;
+  post_now(tensors, peer, tag, is_send, reqs, unpack);
+  auto work = c10::make_intrusive<CommuxWork>(engine_.get(), is_send ? c10d::OpType::SEND : c10d::OpType::RECV,
+                                              reqs, is_send ? std::vector<at::Tensor>{} : tensors);
+  for (auto& tv : unpack) work->add_unpack(tv.first, tv.second);
+  glk.lock();
+  if (g.open && g.pending) {
+    g.pending->add(reqs, {});
+    for (auto& tv : unpack) g.pending->add_unpack(tv.first, tv.second);
+  }
+  return work;
+}
+
+c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::batch_p2p(
+    std::vector<at::Tensor>& recv_tensors, const std::vector<int>& recv_peers,
+    const std::vector<int>& recv_tags, std::vector<at::Tensor>& send_tensors,
+    const std::vector<int>& send_peers, const std::vector<int>& send_tags) {
+  TORCH_CHECK(recv_tensors.size() == recv_peers.size() && recv_peers.size() == recv_tags.size() &&
+                  send_tensors.size() == send_peers.size() && send_peers.size() == send_tags.size(),
+              "commux batch_p2p: tensors, peers and tags must have equal lengths");
+  const int P = getSize();
+  bool any_cuda = false;
+  for (auto* v : {&recv_tensors, &send_tensors})
+    for (auto& t : *v) any_cuda |= t.is_cuda();
+  auto work = c10::make_intrusive<CommuxWork>(engine_.get(), c10d::OpType::COALESCED,
+                                              std::vector<ReqPtr>{}, recv_tensors);
+  DeviceTransport* dev = any_cuda ? engine_->device() : nullptr;
+  if (dev) dev->begin_batch();
+  try {
+    for (int pass = 0; pass < 2; ++pass) {
+      const bool is_send = pass == 1;
+      auto& ts = is_send ? send_tensors : recv_tensors;
+      auto& peers = is_send ? send_peers : recv_peers;
+      auto& tags = is_send ? send_tags : recv_tags;
+      for (std::size_t i = 0; i < ts.size(); ++i) {
+        TORCH_CHECK(peers[i] >= 0 && peers[i] < P, "commux batch_p2p: invalid peer rank ", peers[i]);
+        std::vector<at::Tensor> one{ts[i]};
+        std::vector<ReqPtr> reqs;
+        std::vector<std::pair<at::Tensor, at::Tensor>> unpack;
+        post_now(one, peers[i], tags[i], is_send, reqs, unpack);
+        work->add(reqs, {});
+        for (auto& tv : unpack) work->add_unpack(tv.first, tv.second);
+      }
+    }
+  } catch (...) {
+    if (dev) dev->end_batch();
+    throw;
+  }
+  if (dev) dev->end_batch();
+  return work;
+}
+
+void ProcessGroupUCX::post_now(std::vector<at::Tensor>& tensors, int peer, int tag, bool is_send,
+                               std::vector<ReqPtr>& reqs,
+                               std::vector<std::pair<at::Tensor, at::Tensor>>& unpack) {
+  std::vector<at::Tensor> keep;
   keep.reserve(tensors.size());
   for (auto& t : tensors) {
     // CPU sends go from a contiguous copy (the reference does the same,
@@ -598,7 +653,6 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::post_p2p(std::vector<at::Tensor>
       keep.push_back(tmp);
     }
   }
-  std::vector<ReqPtr> reqs;
   const std::uint32_t ut = static_cast<std::uint32_t>(tag);
   if (keep.size() > 1 && coalesce_enabled()) {
     // one message for the whole vector, sub-index 0 (both sides decide from
@@ -612,15 +666,6 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::post_p2p(std::vector<at::Tensor>
                              : engine_->post_recv({keep[i]}, peer, tg));
     }
   }
-  auto work = c10::make_intrusive<CommuxWork>(engine_.get(), is_send ? c10d::OpType::SEND : c10d::OpType::RECV,
-                                              reqs, is_send ? std::vector<at::Tensor>{} : tensors);
-  for (auto& tv : unpack) work->add_unpack(tv.first, tv.second);
-  glk.lock();
-  if (g.open && g.pending) {
-    g.pending->add(reqs, {});
-    for (auto& tv : unpack) g.pending->add_unpack(tv.first, tv.second);
-  }
-  return work;
 }
 
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::send(std::vector<at::Tensor>& tensors, int dstRank,

@@ -132,7 +132,7 @@ CollImpl::CollImpl(CudaTransport* tr, int dev)
 }
 
 CollImpl::~CollImpl() {
-  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev_));
+  if (!select_device_quiet(dev_)) return;  // context gone at process exit
   if (stream_) cudaStreamSynchronize(stream_);
   for (int p = 0; p < P_; ++p)
     if (p != me_ && flags_[p]) cudaIpcCloseMemHandle(flags_[p]);

@@ -14,7 +14,7 @@ constexpr int kMaxPullDims = 4;      // dims of a pull descriptor after merging
 constexpr int kMaxBatch = 128;       // descriptors per pull launch (by value)
 constexpr int kMaxWaitFlags = 32;    // flags per wait launch (one warp)
 constexpr std::uint32_t kCounterSlots = 1024;  // per-stream message counters
-constexpr std::uint32_t kChunkUnits = 4096;  // units per CTA work item
+constexpr std::uint32_t kChunkUnits = 1024;  // units per CTA work item (16 KB of 16 B units)
 
 // 32-bit division by an invariant divisor through a multiply-high and a shift
 // (Granlund & Montgomery, "Division by invariant integers using

@@ -73,7 +73,7 @@ __device__ __forceinline__ void copy_units(const PullDesc& d, std::uint32_t u0, 
   }
 }
 
-__global__ void __launch_bounds__(kThreads) pull_kernel(const __grid_constant__ PullBatch b) {
+__global__ void __launch_bounds__(kThreads, 4) pull_kernel(const __grid_constant__ PullBatch b) {
   for (std::uint32_t c = blockIdx.x; c < b.total_chunks; c += gridDim.x) {
     std::uint32_t di = 0;
     while (di + 1 < b.n && c >= b.d[di + 1].chunk0) ++di;

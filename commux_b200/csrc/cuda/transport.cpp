@@ -197,6 +197,30 @@ void emit_descs(const char* sp, char* dp, std::vector<Dim> dims, std::int64_t el
   }
 }
 
+// Host-side bounds check of every descriptor before launch: the bytes a
+// descriptor touches must lie inside the source allocation (the IPC mapping)
+// and the destination storage. A layout bug then raises here instead of
+// reaching the GPU as an out-of-bounds access.
+void check_desc(const PullDesc& d, std::uintptr_t src_lo, std::uintptr_t src_hi,
+                std::uintptr_t dst_lo, std::uintptr_t dst_hi) {
+  if (d.units == 0) return;
+  std::int64_t s_min = 0, s_max = 0, d_min = 0, d_max = 0;
+  for (int k = 0; k < kMaxPullDims; ++k) {
+    std::int64_t ext = static_cast<std::int64_t>(d.div[k].d) - 1;
+    std::int64_t a = ext * d.sst[k], b = ext * d.dstr[k];
+    (a < 0 ? s_min : s_max) += a;
+    (b < 0 ? d_min : d_max) += b;
+  }
+  auto sp = reinterpret_cast<std::intptr_t>(d.src), dp = reinterpret_cast<std::intptr_t>(d.dst);
+  bool ok = sp + s_min >= static_cast<std::intptr_t>(src_lo) &&
+            sp + s_max + static_cast<std::intptr_t>(d.unit) <= static_cast<std::intptr_t>(src_hi) &&
+            dp + d_min >= static_cast<std::intptr_t>(dst_lo) &&
+            dp + d_max + static_cast<std::intptr_t>(d.unit) <= static_cast<std::intptr_t>(dst_hi);
+  if (!ok)
+    throw std::runtime_error("commux: internal error, a copy descriptor leaves its buffers "
+                             "(layout bug caught before launch)");
+}
+
 bool contiguous_wire(const SegWire& s) {
   std::int64_t expect = 1;
   for (int k = s.ndim - 1; k >= 0; --k) {
@@ -218,11 +242,27 @@ std::int64_t numel_wire(const SegWire& s) {
 // device context
 // ---------------------------------------------------------------------------
 
-EventRef::~EventRef() {
-  if (ctx != nullptr && ev != nullptr) ctx->release(ev);
+bool select_device_quiet(int dev) {
+  if (cudaSetDevice(dev) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return true;
 }
 
-DevCtx::DevCtx(int d) : dev(d) {
+EventPool::~EventPool() {
+  if (!select_device_quiet(dev)) return;  // context already gone at exit
+  for (auto e : free) cudaEventDestroy(e);
+}
+
+EventRef::~EventRef() {
+  if (pool && ev != nullptr) {
+    std::lock_guard<std::mutex> lk(pool->mu);
+    pool->free.push_back(ev);
+  }
+}
+
+DevCtx::DevCtx(int d) : dev(d), pool_(std::make_shared<EventPool>(d)) {
   c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(d));
   cudaDeviceProp prop;
   CMX_CUDA(cudaGetDeviceProperties(&prop, d));
@@ -248,23 +288,24 @@ DevCtx::DevCtx(int d) : dev(d) {
 }
 
 DevCtx::~DevCtx() {
-  // Process teardown may already have destroyed the context; ignore errors.
-  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev));
+  // At process exit the context may already be destroyed: then leave the
+  // resources to the driver instead of calling into a dead context.
+  if (!select_device_quiet(dev)) return;
   cudaStreamSynchronize(comm);
-  for (auto e : free_) cudaEventDestroy(e);
   for (auto& kv : scratch_) cudaFree(kv.second);
   if (mbox) cudaFree(mbox);
   if (status_h) cudaFreeHost(status_h);
   if (comm) cudaStreamDestroy(comm);
+  cudaGetLastError();
 }
 
 EventPtr DevCtx::event() {
   cudaEvent_t e = nullptr;
   {
-    std::lock_guard<std::mutex> lk(mu_);
-    if (!free_.empty()) {
-      e = free_.back();
-      free_.pop_back();
+    std::lock_guard<std::mutex> lk(pool_->mu);
+    if (!pool_->free.empty()) {
+      e = pool_->free.back();
+      pool_->free.pop_back();
     }
   }
   if (e == nullptr) {
@@ -273,13 +314,13 @@ EventPtr DevCtx::event() {
   }
   auto p = std::make_shared<EventRef>();
   p->ev = e;
-  p->ctx = this;
+  p->pool = pool_;
   return p;
 }
 
 void DevCtx::release(cudaEvent_t e) {
-  std::lock_guard<std::mutex> lk(mu_);
-  free_.push_back(e);
+  std::lock_guard<std::mutex> lk(pool_->mu);
+  pool_->free.push_back(e);
 }
 
 std::uint32_t* DevCtx::scratch(cudaStream_t s) {
@@ -321,10 +362,22 @@ void CudaTransport::shutdown() {
     std::lock_guard<std::mutex> lk(pend_mu_);
     pending_.clear();
   }
+  bool alive = true;
+  {
+    std::lock_guard<std::mutex> lk(ctx_mu_);
+    for (auto& kv : ctx_) {
+      // pulls read peer mappings: let them finish before the mappings go
+      // (pull kernels never wait on anything, so this returns)
+      alive = alive && select_device_quiet(kv.first);
+      if (alive) cudaStreamSynchronize(kv.second->comm);
+    }
+  }
   flights_.clear();
   std::lock_guard<std::mutex> lk(ipc_mu_);
-  for (auto& kv : opened_) cudaIpcCloseMemHandle(kv.second);
+  if (alive)
+    for (auto& kv : opened_) cudaIpcCloseMemHandle(kv.second);
   opened_.clear();
+  cudaGetLastError();
 }
 
 DevCtx* CudaTransport::ctx(int dev) {
@@ -344,7 +397,7 @@ void CudaTransport::publish_uuid(DevCtx* c) {
 
 int CudaTransport::pull_ctas(DevCtx* c) const {
   static const std::int64_t v = env_int("COMMUX_P2P_CTAS", 0);
-  return v > 0 ? static_cast<int>(v) : c->sm_count * 4;
+  return v > 0 ? static_cast<int>(v) : c->sm_count * 8;
 }
 
 void CudaTransport::ipc_export(const void* ptr, std::uint64_t* buffer_id, std::uint64_t* base,
@@ -422,8 +475,18 @@ void CudaTransport::prepare_send(const ReqPtr& s, int dst, std::vector<char>& bl
 
   std::vector<at::Tensor> wire_t;
   for (auto& t : s->tensors) {
+    // The receiver's copy kernel walks at most kMaxPullDims dims: stage a
+    // contiguous copy (on this stream, before the ready event) when the
+    // view's own dims do not merge down that far.
     bool ok = t.dim() <= kWireDims;
     for (int k = 0; ok && k < t.dim(); ++k) ok = t.stride(k) >= 0;
+    if (ok) {
+      std::vector<std::int64_t> sz(t.sizes().begin(), t.sizes().end());
+      std::vector<std::int64_t> sd(t.strides().begin(), t.strides().end());
+      auto d = dims_of(sz.data(), sd.data(), t.dim());
+      std::vector<Dim> merged;
+      ok = refine(d, d, merged) && merged.size() <= static_cast<std::size_t>(kMaxPullDims);
+    }
     if (ok) {
       wire_t.push_back(t);
     } else {
@@ -471,8 +534,15 @@ void CudaTransport::prepare_send(const ReqPtr& s, int dst, std::vector<char>& bl
     if (t.numel() == 0) continue;
     const char* p = static_cast<const char*>(t.data_ptr());
     if (st->local) {
-      sw.base = reinterpret_cast<std::uint64_t>(p);
-      sw.offset = 0;
+      CUpointer_attribute attrs[2] = {CU_POINTER_ATTRIBUTE_RANGE_START_ADDR, CU_POINTER_ATTRIBUTE_RANGE_SIZE};
+      CUdeviceptr start = 0;
+      std::size_t sz = 0;
+      void* data[2] = {&start, &sz};
+      cu_check(cuPointerGetAttributes(2, attrs, data, reinterpret_cast<CUdeviceptr>(p)),
+               "cuPointerGetAttributes");
+      sw.base = static_cast<std::uint64_t>(start);
+      sw.alloc_size = sz;
+      sw.offset = reinterpret_cast<std::uint64_t>(p) - sw.base;
     } else {
       ipc_export(p, &sw.buffer_id, &sw.base, &sw.alloc_size, &sw.handle);
       sw.offset = reinterpret_cast<std::uint64_t>(p) - sw.base;
@@ -539,14 +609,24 @@ void CudaTransport::build_descs(const ReqPtr& r, const char* blob, std::size_t l
     throw std::runtime_error("commux recv: message of " + std::to_string(sbytes) +
                              " bytes does not fit the " + std::to_string(r->total) + "-byte buffer");
 
-  auto src_ptr = [&](const SegWire& sw) -> const char* {
+  auto src_base = [&](const SegWire& sw) -> const char* {
     if (numel_wire(sw) == 0) return nullptr;
-    if (local) return reinterpret_cast<const char*>(sw.base + sw.offset);
-    auto* base = static_cast<const char*>(ipc_open(pp.src, sw.buffer_id, sw.handle, c));
-    return base + sw.offset;
+    if (local) return reinterpret_cast<const char*>(sw.base);
+    return static_cast<const char*>(ipc_open(pp.src, sw.buffer_id, sw.handle, c));
+  };
+  auto src_ptr = [&](const SegWire& sw) -> const char* {
+    const char* b = src_base(sw);
+    return b == nullptr ? nullptr : b + sw.offset;
   };
 
   std::vector<PullDesc> out;
+  // every descriptor appended since `from` must stay inside its buffers
+  auto validate = [&](std::size_t from, const SegWire& sw, const at::Tensor& dst) {
+    auto lo = reinterpret_cast<std::uintptr_t>(src_base(sw));
+    auto dlo = reinterpret_cast<std::uintptr_t>(dst.storage().data());
+    for (std::size_t k = from; k < out.size(); ++k)
+      check_desc(out[k], lo, lo + sw.alloc_size, dlo, dlo + dst.storage().nbytes());
+  };
   bool paired = w->nseg == r->tensors.size();
   for (std::uint32_t i = 0; paired && i < w->nseg; ++i)
     paired = numel_wire(segs[i]) == r->tensors[i].numel() &&
@@ -564,8 +644,10 @@ void CudaTransport::build_descs(const ReqPtr& r, const char* blob, std::size_t l
       auto b = dims_of(dsz.data(), dst.data(), static_cast<int>(dsz.size()));
       std::vector<Dim> dims;
       bool ok = refine(a, b, dims) && dims.size() <= static_cast<std::size_t>(kMaxPullDims);
+      const std::size_t from = out.size();
       if (ok) {
         emit_descs(sp, dp, dims, sw.elem, out);
+        validate(from, sw, dt);
         continue;
       }
       // No common <=4-dim walk: land in a contiguous temp laid out like the
@@ -578,19 +660,25 @@ void CudaTransport::build_descs(const ReqPtr& r, const char* blob, std::size_t l
         throw std::runtime_error("commux: the sender's tensor layout has more than 4 "
                                  "non-mergeable dimensions; send a contiguous tensor");
       emit_descs(sp, static_cast<char*>(tmp.data_ptr()), dims, sw.elem, out);
+      validate(from, sw, tmp);
       rs->unpack.push_back({tmp, dt});
     }
   } else {
     // Byte-stream semantics (different tensor counts or element types): both
     // sides must be contiguous; the bytes are concatenated in order.
     std::vector<std::pair<const char*, std::uint64_t>> src_ranges;
+    std::vector<const SegWire*> src_segs;
     for (std::uint32_t i = 0; i < w->nseg; ++i) {
       if (!contiguous_wire(segs[i]))
         throw std::runtime_error("commux recv: sender and receiver tensors differ in count or "
                                  "dtype, which needs contiguous tensors on both sides");
       std::uint64_t nb = static_cast<std::uint64_t>(numel_wire(segs[i])) * segs[i].elem;
-      if (nb) src_ranges.push_back({src_ptr(segs[i]), nb});
+      if (nb) {
+        src_ranges.push_back({src_ptr(segs[i]), nb});
+        src_segs.push_back(&segs[i]);
+      }
     }
+    std::size_t si = 0;
     std::size_t di = 0;
     std::uint64_t doff = 0;
     for (auto& sr : src_ranges) {
@@ -607,10 +695,13 @@ void CudaTransport::build_descs(const ReqPtr& r, const char* blob, std::size_t l
         std::uint64_t dcap = static_cast<std::uint64_t>(dt.numel()) * dt.element_size() - doff;
         std::uint64_t n = std::min(dcap, sr.second - soff);
         std::vector<Dim> dims{{static_cast<std::int64_t>(n), 1, 1}};
+        const std::size_t from = out.size();
         emit_descs(sr.first + soff, static_cast<char*>(dt.data_ptr()) + doff, dims, 1, out);
+        validate(from, *src_segs[si], dt);
         soff += n;
         doff += n;
       }
+      ++si;
     }
   }
   if (out.empty()) {
@@ -862,25 +953,32 @@ void CudaTransport::wait_sends_on_stream(const std::vector<ReqPtr>& sends) {
 void CudaTransport::stream_wait(const ReqPtr& r) { stream_wait_all({r}); }
 
 void CudaTransport::stream_wait_all(const std::vector<ReqPtr>& rs) {
+  // One stream wait per distinct event: the messages of one batch share the
+  // event of their launch.
   std::vector<ReqPtr> dev_sends;
+  std::vector<std::pair<int, cudaEvent_t>> events;
+  auto add = [&](int dev, const EventPtr& e) {
+    if (!e) return;
+    for (auto& x : events)
+      if (x.second == e->ev) return;
+    events.push_back({dev, e->ev});
+  };
   for (auto& r : rs) {
     if (!r->dev || r->state.load() != kDone) continue;
     if (r->kind == ReqKind::Recv) {
       auto st = state<RecvState>(r);
-      if (!st->done) continue;
-      c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(st->device));
-      CMX_CUDA(cudaStreamWaitEvent(current_stream(st->device), st->done->ev, 0));
+      add(st->device, st->done);
     } else {
       auto st = state<SendState>(r);
-      if (st->local) {
-        if (st->local_done) {
-          c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(st->device));
-          CMX_CUDA(cudaStreamWaitEvent(current_stream(st->device), st->local_done->ev, 0));
-        }
-      } else if (st->device_wait) {
+      if (st->local)
+        add(st->device, st->local_done);
+      else if (st->device_wait)
         dev_sends.push_back(r);
-      }
     }
+  }
+  for (auto& e : events) {
+    c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(e.first));
+    CMX_CUDA(cudaStreamWaitEvent(current_stream(e.first), e.second, 0));
   }
   if (!dev_sends.empty()) wait_sends_on_stream(dev_sends);
 }

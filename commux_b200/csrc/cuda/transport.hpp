@@ -54,10 +54,25 @@ namespace cuda {
 
 class DevCtx;
 
-// Event returned to its context's pool when the last holder drops it.
+// Select `dev` without throwing; false once the CUDA context is gone (process
+// teardown), in which case destructors skip their CUDA cleanup.
+bool select_device_quiet(int dev);
+
+// Pool of timing-free events of one device. Shared by every EventRef, so an
+// event can outlive the transport (a Work collected after the group was
+// destroyed still returns its event safely).
+struct EventPool {
+  explicit EventPool(int d) : dev(d) {}
+  ~EventPool();
+  int dev;
+  std::mutex mu;
+  std::vector<cudaEvent_t> free;
+};
+
+// Event returned to its pool when the last holder drops it.
 struct EventRef {
   cudaEvent_t ev = nullptr;
-  DevCtx* ctx = nullptr;
+  std::shared_ptr<EventPool> pool;
   ~EventRef();
 };
 using EventPtr = std::shared_ptr<EventRef>;
@@ -86,7 +101,7 @@ class DevCtx {
 
  private:
   std::mutex mu_;
-  std::vector<cudaEvent_t> free_;
+  std::shared_ptr<EventPool> pool_;
   std::unordered_map<cudaStream_t, std::uint32_t*> scratch_;
   std::unordered_map<cudaStream_t, std::uint32_t> next_slot_;
 };

@@ -16,6 +16,10 @@
 
 #include <atomic>
 #include <cstdint>
+#include <cstdlib>
+#include <string>
+
+#include "stencil_tma.cuh"
 
 namespace {
 
@@ -78,6 +82,71 @@ __global__ void __launch_bounds__(kTX* kTY)
   }
 }
 
+bool use_simple() {
+  static const bool v = [] {
+    const char* e = std::getenv("COMMUX_JACOBI");
+    return e != nullptr && std::string(e) == "simple";
+  }();
+  return v;
+}
+
+// host-mapped status word of the TMA kernel (nonzero: a bounded wait gave up)
+unsigned* status_word(unsigned** dev) {
+  static unsigned* host = nullptr;
+  static unsigned* device = nullptr;
+  if (host == nullptr) {
+    C10_CUDA_CHECK(cudaHostAlloc(reinterpret_cast<void**>(&host), 64, cudaHostAllocMapped | cudaHostAllocPortable));
+    *host = 0;
+    C10_CUDA_CHECK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&device), host, 0));
+  }
+  *dev = device;
+  return host;
+}
+
+template <typename T>
+void launch_tma(const at::Tensor& u, at::Tensor& v, int nz, int ny, int nx, int h, int iz, int iy, int ix,
+                double* res, cudaStream_t stream) {
+  using B = stencil::Box<T>;
+  CUtensorMap map;
+  cuuint64_t gdim[3] = {static_cast<cuuint64_t>(nx), static_cast<cuuint64_t>(ny), static_cast<cuuint64_t>(nz)};
+  cuuint64_t gstride[2] = {static_cast<cuuint64_t>(nx) * sizeof(T),
+                           static_cast<cuuint64_t>(nx) * ny * sizeof(T)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(B::kW), static_cast<cuuint32_t>(B::kH), 1};
+  cuuint32_t estride[3] = {1, 1, 1};
+  CUresult rc = cuTensorMapEncodeTiled(
+      &map, sizeof(T) == 8 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT64 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+      const_cast<void*>(u.data_ptr()), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+      CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(rc == CUDA_SUCCESS, "jacobi7: cuTensorMapEncodeTiled failed (", static_cast<int>(rc), ")");
+  static bool attr_set[2] = {false, false};
+  const int which = sizeof(T) == 8 ? 0 : 1;
+  if (!attr_set[which]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(stencil::jacobi7_tma_kernel<T>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, B::kSmem));
+    attr_set[which] = true;
+  }
+  unsigned* st_dev = nullptr;
+  status_word(&st_dev);
+  static const std::uint64_t limit_ns = [] {
+    const char* e = std::getenv("COMMUX_KERNEL_WAIT_MS");
+    return static_cast<std::uint64_t>(e ? std::atoll(e) : 2000) * 1000000ull;
+  }();
+  dim3 grid((ix + stencil::kTX - 1) / stencil::kTX, (iy + stencil::kTY - 1) / stencil::kTY,
+            (iz + stencil::kZB - 1) / stencil::kZB);
+  stencil::jacobi7_tma_kernel<T><<<grid, stencil::kThreads, B::kSmem, stream>>>(
+      map, v.data_ptr<T>(), nz, ny, nx, h, iz, iy, ix, res, st_dev, limit_ns);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// 0 when every TMA wait completed; nonzero after a bounded wait gave up.
+int64_t kernel_status(bool reset) {
+  unsigned* dev = nullptr;
+  unsigned* host = status_word(&dev);
+  int64_t v = *reinterpret_cast<volatile unsigned*>(host);
+  if (reset) *host = 0;
+  return v;
+}
+
 // v[interior] = jacobi(u); residual (optional, fp64 scalar on the device) += sum (v-u)^2
 void jacobi7(const at::Tensor& u, at::Tensor& v, int64_t halo, c10::optional<at::Tensor> residual) {
   TORCH_CHECK(u.is_cuda() && v.is_cuda(), "jacobi7: CUDA tensors");
@@ -96,6 +165,18 @@ void jacobi7(const at::Tensor& u, at::Tensor& v, int64_t halo, c10::optional<at:
   }
   c10::cuda::CUDAGuard g(u.device());
   auto stream = c10::cuda::getCurrentCUDAStream(u.device().index()).stream();
+  const bool tma_ok = (static_cast<std::int64_t>(nx) * u.element_size()) % 16 == 0 &&
+                      (reinterpret_cast<std::uintptr_t>(u.data_ptr()) & 15u) == 0 && ix >= 1;
+  if (tma_ok && !use_simple()) {
+    if (u.scalar_type() == at::kDouble)
+      launch_tma<double>(u, v, nz, ny, nx, h, iz, iy, ix, res, stream);
+    else if (u.scalar_type() == at::kFloat)
+      launch_tma<float>(u, v, nz, ny, nx, h, iz, iy, ix, res, stream);
+    else
+      TORCH_CHECK(false, "jacobi7: float32 or float64 fields");
+    g_launches++;
+    return;
+  }
   dim3 block(kTX, kTY);
   dim3 grid((ix + kTX - 1) / kTX, (iy + kTY - 1) / kTY, (iz + kZB - 1) / kZB);
   if (u.scalar_type() == at::kDouble)
@@ -118,4 +199,5 @@ PYBIND11_MODULE(_ops, m) {
   m.doc() = "commux_b200 compute kernels (sm_100a)";
   m.def("jacobi7", &jacobi7, py::arg("u"), py::arg("v"), py::arg("halo"), py::arg("residual") = py::none());
   m.def("launches", &launches);
+  m.def("kernel_status", &kernel_status, py::arg("reset") = false);
 }

@@ -56,6 +56,17 @@ PYBIND11_MODULE(_C, m) {
     return d;
   });
   m.def("reset_stats", [](const c10::intrusive_ptr<c10d::Backend>& b) { as_commux(b)->reset_stats(); });
+  m.def(
+      "batch_p2p",
+      [](const c10::intrusive_ptr<c10d::Backend>& b, std::vector<at::Tensor> recv_tensors,
+         std::vector<int> recv_peers, std::vector<int> recv_tags, std::vector<at::Tensor> send_tensors,
+         std::vector<int> send_peers, std::vector<int> send_tags) {
+        py::gil_scoped_release nogil;
+        return as_commux(b)->batch_p2p(recv_tensors, recv_peers, recv_tags, send_tensors, send_peers,
+                                       send_tags);
+      },
+      py::arg("backend"), py::arg("recv_tensors"), py::arg("recv_peers"), py::arg("recv_tags"),
+      py::arg("send_tensors"), py::arg("send_peers"), py::arg("send_tags"));
 
   py::class_<commux::IOContext, std::shared_ptr<commux::IOContext>>(m, "IOContext")
       .def(py::init([](c10::intrusive_ptr<c10d::Store> store, int rank, int size) {

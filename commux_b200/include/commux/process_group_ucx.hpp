@@ -44,6 +44,7 @@ constexpr tag_t kTagMaskAnySource = 0x0000FFFFFFFFFFFFull;
 class Engine;       // host tag-matching engine (opaque)
 class CollEngine;   // collective algorithms (opaque)
 struct GroupWindow;  // coalescing-window state (opaque)
+struct Request;      // one message in flight (opaque)
 
 class ProcessGroupUCX : public c10d::Backend {
  public:
@@ -127,6 +128,15 @@ class ProcessGroupUCX : public c10d::Backend {
   void startCoalescing() override;
   c10::intrusive_ptr<c10d::Work> endCoalescing() override;
 
+  // Post a batch of tagged receives and sends (receives first) as one group
+  // and return one Work covering all of them: the native form of
+  // torch.distributed.batch_isend_irecv. On CUDA the whole batch shares one
+  // readiness event and, for messages to self, one copy launch.
+  c10::intrusive_ptr<c10d::Work> batch_p2p(
+      std::vector<at::Tensor>& recv_tensors, const std::vector<int>& recv_peers,
+      const std::vector<int>& recv_tags, std::vector<at::Tensor>& send_tensors,
+      const std::vector<int>& send_peers, const std::vector<int>& send_tags);
+
   void setTimeout(std::chrono::milliseconds timeout) override;
   c10::intrusive_ptr<Options> getBackendOptions() override;
   void abort() override;
@@ -142,6 +152,9 @@ class ProcessGroupUCX : public c10d::Backend {
  private:
   c10::intrusive_ptr<c10d::Work> post_p2p(std::vector<at::Tensor>& tensors,
                                           int peer, int tag, bool is_send);
+  void post_now(std::vector<at::Tensor>& tensors, int peer, int tag, bool is_send,
+                std::vector<std::shared_ptr<Request>>& reqs,
+                std::vector<std::pair<at::Tensor, at::Tensor>>& unpack);
   bool device_coll(const at::Tensor& t);
   static std::vector<at::Tensor> to_host(const std::vector<at::Tensor>& ts);
   static void from_host(std::vector<at::Tensor>& ts,

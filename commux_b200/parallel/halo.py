@@ -88,6 +88,7 @@ class HaloExchange:
         self.grid = grid
         self.group = group
         self.directions = list(directions or DIRECTIONS)
+        self._native = None
         for n in self.n:
             if n < halo:
                 raise ValueError("interior must be at least as wide as the halo")
@@ -117,7 +118,25 @@ class HaloExchange:
         return ops
 
     def start(self, u: torch.Tensor) -> list:
-        return dist.batch_isend_irecv(self.ops(u))
+        """Post the 26 receives and 26 sends; returns the Works to wait on.
+
+        On the commux backend this is one native batch call; on any other
+        backend it goes through ``torch.distributed.batch_isend_irecv``.
+        """
+        if self._native is None:
+            import commux_b200
+
+            self._native = commux_b200.is_commux(self.group, u.device)
+        if not self._native:
+            return dist.batch_isend_irecv(self.ops(u))
+        import commux_b200
+
+        recvs, sends = [], []
+        for d in self.directions:
+            tag = TAG_BASE + dir_index(d)
+            recvs.append((self.recv_view(u, d), self.grid.neighbor(tuple(-o for o in d)), tag))
+            sends.append((self.send_view(u, d), self.grid.neighbor(d), tag))
+        return [commux_b200.batch_p2p(sends=sends, recvs=recvs, group=self.group)]
 
     def exchange(self, u: torch.Tensor) -> None:
         for w in self.start(u):

@@ -20,9 +20,10 @@ _REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_pow
 
 
 class ClockSampler:
-    def __init__(self, gpu_ids: list[str], interval_ms: int = 200):
+    def __init__(self, gpu_ids: list[str], interval_ms: int = 200, raw_path: str | None = None):
         self.gpu_ids = gpu_ids
         self.interval_ms = interval_ms
+        self.raw_path = raw_path
         self.proc = None
         self.out = None
 
@@ -46,7 +47,11 @@ class ClockSampler:
             self.proc.kill()
         self.out.flush()
         self.out.seek(0)
-        rows = [r.split(", ") for r in self.out.read().strip().splitlines() if r.strip()]
+        text = self.out.read()
+        if self.raw_path:
+            with open(self.raw_path, "w") as f:
+                f.write(text)
+        rows = [[c.strip() for c in r.split(",")] for r in text.strip().splitlines() if r.strip()]
         return summarize(rows)
 
 
