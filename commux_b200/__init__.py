@@ -62,6 +62,12 @@ else:
     TAG_MASK_ANY_SOURCE = _C.TAG_MASK_ANY_SOURCE
     IOContext = _C.IOContext
     make_tcp_io_context = _C.make_tcp_io_context
+    import atexit as _atexit
+
+    # Release CUDA state of groups still alive at exit while the CUDA context
+    # exists (interpreter teardown would otherwise free it too late).
+    if hasattr(_C, "_release_all"):
+        _atexit.register(_C._release_all)
 
 
 def create_backend(store, rank, size, timeout):

@@ -123,6 +123,15 @@ FaultSpec FaultSpec::from_env() {
 // construction / bootstrap
 // ---------------------------------------------------------------------------
 
+namespace {
+// every live engine (for the exit-time release)
+std::mutex g_registry_mu;
+std::vector<Engine*>& registry() {
+  static std::vector<Engine*> r;
+  return r;
+}
+}  // namespace
+
 Engine::Engine(c10::intrusive_ptr<c10d::Store> store, int rank, int size,
                std::chrono::milliseconds timeout)
     : store_(std::move(store)),
@@ -141,9 +150,48 @@ Engine::Engine(c10::intrusive_ptr<c10d::Store> store, int rank, int size,
   bootstrap();
   last_liveness_ = std::chrono::steady_clock::now();
   progress_ = std::thread([this] { progress_loop(); });
+  std::lock_guard<std::mutex> lk(g_registry_mu);
+  registry().push_back(this);
+}
+
+void Engine::release_all() {
+  std::vector<Engine*> all;
+  {
+    std::lock_guard<std::mutex> lk(g_registry_mu);
+    all = registry();
+  }
+  for (auto* e : all) e->release_for_exit();
+}
+
+void Engine::release_for_exit() {
+  if (released_.exchange(true)) return;
+  if (my_header() != nullptr) my_header()->closed.store(1);
+  stop_.store(true);
+  wake_progress();
+  if (progress_.joinable()) progress_.join();
+  {
+    std::lock_guard<std::mutex> lk(dev_mu_);
+    if (dev_) {
+      try {
+        dev_->shutdown();
+      } catch (...) {
+      }
+      dev_.reset();
+    }
+  }
+  std::lock_guard<std::mutex> lk(mu_);
+  posted_.clear();
+  unexpected_.clear();
+  sends_waiting_.clear();
+  for (auto& m : inflight_) m.clear();
 }
 
 Engine::~Engine() {
+  {
+    std::lock_guard<std::mutex> lk(g_registry_mu);
+    auto& r = registry();
+    r.erase(std::remove(r.begin(), r.end(), this), r.end());
+  }
   if (my_header() != nullptr) my_header()->closed.store(1);
   stop_.store(true);
   wake_progress();
@@ -249,6 +297,7 @@ void Engine::count_op() {
 
 ReqPtr Engine::post_send(std::vector<at::Tensor> tensors, int dst, tag_t tag) {
   count_op();
+  if (released_.load()) throw_backend("commux: the process is shutting down");
   if (aborted_.load()) throw_backend("commux: group aborted: " + failure_reason());
   if (dead_[dst].load())
     throw_backend("commux send: peer rank " + std::to_string(dst) + " has failed");
@@ -372,6 +421,7 @@ ReqPtr Engine::post_send(std::vector<at::Tensor> tensors, int dst, tag_t tag) {
 
 ReqPtr Engine::post_recv(std::vector<at::Tensor> tensors, int src, tag_t tag) {
   count_op();
+  if (released_.load()) throw_backend("commux: the process is shutting down");
   if (aborted_.load()) throw_backend("commux: group aborted: " + failure_reason());
   if (src >= 0 && dead_[src].load())
     throw_backend("commux recv: peer rank " + std::to_string(src) + " has failed");
@@ -1216,6 +1266,7 @@ void Engine::progress_loop() {
 DeviceTransport* Engine::device(bool create) {
   std::lock_guard<std::mutex> lk(dev_mu_);
   if (dev_ || !create) return dev_.get();
+  if (released_.load()) throw std::runtime_error("commux: the process is shutting down");
   // libcommux_cuda.so sits next to this library (found through dladdr), so
   // it resolves regardless of LD_LIBRARY_PATH; it is the only commux library
   // that links the CUDA runtime (reference keeps the same split:

@@ -173,6 +173,14 @@ class Engine {
 
   DeviceTransport* device(bool create = true);
   Stats& stats() { return stats_; }
+
+  // Drop every CUDA resource and every tensor reference this engine holds
+  // while the CUDA context is still alive (Python calls release_all() from
+  // an atexit hook). Afterwards the engine refuses new operations. Without
+  // this, a group kept alive until interpreter exit would free CUDA memory
+  // after the runtime tore its context down.
+  void release_for_exit();
+  static void release_all();
   const Stats& stats() const { return stats_; }
 
   // Internal fault injection hook (counts operations for kill:<rank>:<n>).
@@ -260,6 +268,7 @@ class Engine {
   void* dev_lib_ = nullptr;
 
   std::atomic<bool> stop_{false};
+  std::atomic<bool> released_{false};
   std::thread progress_;
   Stats stats_;
 };

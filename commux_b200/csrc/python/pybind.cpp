@@ -11,6 +11,7 @@
 #include <torch/csrc/distributed/c10d/Store.hpp>
 #include <utility>
 
+#include "../engine/engine.hpp"
 #include "commux/io.hpp"
 #include "commux/process_group_ucx.hpp"
 
@@ -56,6 +57,9 @@ PYBIND11_MODULE(_C, m) {
     return d;
   });
   m.def("reset_stats", [](const c10::intrusive_ptr<c10d::Backend>& b) { as_commux(b)->reset_stats(); });
+  m.def(
+      "_release_all", [] { commux::Engine::release_all(); }, py::call_guard<py::gil_scoped_release>(),
+      "Release every backend's CUDA state (atexit hook; the CUDA context is still alive then).");
   m.def(
       "batch_p2p",
       [](const c10::intrusive_ptr<c10d::Backend>& b, std::vector<at::Tensor> recv_tensors,

@@ -79,10 +79,11 @@ def summarize(rows: list[list[str]]) -> dict | None:
 
 
 def gpu_uuid(device_index: int) -> str | None:
-    """nvidia-smi id (``GPU-<uuid>``) of a torch CUDA device."""
+    """nvidia-smi id of a torch CUDA device: its PCI bus id (the CUDA UUID that
+    torch reports need not equal NVML's), else the index."""
     try:
         import torch
-        u = str(torch.cuda.get_device_properties(device_index).uuid)
-        return u if u.startswith("GPU-") else "GPU-" + u
+        p = torch.cuda.get_device_properties(device_index)
+        return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
     except Exception:
-        return None
+        return str(device_index)

@@ -5,6 +5,7 @@ from (rank-1) % world, so at world 1 every message is a self-send (launched
 on the caller's stream), with ranks sharing one GPU the host-gated path runs,
 and with one GPU per rank the device-flag path runs."""
 import os
+import zlib
 
 from common import Checker, init, torch, dist
 
@@ -15,7 +16,8 @@ g = torch.Generator(device="cpu").manual_seed(0)
 
 
 def data(shape, dtype, r):
-    gg = torch.Generator().manual_seed(hash((shape, str(dtype), r)) % (1 << 31))
+    # crc32, not hash(): string hashing is randomised per process
+    gg = torch.Generator().manual_seed(zlib.crc32(repr((shape, str(dtype), r)).encode()))
     if dtype.is_floating_point:
         return torch.randn(shape, generator=gg).to(dtype)
     return torch.randint(-100, 100, shape, generator=gg).to(dtype)
