@@ -143,6 +143,26 @@ def batch_p2p(sends=(), recvs=(), group=None):
                         [t for t, _, _ in s], [int(p) for _, p, _ in s], [int(g) for _, _, g in s])
 
 
+def p2p_plan(sends=(), recvs=(), group=None):
+    """Persistent plan of CUDA sends and receives, matched once.
+
+    ``sends``/``recvs`` are ``(tensor, peer, tag)`` like :func:`batch_p2p`.
+    ``plan.start()`` enqueues one exchange of the same buffers on the current
+    stream: a signal launch (data ready), one pull launch (copies, waiting on
+    the peers' ready flags on the device) and one wait launch (this rank's
+    data was consumed) -- no host matching and no host round trip per step.
+    Every rank the plan talks to creates its side in the same order and calls
+    start() the same number of times (the analogue of MPI_Startall).
+    """
+    group = group if group is not None else dist.distributed_c10d._get_default_group()
+    first = (list(recvs) + list(sends))[0][0]
+    backend = group._get_backend(first.device)
+    r = list(recvs)
+    s = list(sends)
+    return _C.p2p_plan(backend, [t for t, _, _ in r], [int(p) for _, p, _ in r], [int(g) for _, _, g in r],
+                       [t for t, _, _ in s], [int(p) for _, p, _ in s], [int(g) for _, _, g in s])
+
+
 def is_commux(group=None, device="cpu") -> bool:
     """True if ``group`` runs on the commux backend."""
     try:

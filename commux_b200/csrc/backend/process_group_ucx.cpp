@@ -493,6 +493,20 @@ ProcessGroupUCX::~ProcessGroupUCX() {
 
 void ProcessGroupUCX::setTimeout(std::chrono::milliseconds timeout) { engine_->set_timeout(timeout); }
 
+std::shared_ptr<DevicePlan> ProcessGroupUCX::p2p_plan(
+    const std::vector<at::Tensor>& recv_tensors, const std::vector<int>& recv_peers,
+    const std::vector<int>& recv_tags, const std::vector<at::Tensor>& send_tensors,
+    const std::vector<int>& send_peers, const std::vector<int>& send_tags) {
+  TORCH_CHECK(recv_tensors.size() == recv_peers.size() && recv_peers.size() == recv_tags.size() &&
+                  send_tensors.size() == send_peers.size() && send_peers.size() == send_tags.size(),
+              "commux p2p_plan: tensors, peers and tags must have equal lengths");
+  for (auto* v : {&recv_tensors, &send_tensors})
+    for (auto& t : *v)
+      TORCH_CHECK(t.is_cuda(), "commux p2p_plan: persistent plans take CUDA tensors (use batch_p2p on CPU)");
+  return engine_->device()->create_plan(recv_tensors, recv_peers, recv_tags, send_tensors, send_peers,
+                                        send_tags);
+}
+
 bool ProcessGroupUCX::device_coll(const at::Tensor& t) {
   return engine_->device()->device_collectives(t.device().index());
 }

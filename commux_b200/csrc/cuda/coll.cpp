@@ -137,7 +137,8 @@ CollImpl::~CollImpl() {
   for (int p = 0; p < P_; ++p)
     if (p != me_ && flags_[p]) cudaIpcCloseMemHandle(flags_[p]);
   if (ws_) cudaFree(ws_);
-  if (stream_) cudaStreamDestroy(stream_);
+  // stream_ stays: tensors freed later may carry stream-use records of it
+  cudaGetLastError();
 }
 
 int CollImpl::choose_ctas(int mode, int algo, std::int64_t bytes) const {

@@ -12,7 +12,7 @@ namespace cuda {
 
 constexpr int kMaxPullDims = 4;      // dims of a pull descriptor after merging
 constexpr int kMaxBatch = 128;       // descriptors per pull launch (by value)
-constexpr int kMaxWaitFlags = 32;    // flags per wait launch (one warp)
+constexpr int kMaxWaitFlags = 128;   // flags per wait launch (one thread each)
 constexpr std::uint32_t kCounterSlots = 1024;  // per-stream message counters
 constexpr std::uint32_t kChunkUnits = 1024;  // units per CTA work item (16 KB of 16 B units)
 
@@ -57,6 +57,10 @@ struct PullDesc {
   std::uint32_t counter_idx;        // per-message completion counter (scratch)
   std::uint64_t* done;              // flag to set once copied (may be remote)
   std::uint64_t done_val;
+  // persistent plans: the copy may start once *ready >= ready_val (a flag in
+  // this GPU's memory that the sender's stream sets); nullptr: no wait
+  const std::uint64_t* ready;
+  std::uint64_t ready_val;
 };
 
 struct PullBatch {
@@ -64,7 +68,16 @@ struct PullBatch {
   std::uint32_t total_chunks;
   std::uint32_t* counters;          // per-stream scratch, zero between launches
   unsigned long long* status;       // host-mapped status word (4 x u64)
+  std::uint64_t timeout_ns;         // bound of the ready-flag waits
   PullDesc d[kMaxBatch];
+};
+
+// Flags a signal launch stores (release, system scope), one thread each.
+constexpr int kMaxSignal = 128;
+struct SignalBatch {
+  std::uint32_t n;
+  std::uint64_t* flag[kMaxSignal];
+  std::uint64_t val[kMaxSignal];
 };
 
 // Flags a wait kernel polls (all in this GPU's own memory, written remotely).
@@ -88,6 +101,7 @@ enum : unsigned long long {
 cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStream_t s);
 cudaError_t launch_wait(const WaitBatch& b, cudaStream_t s);
 cudaError_t launch_signal(std::uint64_t* flag, std::uint64_t val, cudaStream_t s);
+cudaError_t launch_signal_many(const SignalBatch& b, cudaStream_t s);
 
 }  // namespace cuda
 }  // namespace commux

@@ -73,13 +73,42 @@ __device__ __forceinline__ void copy_units(const PullDesc& d, std::uint32_t u0, 
   }
 }
 
+// Bounded wait for a persistent plan's ready flag (thread 0 of the CTA).
+// Gives up after the timeout, or at once if another wait already failed.
+__device__ __forceinline__ bool wait_ready(const PullDesc& d, const PullBatch& b) {
+  if (ld_acquire_sys(d.ready) >= d.ready_val) return true;
+  const std::uint64_t t0 = globaltimer_ns();
+  std::uint32_t spins = 0;
+  while (ld_acquire_sys(d.ready) < d.ready_val) {
+    if ((++spins & 63u) == 0u) {
+      if (*reinterpret_cast<volatile unsigned long long*>(b.status) != 0ull) return false;
+      if (globaltimer_ns() - t0 > b.timeout_ns) {
+        report_status(b.status, kStatusWaitTimeout, reinterpret_cast<unsigned long long>(d.ready),
+                      d.ready_val, ld_acquire_sys(d.ready));
+        return false;
+      }
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
 __global__ void __launch_bounds__(kThreads, 4) pull_kernel(const __grid_constant__ PullBatch b) {
+  __shared__ int skip;
   for (std::uint32_t c = blockIdx.x; c < b.total_chunks; c += gridDim.x) {
     std::uint32_t di = 0;
     while (di + 1 < b.n && c >= b.d[di + 1].chunk0) ++di;
     const PullDesc& d = b.d[di];
     const std::uint32_t u0 = (c - d.chunk0) * kChunkUnits;
-    const std::uint32_t u1 = min(u0 + kChunkUnits, d.units);
+    bool failed = false;
+    if (d.ready != nullptr) {  // persistent plan: wait for the sender's data
+      if (threadIdx.x == 0) skip = wait_ready(d, b) ? 0 : 1;
+      __syncthreads();
+      failed = skip != 0;
+    }
+    // a failed wait copies nothing but still counts, so the scratch counter
+    // returns to zero; the message's completion flag is then not stored
+    const std::uint32_t u1 = failed ? u0 : min(u0 + kChunkUnits, d.units);
     switch (d.unit) {
       case 16:
         copy_units<16>(d, u0, u1);
@@ -100,10 +129,13 @@ __global__ void __launch_bounds__(kThreads, 4) pull_kernel(const __grid_constant
     __syncthreads();  // every load of this chunk has returned
     if (threadIdx.x == 0) {
       __threadfence();
+      constexpr std::uint32_t kFailBit = 0x80000000u;
+      if (failed) atomicOr(&b.counters[d.counter_idx], kFailBit);
       std::uint32_t prev = atomicAdd(&b.counters[d.counter_idx], 1u);
-      if (prev + 1 == d.msg_chunks) {
+      if ((prev & ~kFailBit) + 1 == d.msg_chunks) {
+        const bool any_failed = failed || (prev & kFailBit) != 0u;
         b.counters[d.counter_idx] = 0u;
-        if (d.done != nullptr) {
+        if (d.done != nullptr && !any_failed) {
           fence_acq_rel_sys();
           st_release_sys(d.done, d.done_val);
         }
@@ -111,6 +143,15 @@ __global__ void __launch_bounds__(kThreads, 4) pull_kernel(const __grid_constant
     }
     __syncthreads();
   }
+}
+
+// Store each flag with release semantics at system scope (after everything
+// the stream did before): "data ready" signals of persistent plans.
+__global__ void signal_many_kernel(const __grid_constant__ SignalBatch b) {
+  const std::uint32_t i = threadIdx.x;
+  if (i >= b.n) return;
+  fence_acq_rel_sys();
+  st_release_sys(b.flag[i], b.val[i]);
 }
 
 // One warp: lane i waits until *flag[i] >= val[i], giving up after the
@@ -147,7 +188,13 @@ cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStrea
 
 cudaError_t launch_wait(const WaitBatch& b, cudaStream_t s) {
   if (b.n == 0) return cudaSuccess;
-  wait_kernel<<<1, 32, 0, s>>>(b);
+  wait_kernel<<<1, kMaxWaitFlags, 0, s>>>(b);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_signal_many(const SignalBatch& b, cudaStream_t s) {
+  if (b.n == 0) return cudaSuccess;
+  signal_many_kernel<<<1, kMaxSignal, 0, s>>>(b);
   return cudaGetLastError();
 }
 

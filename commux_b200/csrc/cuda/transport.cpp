@@ -12,6 +12,7 @@
 #include <sstream>
 
 #include "coll.hpp"
+#include "commux/process_group_ucx.hpp"
 
 namespace commux {
 namespace cuda {
@@ -271,8 +272,10 @@ DevCtx::DevCtx(int d) : dev(d), pool_(std::make_shared<EventPool>(d)) {
   int lo = 0, hi = 0;
   CMX_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
   CMX_CUDA(cudaStreamCreateWithPriority(&comm, cudaStreamNonBlocking, hi));
-  CMX_CUDA(cudaMalloc(reinterpret_cast<void**>(&mbox), kSlots * sizeof(std::uint64_t)));
-  CMX_CUDA(cudaMemsetAsync(mbox, 0, kSlots * sizeof(std::uint64_t), comm));
+  // [0, kSlots): consumed flags of one-shot sends; [kSlots, 2 kSlots): flags
+  // of persistent plans (never reused)
+  CMX_CUDA(cudaMalloc(reinterpret_cast<void**>(&mbox), 2 * kSlots * sizeof(std::uint64_t)));
+  CMX_CUDA(cudaMemsetAsync(mbox, 0, 2 * kSlots * sizeof(std::uint64_t), comm));
   CMX_CUDA(cudaStreamSynchronize(comm));
   CMX_CUDA(cudaIpcGetMemHandle(&mbox_handle, mbox));
   unsigned long long id = 0;
@@ -295,7 +298,9 @@ DevCtx::~DevCtx() {
   for (auto& kv : scratch_) cudaFree(kv.second);
   if (mbox) cudaFree(mbox);
   if (status_h) cudaFreeHost(status_h);
-  if (comm) cudaStreamDestroy(comm);
+  // `comm` is not destroyed: tensors freed later may still carry stream-use
+  // records of it in torch's caching allocator, which then records events on
+  // it. A stream lives until process exit anyway.
   cudaGetLastError();
 }
 
@@ -833,15 +838,12 @@ void CudaTransport::launch_batch(DevCtx* c, std::vector<PendingPull>& pulls, cud
   }
   auto done = c->event();
   CMX_CUDA(cudaEventRecord(done->ev, stream));
-  const bool foreign = stream == c->comm;
+  // No recordStream on the receive tensors: the request (and its tensors)
+  // stays referenced until the done event completed (progress thread), and a
+  // caller that waited has its stream ordered after that event.
   for (auto& p : pulls) {
     auto rs = state<RecvState>(p.r);
     rs->done = done;
-    if (foreign)
-      for (auto& t : p.r->tensors)
-        if (t.numel() > 0)
-          c10::cuda::CUDACachingAllocator::recordStream(
-              t.storage().data_ptr(), c10::cuda::getStreamFromExternal(stream, static_cast<c10::DeviceIndex>(c->dev)));
     eng_->complete(p.r);
   }
 }
@@ -1068,6 +1070,376 @@ std::vector<std::pair<std::string, std::int64_t>> CudaTransport::stats() {
   if (coll_)
     for (auto& kv : coll_->stats()) v.push_back(kv);
   return v;
+}
+
+// ---------------------------------------------------------------------------
+// persistent plans
+// ---------------------------------------------------------------------------
+
+namespace {
+
+constexpr std::uint32_t kPlanSub = 0x7FF0;       // sub-index of setup descriptors
+constexpr std::uint32_t kPlanReplySub = 0x7FF1;  // sub-index of setup replies
+constexpr std::uint32_t kPlanMagic = 0x4E414C50u;
+
+// receiver -> sender at setup: where the sender stores "ready"
+struct PlanReply {
+  std::uint32_t magic;
+  std::int32_t pid;
+  unsigned char uuid[16];
+  std::uint64_t mbox_id;
+  cudaIpcMemHandle_t mbox_handle;
+  std::uint64_t ready_slot;
+};
+
+enum class PlanMode { Local, Device, Shared };
+
+}  // namespace
+
+class CudaPlan final : public DevicePlan {
+ public:
+  struct Msg {
+    at::Tensor t;
+    int peer = -1;
+    int tag = 0;
+    PlanMode mode = PlanMode::Local;
+    std::uint64_t* ready_remote = nullptr;    // send: where "ready" is stored
+    std::uint64_t* consumed_local = nullptr;  // send: set by the receiver's pull
+    const std::uint64_t* ready_local = nullptr;  // recv: set by the sender
+    std::vector<PullDesc> descs;              // recv (local/device)
+    bool matched = false;                     // self recv paired with a send
+  };
+
+  CudaPlan(CudaTransport* tr, Engine* eng, DevCtx* c) : tr_(tr), eng_(eng), c_(c) {}
+  std::vector<Msg> sends, recvs;
+
+  void start() override {
+    ++epoch_;
+    c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(c_->dev));
+    cudaStream_t cur = c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(c_->dev)).stream();
+    // messages to/from a rank on this same GPU go through the host-gated path
+    std::vector<ReqPtr> shared;
+    if (n_shared_) {
+      tr_->begin_batch();
+      try {
+        for (auto& m : recvs)
+          if (m.mode == PlanMode::Shared)
+            shared.push_back(eng_->post_recv({m.t}, m.peer, make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), 0, false)));
+        for (auto& m : sends)
+          if (m.mode == PlanMode::Shared)
+            shared.push_back(eng_->post_send({m.t}, m.peer, make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), 0, false)));
+      } catch (...) {
+        tr_->end_batch();
+        throw;
+      }
+      tr_->end_batch();
+    }
+    // 1. tell every receiver on another GPU that this rank's data is ready
+    SignalBatch sb;
+    std::memset(&sb, 0, sizeof(sb));
+    for (auto& m : sends) {
+      if (m.mode != PlanMode::Device) continue;
+      if (sb.n == static_cast<std::uint32_t>(kMaxSignal)) {
+        CMX_CUDA(launch_signal_many(sb, cur));
+        tr_->kernel_launches++;
+        sb.n = 0;
+      }
+      sb.flag[sb.n] = m.ready_remote;
+      sb.val[sb.n++] = epoch_;
+    }
+    if (sb.n) {
+      CMX_CUDA(launch_signal_many(sb, cur));
+      tr_->kernel_launches++;
+    }
+    // 2. one pull launch for every receive (waits on the peers' ready flags)
+    std::vector<std::vector<PullDesc>> msgs;
+    for (auto& m : recvs) {
+      if (m.mode == PlanMode::Shared) continue;
+      std::vector<PullDesc> d = m.descs;
+      for (auto& x : d) {
+        if (m.mode == PlanMode::Device) {
+          x.ready_val = epoch_;
+          x.done_val = epoch_;
+        }
+      }
+      msgs.push_back(std::move(d));
+    }
+    if (!msgs.empty()) tr_->launch_plan_pulls(c_, msgs, cur);
+    // 3. the stream continues once every receiver consumed this rank's data
+    WaitBatch wb;
+    std::memset(&wb, 0, sizeof(wb));
+    wb.timeout_ns = tr_->device_timeout_ns();
+    wb.status = c_->status_d;
+    for (auto& m : sends) {
+      if (m.mode != PlanMode::Device) continue;
+      if (wb.n == static_cast<std::uint32_t>(kMaxWaitFlags)) {
+        CMX_CUDA(launch_wait(wb, cur));
+        tr_->kernel_launches++;
+        wb.n = 0;
+      }
+      wb.flag[wb.n] = m.consumed_local;
+      wb.val[wb.n++] = epoch_;
+    }
+    if (wb.n) {
+      CMX_CUDA(launch_wait(wb, cur));
+      tr_->kernel_launches++;
+    }
+    if (!shared.empty()) {
+      for (auto& r : shared) eng_->wait(r, std::chrono::milliseconds(0));
+      tr_->stream_wait_all(shared);
+    }
+    std::string e = tr_->device_error();
+    if (!e.empty()) C10_THROW_ERROR(DistBackendError, e);
+  }
+
+  std::vector<std::pair<std::string, std::int64_t>> info() override {
+    std::int64_t loc = 0, dev = 0;
+    for (auto* v : {&sends, &recvs})
+      for (auto& m : *v) (m.mode == PlanMode::Local ? loc : dev) += m.mode != PlanMode::Shared;
+    return {{"local", loc}, {"device", dev}, {"shared", n_shared_}, {"starts", static_cast<std::int64_t>(epoch_)}};
+  }
+
+  std::int64_t n_shared_ = 0;
+
+ private:
+  CudaTransport* tr_;
+  Engine* eng_;
+  DevCtx* c_;
+  std::uint64_t epoch_ = 0;
+};
+
+void CudaTransport::launch_plan_pulls(DevCtx* c, const std::vector<std::vector<PullDesc>>& msgs,
+                                      cudaStream_t stream) {
+  std::uint32_t* counters = c->scratch(stream);
+  std::uint32_t first = c->take_slots(stream, static_cast<std::uint32_t>(msgs.size()));
+  PullBatch b;
+  std::memset(&b, 0, sizeof(b));
+  b.counters = counters;
+  b.status = c->status_d;
+  b.timeout_ns = timeout_ns_;
+  const int ctas = pull_ctas(c);
+  auto flush = [&]() {
+    if (b.n == 0) return;
+    CMX_CUDA(launch_pull(b, ctas, 256, stream));
+    kernel_launches++;
+    b.n = 0;
+    b.total_chunks = 0;
+  };
+  for (std::size_t i = 0; i < msgs.size(); ++i) {
+    std::uint32_t slot = (first + static_cast<std::uint32_t>(i)) % kCounterSlots;
+    std::uint32_t chunks = 0;
+    for (auto& d : msgs[i]) chunks += d.nchunks;
+    for (const auto& d0 : msgs[i]) {
+      if (b.n == static_cast<std::uint32_t>(kMaxBatch)) flush();
+      PullDesc d = d0;
+      d.chunk0 = b.total_chunks;
+      d.counter_idx = slot;
+      d.msg_chunks = chunks;
+      b.d[b.n++] = d;
+      b.total_chunks += d.nchunks;
+    }
+  }
+  flush();
+}
+
+std::vector<PullDesc> CudaTransport::plan_descs(const char* wire, std::size_t len, int src, bool local,
+                                                const at::Tensor& dst, DevCtx* c) {
+  auto r = std::make_shared<Request>();
+  r->kind = ReqKind::Recv;
+  r->device = true;
+  r->tensors = {dst};
+  r->total = static_cast<std::uint64_t>(dst.numel()) * dst.element_size();
+  auto rs = std::make_shared<RecvState>();
+  rs->device = c->dev;
+  r->dev = rs;
+  PendingPull pp;
+  pp.r = r;
+  pp.src = src;
+  pp.ctx = c;
+  build_descs(r, wire, len, local, pp);
+  TORCH_CHECK(rs->unpack.empty(), "commux plan: this receive layout needs a staged copy; persistent plans "
+              "take views whose strides merge to at most 4 dims on both sides");
+  return pp.descs;
+}
+
+DevicePlanPtr CudaTransport::create_plan(const std::vector<at::Tensor>& recv_t, const std::vector<int>& recv_peer,
+                                         const std::vector<int>& recv_tag, const std::vector<at::Tensor>& send_t,
+                                         const std::vector<int>& send_peer, const std::vector<int>& send_tag) {
+  TORCH_CHECK(!recv_t.empty() || !send_t.empty(), "commux plan: no messages");
+  const at::Tensor& any = recv_t.empty() ? send_t[0] : recv_t[0];
+  const int dev = any.device().index();
+  for (auto* v : {&recv_t, &send_t})
+    for (auto& t : *v)
+      TORCH_CHECK(t.is_cuda() && t.device().index() == dev, "commux plan: all tensors must be on one CUDA device");
+  DevCtx* c = ctx(dev);
+  publish_uuid(c);
+  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev));
+  const int me = eng_->rank();
+  auto plan = std::make_shared<CudaPlan>(this, eng_, c);
+
+  // wire description of one tensor (DrtsWire + one SegWire), as a send would
+  auto wire_of = [&](const at::Tensor& t, bool local, std::uint64_t consumed_slot) {
+    std::vector<std::int64_t> sz(t.sizes().begin(), t.sizes().end()), sd(t.strides().begin(), t.strides().end());
+    auto d = dims_of(sz.data(), sd.data(), t.dim());
+    std::vector<Dim> merged;
+    TORCH_CHECK(t.dim() <= kWireDims && refine(d, d, merged) && merged.size() <= static_cast<std::size_t>(kMaxPullDims),
+                "commux plan: send views must merge to at most 4 dims (send a contiguous tensor)");
+    std::vector<char> blob(sizeof(DrtsWire) + sizeof(SegWire), 0);
+    auto* w = reinterpret_cast<DrtsWire*>(blob.data());
+    w->magic = kWireMagic;
+    w->nseg = 1;
+    w->pid = static_cast<std::int32_t>(::getpid());
+    w->device = dev;
+    std::memcpy(w->uuid, c->uuid, 16);
+    w->mbox_id = c->mbox_id;
+    w->mbox_base = c->mbox_base;
+    w->mbox_handle = c->mbox_handle;
+    w->slot = consumed_slot;
+    auto* sw = reinterpret_cast<SegWire*>(blob.data() + sizeof(DrtsWire));
+    sw->elem = static_cast<std::uint32_t>(t.element_size());
+    sw->ndim = static_cast<std::int32_t>(t.dim());
+    for (int k = 0; k < t.dim(); ++k) {
+      sw->sizes[k] = t.size(k);
+      sw->strides[k] = t.stride(k);
+    }
+    if (t.numel() > 0) {
+      const char* p = static_cast<const char*>(t.data_ptr());
+      if (local) {
+        CUpointer_attribute attrs[2] = {CU_POINTER_ATTRIBUTE_RANGE_START_ADDR, CU_POINTER_ATTRIBUTE_RANGE_SIZE};
+        CUdeviceptr start = 0;
+        std::size_t asz = 0;
+        void* data[2] = {&start, &asz};
+        cu_check(cuPointerGetAttributes(2, attrs, data, reinterpret_cast<CUdeviceptr>(p)), "cuPointerGetAttributes");
+        sw->base = static_cast<std::uint64_t>(start);
+        sw->alloc_size = asz;
+      } else {
+        ipc_export(p, &sw->buffer_id, &sw->base, &sw->alloc_size, &sw->handle);
+      }
+      sw->offset = reinterpret_cast<std::uint64_t>(p) - sw->base;
+    }
+    return blob;
+  };
+  auto plan_slot = [&]() {
+    std::uint64_t s = kSlots + c->next_plan_slot.fetch_add(1);
+    TORCH_CHECK(s < 2 * kSlots, "commux plan: out of persistent flag slots");
+    return s;
+  };
+  auto bytes_tensor = [](const void* p, std::size_t n) {
+    at::Tensor t = at::empty({static_cast<std::int64_t>(n)}, at::TensorOptions().dtype(at::kByte));
+    std::memcpy(t.data_ptr(), p, n);
+    return t;
+  };
+  const std::size_t wire_len = sizeof(DrtsWire) + sizeof(SegWire);
+
+  std::vector<ReqPtr> pending_sends;
+  struct RecvSetup {
+    std::size_t idx;
+    ReqPtr req;
+    at::Tensor buf;
+  };
+  std::vector<RecvSetup> desc_recvs, reply_recvs;
+  // sends: descriptor to the receiver, then expect its reply
+  for (std::size_t i = 0; i < send_t.size(); ++i) {
+    CudaPlan::Msg m;
+    m.t = send_t[i];
+    m.peer = send_peer[i];
+    m.tag = send_tag[i];
+    TORCH_CHECK(m.peer >= 0 && m.peer < eng_->size(), "commux plan: invalid send peer ", m.peer);
+    if (m.peer == me) {
+      m.mode = PlanMode::Local;
+    } else {
+      std::uint64_t slot = plan_slot();
+      m.consumed_local = c->mbox + slot;
+      auto blob = wire_of(m.t, false, slot);
+      pending_sends.push_back(eng_->post_send({bytes_tensor(blob.data(), blob.size())}, m.peer,
+                                              make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), kPlanSub, true)));
+      at::Tensor rb = at::empty({static_cast<std::int64_t>(sizeof(PlanReply))}, at::TensorOptions().dtype(at::kByte));
+      reply_recvs.push_back({plan->sends.size(),
+                             eng_->post_recv({rb}, m.peer, make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), kPlanReplySub, true)),
+                             rb});
+    }
+    plan->sends.push_back(std::move(m));
+  }
+  // receives: expect the sender's descriptor
+  for (std::size_t j = 0; j < recv_t.size(); ++j) {
+    CudaPlan::Msg m;
+    m.t = recv_t[j];
+    m.peer = recv_peer[j];
+    m.tag = recv_tag[j];
+    TORCH_CHECK(m.peer >= 0 && m.peer < eng_->size(), "commux plan: invalid recv peer ", m.peer);
+    if (m.peer == me) {
+      m.mode = PlanMode::Local;
+    } else {
+      at::Tensor db = at::empty({static_cast<std::int64_t>(wire_len)}, at::TensorOptions().dtype(at::kByte));
+      desc_recvs.push_back({plan->recvs.size(),
+                            eng_->post_recv({db}, m.peer, make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), kPlanSub, true)),
+                            db});
+    }
+    plan->recvs.push_back(std::move(m));
+  }
+  // self messages pair up locally, FIFO per tag
+  for (auto& s : plan->sends) {
+    if (s.mode != PlanMode::Local) continue;
+    CudaPlan::Msg* r = nullptr;
+    for (auto& x : plan->recvs)
+      if (x.peer == me && !x.matched && x.tag == s.tag) {
+        r = &x;
+        break;
+      }
+    TORCH_CHECK(r != nullptr, "commux plan: self-send with tag ", s.tag, " has no matching self-receive");
+    r->matched = true;
+    auto blob = wire_of(s.t, true, 0);
+    r->descs = plan_descs(blob.data(), blob.size(), me, true, r->t, c);
+  }
+  for (auto& x : plan->recvs)
+    TORCH_CHECK(x.peer != me || x.matched, "commux plan: self-receive with tag ", x.tag, " has no matching self-send");
+  // remote receives: build the pull, allocate "ready", reply to the sender
+  for (auto& rs : desc_recvs) {
+    eng_->wait(rs.req, std::chrono::milliseconds(0));
+    CudaPlan::Msg& m = plan->recvs[rs.idx];
+    const char* blob = static_cast<const char*>(rs.buf.data_ptr());
+    auto* w = reinterpret_cast<const DrtsWire*>(blob);
+    TORCH_CHECK(w->magic == kWireMagic, "commux plan: malformed setup descriptor from rank ", m.peer);
+    const bool same_gpu = std::memcmp(w->uuid, c->uuid, 16) == 0;
+    PlanReply rep;
+    std::memset(&rep, 0, sizeof(rep));
+    rep.magic = kPlanMagic;
+    rep.pid = static_cast<std::int32_t>(::getpid());
+    std::memcpy(rep.uuid, c->uuid, 16);
+    rep.mbox_id = c->mbox_id;
+    rep.mbox_handle = c->mbox_handle;
+    if (same_gpu) {
+      m.mode = PlanMode::Shared;
+      plan->n_shared_++;
+    } else {
+      m.mode = PlanMode::Device;
+      std::uint64_t slot = plan_slot();
+      m.ready_local = c->mbox + slot;
+      rep.ready_slot = slot;
+      m.descs = plan_descs(blob, wire_len, m.peer, false, m.t, c);
+      for (auto& d : m.descs) d.ready = m.ready_local;
+    }
+    pending_sends.push_back(eng_->post_send({bytes_tensor(&rep, sizeof(rep))}, m.peer,
+                                            make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), kPlanReplySub, true)));
+  }
+  // remote sends: learn where to store "ready"
+  for (auto& rr : reply_recvs) {
+    eng_->wait(rr.req, std::chrono::milliseconds(0));
+    CudaPlan::Msg& m = plan->sends[rr.idx];
+    PlanReply rep;
+    std::memcpy(&rep, rr.buf.data_ptr(), sizeof(rep));
+    TORCH_CHECK(rep.magic == kPlanMagic, "commux plan: malformed setup reply from rank ", m.peer);
+    if (std::memcmp(rep.uuid, c->uuid, 16) == 0) {
+      m.mode = PlanMode::Shared;
+      plan->n_shared_++;
+    } else {
+      m.mode = PlanMode::Device;
+      auto* mb = static_cast<std::uint64_t*>(ipc_open(m.peer, rep.mbox_id, rep.mbox_handle, c));
+      m.ready_remote = mb + rep.ready_slot;
+    }
+  }
+  for (auto& s : pending_sends) eng_->wait(s, std::chrono::milliseconds(0));
+  return plan;
 }
 
 }  // namespace cuda

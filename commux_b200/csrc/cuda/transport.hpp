@@ -90,6 +90,7 @@ class DevCtx {
   std::uint64_t mbox_id = 0;
   std::uint64_t mbox_base = 0;
   std::atomic<std::uint64_t> next_value{0};
+  std::atomic<std::uint64_t> next_plan_slot{0};  // persistent-plan flags (second half of mbox)
   unsigned long long* status_h = nullptr;  // host-mapped error block (4 x u64)
   unsigned long long* status_d = nullptr;
 
@@ -166,6 +167,14 @@ class CudaTransport final : public DeviceTransport {
   DevCollPtr reduce_scatter(at::Tensor& out, const at::Tensor& in, RedOp op) override;
   DevCollPtr barrier() override;
   bool device_collectives(int dev) override;
+  DevicePlanPtr create_plan(const std::vector<at::Tensor>& recv_t, const std::vector<int>& recv_peer,
+                            const std::vector<int>& recv_tag, const std::vector<at::Tensor>& send_t,
+                            const std::vector<int>& send_peer, const std::vector<int>& send_tag) override;
+  // pull launch(es) of prebuilt per-message descriptors on `stream` (plans)
+  void launch_plan_pulls(DevCtx* c, const std::vector<std::vector<PullDesc>>& msgs, cudaStream_t stream);
+  // descriptors of one message from its wire description (plans)
+  std::vector<PullDesc> plan_descs(const char* wire, std::size_t len, int src, bool local,
+                                   const at::Tensor& dst, DevCtx* c);
   void stream_wait_all(const std::vector<ReqPtr>& rs) override;
 
   // shared with the collectives

@@ -290,6 +290,18 @@ class DevCollResult {
 };
 using DevCollPtr = std::shared_ptr<DevCollResult>;
 
+// A persistent set of tagged CUDA messages, matched once (the analogue of
+// MPI_Send_init/MPI_Recv_init + MPI_Startall). Every start() enqueues one
+// exchange of the same buffers on the caller's current stream: no host
+// matching, no host round trip, a few launches.
+class DevicePlan {
+ public:
+  virtual ~DevicePlan() = default;
+  virtual void start() = 0;
+  virtual std::vector<std::pair<std::string, std::int64_t>> info() = 0;
+};
+using DevicePlanPtr = std::shared_ptr<DevicePlan>;
+
 // Device transport interface, implemented by libcommux_cuda.so (loaded on the
 // first CUDA tensor; the host engine has no link-time CUDA dependency).
 class DeviceTransport {
@@ -348,6 +360,16 @@ class DeviceTransport {
   // the host collectives instead. The first call is collective (workspace
   // exchange): all ranks make it in the same order.
   virtual bool device_collectives(int dev) = 0;
+
+  // Persistent plan over the given receives and sends (matched by (peer,
+  // tag) in FIFO order, like the one-shot path). Collective among the ranks
+  // the plan talks to: each must create its side, in the same order.
+  virtual DevicePlanPtr create_plan(const std::vector<at::Tensor>& recv_t,
+                                    const std::vector<int>& recv_peer,
+                                    const std::vector<int>& recv_tag,
+                                    const std::vector<at::Tensor>& send_t,
+                                    const std::vector<int>& send_peer,
+                                    const std::vector<int>& send_tag) = 0;
 };
 
 using DeviceTransportFactory = DeviceTransport* (*)(Engine*);

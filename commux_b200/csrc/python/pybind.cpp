@@ -57,6 +57,25 @@ PYBIND11_MODULE(_C, m) {
     return d;
   });
   m.def("reset_stats", [](const c10::intrusive_ptr<c10d::Backend>& b) { as_commux(b)->reset_stats(); });
+  py::class_<commux::DevicePlan, std::shared_ptr<commux::DevicePlan>>(m, "P2PPlan")
+      .def("start", &commux::DevicePlan::start, py::call_guard<py::gil_scoped_release>(),
+           "Enqueue one exchange of the plan's buffers on the current CUDA stream.")
+      .def("info", [](commux::DevicePlan& p) {
+        py::dict d;
+        for (auto& kv : p.info()) d[py::str(kv.first)] = kv.second;
+        return d;
+      });
+  m.def(
+      "p2p_plan",
+      [](const c10::intrusive_ptr<c10d::Backend>& b, std::vector<at::Tensor> recv_tensors,
+         std::vector<int> recv_peers, std::vector<int> recv_tags, std::vector<at::Tensor> send_tensors,
+         std::vector<int> send_peers, std::vector<int> send_tags) {
+        py::gil_scoped_release nogil;
+        return as_commux(b)->p2p_plan(recv_tensors, recv_peers, recv_tags, send_tensors, send_peers,
+                                      send_tags);
+      },
+      py::arg("backend"), py::arg("recv_tensors"), py::arg("recv_peers"), py::arg("recv_tags"),
+      py::arg("send_tensors"), py::arg("send_peers"), py::arg("send_tags"));
   m.def(
       "_release_all", [] { commux::Engine::release_all(); }, py::call_guard<py::gil_scoped_release>(),
       "Release every backend's CUDA state (atexit hook; the CUDA context is still alive then).");

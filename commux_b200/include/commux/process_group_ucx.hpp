@@ -45,6 +45,7 @@ class Engine;       // host tag-matching engine (opaque)
 class CollEngine;   // collective algorithms (opaque)
 struct GroupWindow;  // coalescing-window state (opaque)
 struct Request;      // one message in flight (opaque)
+class DevicePlan;    // persistent CUDA message plan (opaque)
 
 class ProcessGroupUCX : public c10d::Backend {
  public:
@@ -135,6 +136,16 @@ class ProcessGroupUCX : public c10d::Backend {
   c10::intrusive_ptr<c10d::Work> batch_p2p(
       std::vector<at::Tensor>& recv_tensors, const std::vector<int>& recv_peers,
       const std::vector<int>& recv_tags, std::vector<at::Tensor>& send_tensors,
+      const std::vector<int>& send_peers, const std::vector<int>& send_tags);
+
+  // Persistent plan of CUDA receives and sends (matched once; the analogue of
+  // MPI_Send_init/MPI_Recv_init). plan->start() enqueues one exchange of the
+  // same buffers on the current stream with no host round trip. Every rank
+  // the plan talks to creates its side, in the same order, and starts it the
+  // same number of times.
+  std::shared_ptr<DevicePlan> p2p_plan(
+      const std::vector<at::Tensor>& recv_tensors, const std::vector<int>& recv_peers,
+      const std::vector<int>& recv_tags, const std::vector<at::Tensor>& send_tensors,
       const std::vector<int>& send_peers, const std::vector<int>& send_tags);
 
   void setTimeout(std::chrono::milliseconds timeout) override;

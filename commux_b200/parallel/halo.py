@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import itertools
 import math
+import os
 
 import torch
 import torch.distributed as dist
@@ -89,7 +90,8 @@ class HaloExchange:
         self.group = group
         self.directions = list(directions or DIRECTIONS)
         self._native = None
-        self._plans = {}  # views per field (the fields alternate between steps)
+        self._plans = {}  # views (+ persistent plan) per field; fields alternate
+        self.use_plans = os.environ.get("COMMUX_HALO_PLAN", "1") != "0"
         for n in self.n:
             if n < halo:
                 raise ValueError("interior must be at least as wide as the halo")
@@ -142,7 +144,15 @@ class HaloExchange:
                 sends.append((self.send_view(u, d), self.grid.neighbor(d), tag))
             if len(self._plans) >= 8:
                 self._plans.clear()
-            plan = self._plans[key] = (sends, recvs)
+            persistent = None
+            if u.is_cuda and self.use_plans:
+                # matched once; every later exchange of this field is three
+                # stream launches (collective: all ranks reach this together)
+                persistent = commux_b200.p2p_plan(sends=sends, recvs=recvs, group=self.group)
+            plan = self._plans[key] = (sends, recvs, persistent)
+        if plan[2] is not None:
+            plan[2].start()
+            return []
         return [commux_b200.batch_p2p(sends=plan[0], recvs=plan[1], group=self.group)]
 
     def exchange(self, u: torch.Tensor) -> None:

@@ -1,88 +1,113 @@
 """Sample GPU clocks and throttle reasons while a benchmark runs (read-only).
 
-Runs ``nvidia-smi --query-gpu=... -lms <interval>`` for the given GPUs in a
-subprocess and summarises the samples taken under load: median SM clock, the
-maximum SM clock and every throttle reason that was active. Nothing here
-changes a GPU setting.
+A background thread polls NVML every ``interval_ms`` (default 2 ms, so even a
+timed region of a few milliseconds gets samples) for the SM clock, the
+maximum SM clock, power, utilisation and the active clock-event reasons, and
+summarises the samples taken under load: median SM clock, maximum SM clock,
+and every throttle reason that was active. Nothing here changes a GPU
+setting; only query functions are called.
 """
 
 from __future__ import annotations
 
-import shutil
 import statistics
-import subprocess
-import tempfile
+import threading
+import time
 
-_FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,"
-           "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-           "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-_REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+_REASONS = {  # NVML clock-event reason bits
+    "sw_power_cap": 0x4,
+    "hw_slowdown": 0x8,
+    "sw_thermal_slowdown": 0x20,
+    "hw_thermal_slowdown": 0x40,
+    "hw_power_brake_slowdown": 0x80,
+}
 
 
 class ClockSampler:
-    def __init__(self, gpu_ids: list[str], interval_ms: int = 200, raw_path: str | None = None):
+    def __init__(self, gpu_ids: list[str], interval_ms: float = 2.0, raw_path: str | None = None):
         self.gpu_ids = gpu_ids
-        self.interval_ms = interval_ms
+        self.interval = interval_ms / 1e3
         self.raw_path = raw_path
-        self.proc = None
-        self.out = None
+        self._rows: list[tuple] = []
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+        self._handles = []
+        self.error = None
 
     def start(self) -> "ClockSampler":
-        exe = shutil.which("nvidia-smi")
-        if exe is None or not self.gpu_ids:
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            for g in self.gpu_ids:
+                if ":" in g:
+                    self._handles.append(pynvml.nvmlDeviceGetHandleByPciBusId(g))
+                else:
+                    self._handles.append(pynvml.nvmlDeviceGetHandleByIndex(int(g)))
+        except Exception as e:  # no NVML on this machine
+            self.error = str(e)
             return self
-        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-        cmd = [exe, f"--query-gpu={_FIELDS}", "--format=csv,noheader,nounits",
-               "-lms", str(self.interval_ms), "-i", ",".join(self.gpu_ids)]
-        self.proc = subprocess.Popen(cmd, stdout=self.out, stderr=subprocess.DEVNULL)
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
         return self
 
+    def _sample(self):
+        n = self._nvml
+        for h in self._handles:
+            try:
+                sm = n.nvmlDeviceGetClockInfo(h, n.NVML_CLOCK_SM)
+                smax = n.nvmlDeviceGetMaxClockInfo(h, n.NVML_CLOCK_SM)
+                util = n.nvmlDeviceGetUtilizationRates(h).gpu
+                try:
+                    reasons = n.nvmlDeviceGetCurrentClocksEventReasons(h)
+                except AttributeError:
+                    reasons = n.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                power = n.nvmlDeviceGetPowerUsage(h) / 1000.0
+                self._rows.append((time.time(), sm, smax, util, reasons, power))
+            except Exception as e:
+                self.error = str(e)
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self.interval)
+
     def stop(self) -> dict | None:
-        if self.proc is None:
+        if self._thread is None:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.out.flush()
-        self.out.seek(0)
-        text = self.out.read()
+        self._sample()  # at least one sample at the end of the region
+        self._stop.set()
+        self._thread.join(timeout=2)
         if self.raw_path:
             with open(self.raw_path, "w") as f:
-                f.write(text)
-        rows = [[c.strip() for c in r.split(",")] for r in text.strip().splitlines() if r.strip()]
-        return summarize(rows)
+                f.write("t,sm_mhz,sm_max_mhz,util,reasons_mask,power_w\n")
+                for r in self._rows:
+                    f.write(",".join(str(x) for x in r) + "\n")
+        return summarize(self._rows)
 
 
-def summarize(rows: list[list[str]]) -> dict | None:
-    samples, loaded, reasons, maxes = [], [], set(), []
-    for r in rows:
-        if len(r) < 10:
-            continue
-        try:
-            sm, smax, util = float(r[2]), float(r[3]), float(r[5])
-        except ValueError:
-            continue
-        samples.append(sm)
-        maxes.append(smax)
-        if util >= 50:
-            loaded.append(sm)
-        for name, val in zip(_REASONS, r[6:10]):
-            if val.strip().lower() == "active":
-                reasons.add(name)
-    if not samples:
+def summarize(rows) -> dict | None:
+    if not rows:
         return None
-    use = loaded or samples
-    return {"sm_mhz": statistics.median(use), "sm_max_mhz": max(maxes),
-            "reasons": sorted(reasons), "samples": len(samples), "samples_under_load": len(loaded)}
+    sms = [r[1] for r in rows]
+    loaded = [r[1] for r in rows if r[3] >= 50]
+    mask = 0
+    for r in rows:
+        mask |= int(r[4])
+    reasons = sorted(k for k, bit in _REASONS.items() if mask & bit)
+    return {"sm_mhz": statistics.median(loaded or sms), "sm_max_mhz": max(r[2] for r in rows),
+            "reasons": reasons, "samples": len(rows), "samples_under_load": len(loaded),
+            "power_w_max": round(max(r[5] for r in rows), 1)}
 
 
 def gpu_uuid(device_index: int) -> str | None:
-    """nvidia-smi id of a torch CUDA device: its PCI bus id (the CUDA UUID that
-    torch reports need not equal NVML's), else the index."""
+    """NVML id of a torch CUDA device: its PCI bus id (the CUDA UUID that torch
+    reports need not equal NVML's), else the index."""
     try:
         import torch
+
         p = torch.cuda.get_device_properties(device_index)
         return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
     except Exception:

@@ -76,3 +76,17 @@ def test_smoke_entry():
     r = subprocess.run([sys.executable, os.path.join(ROOT, "__graft_entry__.py")], capture_output=True,
                        text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+def test_plan_self():
+    check(run("gpu_plan.py", 1, env=CUDA))
+
+
+def test_plan_two_ranks():
+    # shared GPU: host-gated per start; one GPU per rank: device flags
+    check(run("gpu_plan.py", 2, env=CUDA, timeout=180))
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_halo_cuda_batch_path(world):
+    check(run("halo.py", world, env=dict(CUDA, COMMUX_HALO_PLAN="0", COMMUX_GROUP="1"), timeout=180))
