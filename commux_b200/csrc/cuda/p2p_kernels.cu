@@ -49,11 +49,13 @@ __device__ __forceinline__ void unit_offsets(const PullDesc& d, std::uint32_t u,
   dof += static_cast<std::int64_t>(rem) * d.dstr[0];
 }
 
+// One warp copies units [u0, u1): lane l takes u0 + l, u0 + l + 32, ...,
+// kUnroll loads in flight before the stores.
 template <int U>
 __device__ __forceinline__ void copy_units(const PullDesc& d, std::uint32_t u0, std::uint32_t u1) {
   using V = typename VecT<U>::T;
-  const std::uint32_t step = blockDim.x;
-  for (std::uint32_t base = u0 + threadIdx.x; base < u1; base += step * kUnroll) {
+  constexpr std::uint32_t step = 32;
+  for (std::uint32_t base = u0 + (threadIdx.x & 31u); base < u1; base += step * kUnroll) {
     V v[kUnroll];
     std::int64_t dofs[kUnroll];
 #pragma unroll
@@ -93,8 +95,14 @@ __device__ __forceinline__ bool wait_ready(const PullDesc& d, const PullBatch& b
   return true;
 }
 
+// Each chunk is split into one contiguous slice per warp; every warp counts
+// its own slice into the message's counter (target: chunks x warps), so the
+// CTA needs no barrier except where a plan's ready flag must be awaited.
 __global__ void __launch_bounds__(kThreads, 4) pull_kernel(const __grid_constant__ PullBatch b) {
   __shared__ int skip;
+  constexpr std::uint32_t kWarps = kThreads / 32;
+  constexpr std::uint32_t kFailBit = 0x80000000u;
+  const std::uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   for (std::uint32_t c = blockIdx.x; c < b.total_chunks; c += gridDim.x) {
     std::uint32_t di = 0;
     while (di + 1 < b.n && c >= b.d[di + 1].chunk0) ++di;
@@ -105,34 +113,36 @@ __global__ void __launch_bounds__(kThreads, 4) pull_kernel(const __grid_constant
       if (threadIdx.x == 0) skip = wait_ready(d, b) ? 0 : 1;
       __syncthreads();
       failed = skip != 0;
+      __syncthreads();  // every thread read `skip` before it is rewritten
     }
     // a failed wait copies nothing but still counts, so the scratch counter
     // returns to zero; the message's completion flag is then not stored
-    const std::uint32_t u1 = failed ? u0 : min(u0 + kChunkUnits, d.units);
+    const std::uint32_t end = failed ? u0 : min(u0 + kChunkUnits, d.units);
+    const std::uint32_t per = (end - u0 + kWarps - 1) / kWarps;
+    const std::uint32_t wlo = min(end, u0 + warp * per), whi = min(end, wlo + per);
     switch (d.unit) {
       case 16:
-        copy_units<16>(d, u0, u1);
+        copy_units<16>(d, wlo, whi);
         break;
       case 8:
-        copy_units<8>(d, u0, u1);
+        copy_units<8>(d, wlo, whi);
         break;
       case 4:
-        copy_units<4>(d, u0, u1);
+        copy_units<4>(d, wlo, whi);
         break;
       case 2:
-        copy_units<2>(d, u0, u1);
+        copy_units<2>(d, wlo, whi);
         break;
       default:
-        copy_units<1>(d, u0, u1);
+        copy_units<1>(d, wlo, whi);
         break;
     }
-    __syncthreads();  // every load of this chunk has returned
-    if (threadIdx.x == 0) {
+    __syncwarp();  // every load of this warp's slice has returned
+    if (lane == 0) {
       __threadfence();
-      constexpr std::uint32_t kFailBit = 0x80000000u;
       if (failed) atomicOr(&b.counters[d.counter_idx], kFailBit);
       std::uint32_t prev = atomicAdd(&b.counters[d.counter_idx], 1u);
-      if ((prev & ~kFailBit) + 1 == d.msg_chunks) {
+      if ((prev & ~kFailBit) + 1 == d.msg_chunks * kWarps) {
         const bool any_failed = failed || (prev & kFailBit) != 0u;
         b.counters[d.counter_idx] = 0u;
         if (d.done != nullptr && !any_failed) {
@@ -141,7 +151,6 @@ __global__ void __launch_bounds__(kThreads, 4) pull_kernel(const __grid_constant
         }
       }
     }
-    __syncthreads();
   }
 }
 

@@ -159,6 +159,9 @@ void emit_descs(const char* sp, char* dp, std::vector<Dim> dims, std::int64_t el
     in.size = inner_bytes / unit;
     in.ss = unit;
     in.ds = unit;
+    // a row of exactly one unit (e.g. a 16-byte x-face row): the row dim
+    // adds nothing but a division per unit
+    if (in.size == 1 && dims.size() > 1) dims.pop_back();
   } else if (!(elem == 1 || elem == 2 || elem == 4 || elem == 8 || elem == 16)) {
     throw std::runtime_error("commux: unsupported element size for a strided device copy");
   }
@@ -1379,7 +1382,7 @@ DevicePlanPtr CudaTransport::create_plan(const std::vector<at::Tensor>& recv_t, 
   }
   // self messages pair up locally, FIFO per tag
   for (auto& s : plan->sends) {
-    if (s.mode != PlanMode::Local) continue;
+    if (s.peer != me) continue;
     CudaPlan::Msg* r = nullptr;
     for (auto& x : plan->recvs)
       if (x.peer == me && !x.matched && x.tag == s.tag) {
