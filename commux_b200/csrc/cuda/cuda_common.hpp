@@ -55,6 +55,7 @@ struct PullDesc {
   std::uint32_t nchunks;            // chunks of this descriptor
   std::uint32_t msg_chunks;         // chunks of its whole message
   std::uint32_t counter_idx;        // per-message completion counter (scratch)
+  std::uint32_t wide;               // 1: some |stride| >= 2^31 bytes (64-bit walk)
   std::uint64_t* done;              // flag to set once copied (may be remote)
   std::uint64_t done_val;
   // persistent plans: the copy may start once *ready >= ready_val (a flag in
@@ -98,7 +99,10 @@ enum : unsigned long long {
 };
 
 // Launchers (p2p_kernels.cu).
-cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStream_t s);
+// Launches the pull kernel(s) for a batch; adds the number of launches to
+// *launches when given (one per unit class present in the batch).
+cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStream_t s,
+                        int* launches = nullptr);
 cudaError_t launch_wait(const WaitBatch& b, cudaStream_t s);
 cudaError_t launch_signal(std::uint64_t* flag, std::uint64_t val, cudaStream_t s);
 cudaError_t launch_signal_many(const SignalBatch& b, cudaStream_t s);

@@ -45,6 +45,10 @@ __device__ __forceinline__ void fence_acq_rel_sys() {
   asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
 __device__ __forceinline__ std::uint64_t globaltimer_ns() {
   std::uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

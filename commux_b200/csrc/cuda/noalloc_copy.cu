@@ -27,12 +27,17 @@ constexpr int kNoAllocMaxDevices = 64;
 constexpr std::int64_t kNoAllocUnitsPerDesc = std::int64_t{1} << 30;
 constexpr std::int64_t kNoAllocMaxExtent = std::int64_t{1} << 40;  // sizes and strides, elements
 constexpr std::size_t kNoAllocCounterBytes = kNoAllocDescs * sizeof(std::uint32_t);
-constexpr std::size_t kNoAllocBytes = 1024;    // counters, then the 32-byte status word
-static_assert(kNoAllocCounterBytes + 32 <= kNoAllocBytes, "scratch layout");
+constexpr std::size_t kNoAllocDoneOffset = 512;  // u64 completion flags, one per descriptor
+constexpr std::size_t kNoAllocBytes = 1024;
+static_assert(kNoAllocCounterBytes + 32 <= kNoAllocDoneOffset, "scratch layout");
+static_assert(kNoAllocDoneOffset + kNoAllocDescs * sizeof(std::uint64_t) <= kNoAllocBytes, "scratch layout");
 static_assert(kNoAllocDescs <= kMaxBatch, "one launch holds every descriptor");
 
-// The scratch: [0, 256) counters (u32 x 64), [256, 288) the kernel's status
-// word (only written by ready-flag waits, which this path never has).
+// The scratch: [0, 256) the per-descriptor counters the kernel's warps count
+// their slices into (u32 x 64), [256, 288) the kernel's status word (only
+// written by ready-flag waits, which this path never has), [512, 1024) the
+// per-descriptor completion flags the last warp of a descriptor stores
+// (u64 x 64). All of it is zeroed on the caller's stream before each launch.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
 struct DevSetup {
@@ -249,17 +254,23 @@ extern "C" int commux_strided_copy_noalloc(void* dst, const int64_t* dst_strides
       units *= sz;
     }
     x.units = static_cast<std::uint32_t>(units);
+    for (int k = 0; k < kMaxPullDims; ++k) {
+      constexpr std::int64_t lim = std::int64_t{1} << 31;
+      if (x.sst[k] >= lim || x.sst[k] <= -lim || x.dstr[k] >= lim || x.dstr[k] <= -lim) x.wide = 1;
+    }
     x.nchunks = static_cast<std::uint32_t>((units + kChunkUnits - 1) / kChunkUnits);
     x.chunk0 = chunks;
     x.msg_chunks = x.nchunks;
     x.counter_idx = static_cast<std::uint32_t>(i);
+    x.done = reinterpret_cast<std::uint64_t*>(su.scratch + kNoAllocDoneOffset) + i;
+    x.done_val = 1;
     chunks += x.nchunks;
     b.n = static_cast<std::uint32_t>(i + 1);
   }
   b.total_chunks = chunks;
 
   auto s = static_cast<cudaStream_t>(stream);
-  e = cudaMemsetAsync(su.scratch, 0, kNoAllocBytes, s);  // counters must start at zero
+  e = cudaMemsetAsync(su.scratch, 0, kNoAllocBytes, s);  // counters and flags start at zero
   if (e != cudaSuccess)
     return fail(err, err_len, CMX_NOALLOC_ECUDA, "commux_strided_copy_noalloc: cudaMemsetAsync: %s",
                 cudaGetErrorString(e));

@@ -10,11 +10,11 @@
 // a host stream sync (reference: src/process_group_ucx.cpp:581-591, :490).
 //
 // Work split: each descriptor is cut into chunks of kChunkUnits units; CTAs
-// stride over the global chunk list. The CTA that finishes the last chunk of
-// a descriptor stores the descriptor's completion flag with release
-// semantics at system scope (the sender polls it from its own stream), after
-// which it zeroes the descriptor's counter so the scratch is clean for the
-// next launch on that stream.
+// stride over the global chunk list. The warp that finishes the last slice of
+// a message stores the message's completion flag with release semantics at
+// system scope (the sender polls it from its own stream), after which it
+// zeroes the message's counter so the scratch is clean for the next launch on
+// that stream.
 
 #include "cuda_common.hpp"
 #include "device_utils.cuh"
@@ -27,50 +27,109 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;
 
+// Byte offsets of unit u in the source and destination (dims outermost
+// first, divisors in d.div, sizes of unused outer dims 1). S is the stride
+// type: 32-bit when every stride of the descriptor fits (d.wide == 0), which
+// keeps the unrolled copy loop inside 64 registers; 64-bit otherwise.
+template <typename S>
 __device__ __forceinline__ void unit_offsets(const PullDesc& d, std::uint32_t u, std::int64_t& so,
                                              std::int64_t& dof) {
-  if (d.ndim == 1) {
-    so = static_cast<std::int64_t>(u) * d.sst[kMaxPullDims - 1];
-    dof = static_cast<std::int64_t>(u) * d.dstr[kMaxPullDims - 1];
-    return;
-  }
   so = 0;
   dof = 0;
   std::uint32_t rem = u;
 #pragma unroll
   for (int i = kMaxPullDims - 1; i >= 1; --i) {
-    std::uint32_t q = d.div[i].div(rem);
-    std::uint32_t r = rem - q * d.div[i].d;
-    so += static_cast<std::int64_t>(r) * d.sst[i];
-    dof += static_cast<std::int64_t>(r) * d.dstr[i];
+    const std::uint32_t q = d.div[i].div(rem);
+    const std::uint32_t r = rem - q * d.div[i].d;
+    so += static_cast<std::int64_t>(r) * static_cast<S>(d.sst[i]);
+    dof += static_cast<std::int64_t>(r) * static_cast<S>(d.dstr[i]);
     rem = q;
   }
-  so += static_cast<std::int64_t>(rem) * d.sst[0];
-  dof += static_cast<std::int64_t>(rem) * d.dstr[0];
+  so += static_cast<std::int64_t>(rem) * static_cast<S>(d.sst[0]);
+  dof += static_cast<std::int64_t>(rem) * static_cast<S>(d.dstr[0]);
 }
 
 // One warp copies units [u0, u1): lane l takes u0 + l, u0 + l + 32, ...,
-// kUnroll loads in flight before the stores.
+// kUnroll loads in flight before the stores. A unit is (row, column) of the
+// innermost dim; a lane re-derives the row's offsets over the outer dims only
+// when its row changes, so most units cost one division.
 template <int U>
 __device__ __forceinline__ void copy_units(const PullDesc& d, std::uint32_t u0, std::uint32_t u1) {
   using V = typename VecT<U>::T;
   constexpr std::uint32_t step = 32;
+  constexpr int in = kMaxPullDims - 1;
+  const char* __restrict__ src = d.src;
+  char* __restrict__ dst = d.dst;
+  const std::int32_t css = static_cast<std::int32_t>(d.sst[in]);
+  const std::int32_t cds = static_cast<std::int32_t>(d.dstr[in]);
+  std::uint32_t crow = 0xffffffffu;
+  std::int64_t rso = 0, rdo = 0;
   for (std::uint32_t base = u0 + (threadIdx.x & 31u); base < u1; base += step * kUnroll) {
     V v[kUnroll];
     std::int64_t dofs[kUnroll];
 #pragma unroll
     for (int k = 0; k < kUnroll; ++k) {
-      std::uint32_t u = base + k * step;
+      const std::uint32_t u = base + k * step;
       if (u < u1) {
-        std::int64_t so;
-        unit_offsets(d, u, so, dofs[k]);
-        v[k] = *reinterpret_cast<const V*>(d.src + so);
+        const std::uint32_t row = d.div[in].div(u);
+        const std::uint32_t col = u - row * d.div[in].d;
+        if (row != crow) {
+          crow = row;
+          std::uint32_t rem = row;
+          rso = 0;
+          rdo = 0;
+#pragma unroll
+          for (int i = in - 1; i >= 1; --i) {
+            const std::uint32_t q = d.div[i].div(rem);
+            const std::uint32_t r = rem - q * d.div[i].d;
+            rso += static_cast<std::int64_t>(r) * static_cast<std::int32_t>(d.sst[i]);
+            rdo += static_cast<std::int64_t>(r) * static_cast<std::int32_t>(d.dstr[i]);
+            rem = q;
+          }
+          rso += static_cast<std::int64_t>(rem) * static_cast<std::int32_t>(d.sst[0]);
+          rdo += static_cast<std::int64_t>(rem) * static_cast<std::int32_t>(d.dstr[0]);
+        }
+        dofs[k] = rdo + static_cast<std::int64_t>(col) * cds;
+        v[k] = *reinterpret_cast<const V*>(src + rso + static_cast<std::int64_t>(col) * css);
       }
     }
 #pragma unroll
     for (int k = 0; k < kUnroll; ++k) {
-      std::uint32_t u = base + k * step;
-      if (u < u1) *reinterpret_cast<V*>(d.dst + dofs[k]) = v[k];
+      const std::uint32_t u = base + k * step;
+      if (u < u1) *reinterpret_cast<V*>(dst + dofs[k]) = v[k];
+    }
+  }
+}
+
+template <int U>
+__device__ __forceinline__ void copy_one(const char* s, char* d) {
+  using V = typename VecT<U>::T;
+  *reinterpret_cast<V*>(d) = *reinterpret_cast<const V*>(s);
+}
+
+// Descriptors with a stride of 2 GiB or more: one unit at a time, 64-bit
+// strides (layouts this wide are rare; kept out of line so the common loop
+// keeps its registers).
+__device__ __noinline__ void copy_units_wide(const PullDesc& d, std::uint32_t u0, std::uint32_t u1) {
+  for (std::uint32_t u = u0 + (threadIdx.x & 31u); u < u1; u += 32) {
+    std::int64_t so, dof;
+    unit_offsets<std::int64_t>(d, u, so, dof);
+    switch (d.unit) {
+      case 16:
+        copy_one<16>(d.src + so, d.dst + dof);
+        break;
+      case 8:
+        copy_one<8>(d.src + so, d.dst + dof);
+        break;
+      case 4:
+        copy_one<4>(d.src + so, d.dst + dof);
+        break;
+      case 2:
+        copy_one<2>(d.src + so, d.dst + dof);
+        break;
+      default:
+        copy_one<1>(d.src + so, d.dst + dof);
+        break;
     }
   }
 }
@@ -95,18 +154,37 @@ __device__ __forceinline__ bool wait_ready(const PullDesc& d, const PullBatch& b
   return true;
 }
 
+// Descriptor owning global chunk c: the last one whose chunk0 <= c (binary
+// search; descriptors are sorted by chunk0 and d[0].chunk0 == 0).
+__device__ __forceinline__ std::uint32_t find_desc(const PullBatch& b, std::uint32_t c) {
+  std::uint32_t lo = 0, hi = b.n;  // answer in [lo, hi)
+  while (hi - lo > 1) {
+    const std::uint32_t mid = (lo + hi) >> 1;
+    if (b.d[mid].chunk0 <= c)
+      lo = mid;
+    else
+      hi = mid;
+  }
+  return lo;
+}
+
 // Each chunk is split into one contiguous slice per warp; every warp counts
 // its own slice into the message's counter (target: chunks x warps), so the
 // CTA needs no barrier except where a plan's ready flag must be awaited.
+// Messages without a completion flag (copies ordered by the stream alone)
+// skip the counting and its fence.
+//
+// One instantiation per unit size U (U == 0: the 64-bit-stride walk for wide
+// layouts): a single kernel holding every unit's copy loop needs more than
+// 80 registers, one loop alone fits the 64 that four CTAs per SM allow.
+template <int U>
 __global__ void __launch_bounds__(kThreads, 4) pull_kernel(const __grid_constant__ PullBatch b) {
   __shared__ int skip;
   constexpr std::uint32_t kWarps = kThreads / 32;
   constexpr std::uint32_t kFailBit = 0x80000000u;
   const std::uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   for (std::uint32_t c = blockIdx.x; c < b.total_chunks; c += gridDim.x) {
-    std::uint32_t di = 0;
-    while (di + 1 < b.n && c >= b.d[di + 1].chunk0) ++di;
-    const PullDesc& d = b.d[di];
+    const PullDesc& d = b.d[find_desc(b, c)];
     const std::uint32_t u0 = (c - d.chunk0) * kChunkUnits;
     bool failed = false;
     if (d.ready != nullptr) {  // persistent plan: wait for the sender's data
@@ -120,26 +198,14 @@ __global__ void __launch_bounds__(kThreads, 4) pull_kernel(const __grid_constant
     const std::uint32_t end = failed ? u0 : min(u0 + kChunkUnits, d.units);
     const std::uint32_t per = (end - u0 + kWarps - 1) / kWarps;
     const std::uint32_t wlo = min(end, u0 + warp * per), whi = min(end, wlo + per);
-    switch (d.unit) {
-      case 16:
-        copy_units<16>(d, wlo, whi);
-        break;
-      case 8:
-        copy_units<8>(d, wlo, whi);
-        break;
-      case 4:
-        copy_units<4>(d, wlo, whi);
-        break;
-      case 2:
-        copy_units<2>(d, wlo, whi);
-        break;
-      default:
-        copy_units<1>(d, wlo, whi);
-        break;
-    }
+    if constexpr (U == 0)
+      copy_units_wide(d, wlo, whi);
+    else
+      copy_units<U>(d, wlo, whi);
+    if (d.done == nullptr) continue;
     __syncwarp();  // every load of this warp's slice has returned
     if (lane == 0) {
-      __threadfence();
+      fence_acq_rel_gpu();  // with the relaxed add below: a release of the slice
       if (failed) atomicOr(&b.counters[d.counter_idx], kFailBit);
       std::uint32_t prev = atomicAdd(&b.counters[d.counter_idx], 1u);
       if ((prev & ~kFailBit) + 1 == d.msg_chunks * kWarps) {
@@ -187,12 +253,71 @@ __global__ void signal_kernel(std::uint64_t* flag, std::uint64_t val) {
 
 }  // namespace
 
-cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStream_t s) {
-  if (b.n == 0 || b.total_chunks == 0) return cudaSuccess;
-  int grid = static_cast<int>(b.total_chunks < static_cast<std::uint32_t>(max_ctas) ? b.total_chunks : max_ctas);
-  (void)threads;
-  pull_kernel<<<grid, kThreads, 0, s>>>(b);
+namespace {
+
+int unit_class(const PullDesc& d) { return d.wide ? 0 : static_cast<int>(d.unit); }
+
+cudaError_t launch_class(int cls, const PullBatch& b, int max_ctas, cudaStream_t s) {
+  const int grid =
+      static_cast<int>(b.total_chunks < static_cast<std::uint32_t>(max_ctas) ? b.total_chunks : max_ctas);
+  switch (cls) {
+    case 16:
+      pull_kernel<16><<<grid, kThreads, 0, s>>>(b);
+      break;
+    case 8:
+      pull_kernel<8><<<grid, kThreads, 0, s>>>(b);
+      break;
+    case 4:
+      pull_kernel<4><<<grid, kThreads, 0, s>>>(b);
+      break;
+    case 2:
+      pull_kernel<2><<<grid, kThreads, 0, s>>>(b);
+      break;
+    case 1:
+      pull_kernel<1><<<grid, kThreads, 0, s>>>(b);
+      break;
+    default:
+      pull_kernel<0><<<grid, kThreads, 0, s>>>(b);
+      break;
+  }
   return cudaGetLastError();
+}
+
+}  // namespace
+
+// A batch whose descriptors share one unit class is one launch; a mixed batch
+// becomes one launch per class, in order on the stream (completion counters
+// count warps across all of them, so a message may span launches).
+cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStream_t s, int* launches) {
+  (void)threads;
+  if (b.n == 0 || b.total_chunks == 0) return cudaSuccess;
+  const int first = unit_class(b.d[0]);
+  bool same = true;
+  for (std::uint32_t i = 1; same && i < b.n; ++i) same = unit_class(b.d[i]) == first;
+  if (same) {
+    if (launches != nullptr) ++*launches;
+    return launch_class(first, b, max_ctas, s);
+  }
+  static thread_local PullBatch sub;  // 25 KB: off the stack, reused
+  sub.counters = b.counters;
+  sub.status = b.status;
+  sub.timeout_ns = b.timeout_ns;
+  for (int cls : {16, 8, 4, 2, 1, 0}) {
+    sub.n = 0;
+    sub.total_chunks = 0;
+    for (std::uint32_t i = 0; i < b.n; ++i) {
+      if (unit_class(b.d[i]) != cls) continue;
+      PullDesc x = b.d[i];
+      x.chunk0 = sub.total_chunks;
+      sub.total_chunks += x.nchunks;
+      sub.d[sub.n++] = x;
+    }
+    if (sub.n == 0 || sub.total_chunks == 0) continue;
+    if (launches != nullptr) ++*launches;
+    cudaError_t e = launch_class(cls, sub, max_ctas, s);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 cudaError_t launch_wait(const WaitBatch& b, cudaStream_t s) {

@@ -197,6 +197,10 @@ void emit_descs(const char* sp, char* dp, std::vector<Dim> dims, std::int64_t el
     }
     d.units = static_cast<std::uint32_t>(units);
     d.nchunks = static_cast<std::uint32_t>(std::max<std::int64_t>(1, (units + kChunkUnits - 1) / kChunkUnits));
+    // the kernel's common walk holds strides in 32 bits
+    constexpr std::int64_t lim = std::int64_t{1} << 31;
+    for (int k = 0; k < kMaxPullDims; ++k)
+      if (d.sst[k] >= lim || d.sst[k] <= -lim || d.dstr[k] >= lim || d.dstr[k] <= -lim) d.wide = 1;
     out.push_back(d);
   }
 }
@@ -814,8 +818,9 @@ void CudaTransport::launch_batch(DevCtx* c, std::vector<PendingPull>& pulls, cud
   const int ctas = pull_ctas(c);
   auto flush = [&]() {
     if (b.n == 0) return;
-    CMX_CUDA(launch_pull(b, ctas, 256, stream));
-    kernel_launches++;
+    int launched = 0;
+    CMX_CUDA(launch_pull(b, ctas, 256, stream, &launched));
+    kernel_launches += launched;
     b.n = 0;
     b.total_chunks = 0;
   };
@@ -1223,8 +1228,9 @@ void CudaTransport::launch_plan_pulls(DevCtx* c, const std::vector<std::vector<P
   const int ctas = pull_ctas(c);
   auto flush = [&]() {
     if (b.n == 0) return;
-    CMX_CUDA(launch_pull(b, ctas, 256, stream));
-    kernel_launches++;
+    int launched = 0;
+    CMX_CUDA(launch_pull(b, ctas, 256, stream, &launched));
+    kernel_launches += launched;
     b.n = 0;
     b.total_chunks = 0;
   };

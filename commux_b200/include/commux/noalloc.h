@@ -20,8 +20,8 @@
  * The copy runs the same pull kernel that moves tagged p2p messages (a
  * strided gather from `src` and a strided scatter into `dst` in one pass,
  * vectorised up to 16 bytes). The only scratch the kernel needs, its
- * per-descriptor completion counters, lives in a file-scope device array of
- * 1 KiB per GPU that is compiled into the library, so the call performs no
+ * per-descriptor completion counters and flags, lives in a file-scope device
+ * array of 1 KiB per GPU that is compiled into the library, so the call performs no
  * cudaMalloc, cudaFree or other allocating CUDA or PyTorch routine, and no
  * host heap allocation either.
  *
@@ -33,8 +33,8 @@
  *     device, and must not overlap; the call checks the first, not the second;
  *   - asynchronous on `stream` (a cudaStream_t, NULL = the legacy default
  *     stream), which must belong to the current device;
- *   - before its kernel, each call clears the counters on `stream` with a
- *     cudaMemsetAsync (they must start at zero).
+ *   - before its kernel, each call clears the counters and flags on `stream`
+ *     with a cudaMemsetAsync (they must start at zero).
  *
  * Limits (oversize inputs are rejected with CMX_NOALLOC_ETOOBIG and a message,
  * before any memory is touched):

@@ -55,6 +55,18 @@ for w in reqs:
 torch.cuda.synchronize()
 for name, rv, want in checks:
     c.equal(name, rv.cpu(), want)
+# a layout with a 2 GiB stride (the kernel's 64-bit walk): rows of a 4 GiB field
+big = torch.zeros((2, 1 << 28), dtype=torch.float64, device=dev)
+big[:, 3:1003] = torch.arange(2000, dtype=torch.float64, device=dev).view(2, 1000) + 10000 * rank
+wide_out = torch.zeros((2, 1000), dtype=torch.float64, device=dev)
+rr = dist.irecv(wide_out, src, tag=40)
+ss = dist.isend(big[:, 3:1003], peer, tag=40)
+rr.wait()
+ss.wait()
+torch.cuda.synchronize()
+c.equal("wide stride", wide_out.cpu(), torch.arange(2000, dtype=torch.float64).view(2, 1000) + 10000 * src)
+del big
+torch.cuda.empty_cache()
 # repeated exchange into the same buffers (IPC caches, slot reuse)
 x = torch.arange(4096, dtype=torch.float32, device=dev)
 y = torch.zeros_like(x)
