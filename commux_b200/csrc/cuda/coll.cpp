@@ -6,6 +6,7 @@
 #include <c10/cuda/CUDAStream.h>
 #include <unistd.h>
 
+#include <cstdio>
 #include <cstring>
 
 namespace commux {
@@ -46,6 +47,7 @@ int op_code(RedOp op) { return static_cast<int>(op); }
 
 struct ExchangeRecord {
   std::int32_t pid;
+  std::int32_t nvls_ok;  // this rank can and may join an NVLS group
   unsigned char uuid[16];
   cudaIpcMemHandle_t handle;
 };
@@ -98,6 +100,7 @@ CollImpl::CollImpl(CudaTransport* tr, int dev)
   ExchangeRecord mine;
   std::memset(&mine, 0, sizeof(mine));
   mine.pid = static_cast<std::int32_t>(::getpid());
+  mine.nvls_ok = env_int("COMMUX_NVLS", 1) != 0 && NvlsBuffer::device_supported(dev) ? 1 : 0;
   std::memcpy(mine.uuid, ctx_->uuid, 16);
   CMX_CUDA(cudaIpcGetMemHandle(&mine.handle, ws_));
   const std::string key = eng_->store_prefix() + "cws/";
@@ -129,11 +132,26 @@ CollImpl::CollImpl(CudaTransport* tr, int dev)
     flags_[p] = reinterpret_cast<std::uint64_t*>(base);
     data_[p] = base + kFlagBytes;
   }
+  // NVLS: every rank on its own GPU and able to join (the same records on
+  // every rank, so the decision and the collective set-up are shared)
+  bool nvls = P_ >= 2;
+  for (int p = 0; p < P_; ++p) nvls = nvls && recs[p].nvls_ok != 0;
+  nvls_min_bytes_ = env_int("COMMUX_NVLS_MIN_BYTES", 1ll << 20);
+  if (nvls) {
+    const std::int64_t bytes = std::max<std::int64_t>(env_int("COMMUX_NVLS_BYTES", 2 * region_bytes_), 4 << 20);
+    nvls_ = NvlsBuffer::create(eng_, dev, static_cast<std::size_t>(bytes), &nvls_why_);
+    if (!nvls_ && me_ == 0)
+      std::fprintf(stderr, "commux: NVLS collectives unavailable (%s); using peer-to-peer kernels\n",
+                   nvls_why_.c_str());
+  } else {
+    nvls_why_ = P_ < 2 ? "one rank" : "COMMUX_NVLS=0 or no multicast support on some rank";
+  }
 }
 
 CollImpl::~CollImpl() {
   if (!select_device_quiet(dev_)) return;  // context gone at process exit
   if (stream_) cudaStreamSynchronize(stream_);
+  nvls_.reset();
   for (int p = 0; p < P_; ++p)
     if (p != me_ && flags_[p]) cudaIpcCloseMemHandle(flags_[p]);
   if (ws_) cudaFree(ws_);
@@ -175,6 +193,12 @@ void CollImpl::fill(CollArgs& a, const Launch& l, const at::Tensor& in, const at
   a.seq_base = epoch_ << 20;
   a.timeout_ns = tr_->device_timeout_ns();
   a.status = ctx_->status_d;
+  if (nvls_) {
+    a.nvls_uc = nvls_->uc();
+    a.nvls_mc = nvls_->mc();
+    a.nvls_bytes = static_cast<std::int64_t>(nvls_->size());
+    a.nvls_half_off = (epoch_ & 1) ? a.nvls_bytes / 2 : 0;
+  }
 }
 
 DevCollPtr CollImpl::run(const std::vector<Launch>& launches) {
@@ -209,6 +233,8 @@ DevCollPtr CollImpl::run(const std::vector<Launch>& launches) {
     if ((l.mode == kModeAllreduce || l.mode == kModeReduce) && bytes <= oneshot_bytes_ &&
         l.n * a.elem_bytes * P_ <= region_bytes_ / 2)
       algo = kAlgoOneShot;
+    else if (nvls_ && l.mode == kModeAllreduce && bytes >= nvls_min_bytes_ && nvls_supported(a.dtype, a.op))
+      algo = kAlgoNvls;
     a.algo = algo;
     int ctas = choose_ctas(l.mode, algo, bytes);
     CMX_CUDA(launch_coll(a, ctas, stream_));
@@ -219,6 +245,8 @@ DevCollPtr CollImpl::run(const std::vector<Launch>& launches) {
       st_gather_++;
     else if (algo == kAlgoOneShot)
       st_oneshot_++;
+    else if (algo == kAlgoNvls)
+      st_nvls_++;
     else
       st_twoshot_++;
   }
@@ -271,7 +299,8 @@ DevCollPtr CollImpl::reduce_scatter(at::Tensor& out, const at::Tensor& in, RedOp
 
 std::vector<std::pair<std::string, std::int64_t>> CollImpl::stats() const {
   return {{"coll_calls", st_calls_},   {"coll_oneshot", st_oneshot_}, {"coll_twoshot", st_twoshot_},
-          {"coll_gather", st_gather_}, {"coll_bytes", st_bytes_},     {"coll_shared_gpu", shared_gpu_ ? 1 : 0}};
+          {"coll_gather", st_gather_}, {"coll_bytes", st_bytes_},     {"coll_shared_gpu", shared_gpu_ ? 1 : 0},
+          {"coll_nvls", st_nvls_},     {"coll_nvls_enabled", nvls_ ? 1 : 0}};
 }
 
 // ---------------------------------------------------------------------------

@@ -11,6 +11,7 @@
 #include <vector>
 
 #include "coll_args.hpp"
+#include "nvls.hpp"
 #include "transport.hpp"
 
 namespace commux {
@@ -57,7 +58,10 @@ class CollImpl {
   std::vector<char*> data_;
   std::vector<std::uint64_t*> flags_;
   std::uint64_t epoch_ = 0;
-  std::int64_t st_calls_ = 0, st_oneshot_ = 0, st_twoshot_ = 0, st_gather_ = 0, st_bytes_ = 0;
+  std::unique_ptr<NvlsBuffer> nvls_;  // null: no NVLS on this group
+  std::string nvls_why_;              // why not (empty when enabled or not attempted)
+  std::int64_t nvls_min_bytes_ = 0;
+  std::int64_t st_calls_ = 0, st_oneshot_ = 0, st_twoshot_ = 0, st_gather_ = 0, st_bytes_ = 0, st_nvls_ = 0;
 };
 
 }  // namespace cuda

@@ -5,6 +5,8 @@
 // Workspace of each rank (one cudaMalloc, IPC-mapped by every peer):
 //   [flags: kFlagPhases x kMaxCollRanks x kMaxCollCtas x u64]
 //   [region A: region_bytes][region B: region_bytes]
+// The NVLS buffer (when the group has one) is a separate allocation bound to
+// an NVSwitch multicast object; it is used by halves the same way.
 // Each region is used by halves: a call with epoch e uses half (e & 1) of A
 // and of B, so two consecutive calls never touch the same bytes; the flag
 // round every call contains guarantees a peer finished call e-2 before call e
@@ -30,7 +32,7 @@ enum CollMode : int {
   kModeAllgather = 3,
   kModeBroadcast = 4,
 };
-enum CollAlgo : int { kAlgoOneShot = 0, kAlgoTwoShot = 1 };
+enum CollAlgo : int { kAlgoOneShot = 0, kAlgoTwoShot = 1, kAlgoNvls = 2 };
 enum CollOp : int { kOpSum = 0, kOpProd = 1, kOpMin = 2, kOpMax = 3, kOpAvg = 4 };
 enum CollDtype : int { kF32 = 0, kF64, kF16, kBF16, kI32, kI64, kU8, kI8 };
 
@@ -54,7 +56,22 @@ struct CollArgs {
   std::uint64_t seq_base;               // epoch << 20
   std::uint64_t timeout_ns;
   unsigned long long* status;
+  // NVLS (kAlgoNvls): this rank's unicast mapping and the group's multicast
+  // mapping of the NVLS buffer, used by halves like the regions
+  char* nvls_uc;
+  char* nvls_mc;
+  std::int64_t nvls_bytes;     // whole buffer
+  std::int64_t nvls_half_off;  // bytes: 0 or nvls_bytes / 2
 };
+
+// True when the NVLS kernel supports (dtype, op): SUM and AVG of
+// f32/f16/bf16, MIN and MAX of f16/bf16 (the multimem reductions NVSwitch
+// performs).
+inline bool nvls_supported(int dtype, int op) {
+  if (dtype == kF32) return op == kOpSum || op == kOpAvg;
+  if (dtype == kF16 || dtype == kBF16) return op == kOpSum || op == kOpAvg || op == kOpMin || op == kOpMax;
+  return false;
+}
 
 cudaError_t launch_coll(const CollArgs& a, int ctas, cudaStream_t s);
 

@@ -32,9 +32,20 @@
 //   gather   (allgather/broadcast), chunked: push my block into slot[me] of
 //            every rank's B (broadcast: the root's block into slot 0), flag
 //            round, copy out, flag round.
+//   nvls     (large allreduce of f32/f16/bf16), chunked: copy my data into my
+//            NVLS buffer, flag round, multimem.ld_reduce my segment through
+//            the multicast mapping (NVSwitch sums every rank's copy) and
+//            multimem.st the result back (the switch writes it into every
+//            rank's copy), flag round, copy out. Each rank's NVLink carries
+//            about 1x the message each way instead of 2(P-1)/P x.
+//            The switch's reduction order is its own: results are identical
+//            on every rank but, for f16/bf16 with P > 2, may differ in the
+//            last bit from the rank-order fold.
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
+#include <type_traits>
 
 #include "coll_args.hpp"
 #include "cuda_common.hpp"
@@ -356,8 +367,154 @@ __global__ void __launch_bounds__(kCollThreads) gather_kernel(const __grid_const
   }
 }
 
+// ---- nvls ------------------------------------------------------------------------
+
+__device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
+
+// One 16-byte pack: the switch-side reduction over every rank's copy at the
+// multicast address p, then (AVG) the division by P, stored back through the
+// multicast mapping so that every rank's copy receives it.
+template <typename T, int OP>
+__device__ __forceinline__ void nvls_pack(char* p, int P) {
+  std::uint32_t r0, r1, r2, r3;
+  if constexpr (std::is_same<T, float>::value) {
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "l"(p) : "memory");
+    if constexpr (OP == kOpAvg) {
+      const float pf = static_cast<float>(P);
+      r0 = __float_as_uint(__uint_as_float(r0) / pf);
+      r1 = __float_as_uint(__uint_as_float(r1) / pf);
+      r2 = __float_as_uint(__uint_as_float(r2) / pf);
+      r3 = __float_as_uint(__uint_as_float(r3) / pf);
+    }
+  } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    if constexpr (OP == kOpSum || OP == kOpAvg)
+      asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "l"(p) : "memory");
+    else if constexpr (OP == kOpMin)
+      asm volatile("multimem.ld_reduce.relaxed.sys.global.min.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "l"(p) : "memory");
+    else
+      asm volatile("multimem.ld_reduce.relaxed.sys.global.max.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "l"(p) : "memory");
+    if constexpr (OP == kOpAvg) {
+      const float pf = static_cast<float>(P);
+      std::uint32_t* rr[4] = {&r0, &r1, &r2, &r3};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(rr[k]);
+        float2 f = __bfloat1622float2(h);
+        h = __floats2bfloat162_rn(f.x / pf, f.y / pf);
+        *rr[k] = *reinterpret_cast<std::uint32_t*>(&h);
+      }
+    }
+  } else {  // __half
+    if constexpr (OP == kOpSum || OP == kOpAvg)
+      asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.f16x2 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "l"(p) : "memory");
+    else if constexpr (OP == kOpMin)
+      asm volatile("multimem.ld_reduce.relaxed.sys.global.min.v4.f16x2 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "l"(p) : "memory");
+    else
+      asm volatile("multimem.ld_reduce.relaxed.sys.global.max.v4.f16x2 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "l"(p) : "memory");
+    if constexpr (OP == kOpAvg) {
+      const float pf = static_cast<float>(P);
+      std::uint32_t* rr[4] = {&r0, &r1, &r2, &r3};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        __half2 h = *reinterpret_cast<__half2*>(rr[k]);
+        float2 f = __half22float2(h);
+        h = __floats2half2_rn(f.x / pf, f.y / pf);
+        *rr[k] = *reinterpret_cast<std::uint32_t*>(&h);
+      }
+    }
+  }
+  // a store moves bits: the f32 form serves every element type
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(__uint_as_float(r0)),
+               "f"(__uint_as_float(r1)), "f"(__uint_as_float(r2)), "f"(__uint_as_float(r3))
+               : "memory");
+}
+
+template <typename T, int OP>
+__global__ void __launch_bounds__(kCollThreads) nvls_kernel(const __grid_constant__ CollArgs a) {
+  constexpr int N = Packs<T>::N;
+  const T* in = static_cast<const T*>(a.in);
+  T* out = static_cast<T*>(a.out);
+  const int P = a.P;
+  T* uc = reinterpret_cast<T*>(a.nvls_uc + a.nvls_half_off);
+  char* mc = a.nvls_mc + a.nvls_half_off;
+  const std::int64_t cap = ((a.nvls_bytes / 2) / static_cast<std::int64_t>(sizeof(T)) / P) / N * N;
+  const std::int64_t seg = (((a.n + P - 1) / P + N - 1) / N) * N;
+  const std::int64_t nchunks = (seg + cap - 1) / cap;
+  for (std::int64_t c = 0; c < nchunks; ++c) {
+    const std::int64_t s0 = c * cap;
+    const std::int64_t slen = min(cap, seg - s0);
+    std::int64_t lo, hi;
+    piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
+    const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
+    // piece [lo, hi) of every segment into my buffer (slot s holds segment s)
+    for (int q = 0; q < P; ++q) {
+      const int s = (a.me + q) % P;
+      const std::int64_t g = static_cast<std::int64_t>(s) * seg + s0;
+      copy_range(uc + s * cap - g, in, g + lo, min(g + hi, a.n));
+    }
+    fence_proxy_alias();  // unicast stores before multicast loads of the same bytes
+    signal(a, 0, seq);
+    if (!await(a, 0, seq)) return;
+    // my segment: reduce through the switch, store to every rank
+    {
+      const std::int64_t g = static_cast<std::int64_t>(a.me) * seg + s0;
+      const std::int64_t mhi = min(hi, a.n - g);
+      char* base = mc + (static_cast<std::int64_t>(a.me) * cap) * static_cast<std::int64_t>(sizeof(T));
+      for (std::int64_t i = lo + static_cast<std::int64_t>(threadIdx.x) * N; i < mhi;
+           i += static_cast<std::int64_t>(blockDim.x) * N)
+        nvls_pack<T, OP>(base + i * static_cast<std::int64_t>(sizeof(T)), P);
+    }
+    signal(a, 1, seq);
+    if (!await(a, 1, seq)) return;
+    fence_proxy_alias();  // multicast stores before unicast loads of the same bytes
+    for (int q = 0; q < P; ++q) {
+      const int s = (a.me + q) % P;
+      const std::int64_t g = static_cast<std::int64_t>(s) * seg + s0;
+      copy_range(out, uc + s * cap - g, g + lo, min(g + hi, a.n));
+    }
+  }
+}
+
+template <typename T>
+cudaError_t launch_nvls(const CollArgs& a, int ctas, cudaStream_t s) {
+  if constexpr (std::is_same<T, float>::value || std::is_same<T, __half>::value ||
+                std::is_same<T, __nv_bfloat16>::value) {
+    switch (a.op) {
+      case kOpSum:
+        nvls_kernel<T, kOpSum><<<ctas, kCollThreads, 0, s>>>(a);
+        return cudaGetLastError();
+      case kOpAvg:
+        nvls_kernel<T, kOpAvg><<<ctas, kCollThreads, 0, s>>>(a);
+        return cudaGetLastError();
+      case kOpMin:
+        if constexpr (!std::is_same<T, float>::value) {
+          nvls_kernel<T, kOpMin><<<ctas, kCollThreads, 0, s>>>(a);
+          return cudaGetLastError();
+        }
+        break;
+      case kOpMax:
+        if constexpr (!std::is_same<T, float>::value) {
+          nvls_kernel<T, kOpMax><<<ctas, kCollThreads, 0, s>>>(a);
+          return cudaGetLastError();
+        }
+        break;
+      default:
+        break;
+    }
+  }
+  return cudaErrorInvalidValue;
+}
+
 template <typename T, int OP>
 cudaError_t launch_reduce_family(const CollArgs& a, int ctas, cudaStream_t s) {
+  if (a.algo == kAlgoNvls) return launch_nvls<T>(a, ctas, s);
   if (a.algo == kAlgoOneShot)
     oneshot_kernel<T, OP><<<ctas, kCollThreads, 0, s>>>(a);
   else

@@ -1,0 +1,43 @@
+"""Wheel / editable install of commux_b200 (and the ``commux`` alias package).
+
+The native libraries are built by CMake through ``commux_b200.build`` (the same
+build ``python -m commux_b200.build`` runs in-tree): ``libcommux.so``,
+``libcommux_io.so`` and ``libcommux_cuda.so`` under ``commux_b200/lib``, the
+pybind modules ``commux_b200/_C`` and ``commux_b200/_ops``, and the C++ headers
+under ``commux_b200/include/commux`` for C++ consumers. torch must be
+importable at build time (install with ``--no-build-isolation``).
+
+    pip install --no-build-isolation .
+"""
+
+import subprocess
+import sys
+
+from setuptools import find_packages, setup
+from setuptools.command.build_py import build_py
+from setuptools.dist import Distribution
+
+
+class BuildNative(build_py):
+    def run(self):
+        subprocess.check_call([sys.executable, "-m", "commux_b200.build"])
+        super().run()
+
+
+class BinaryDistribution(Distribution):
+    def has_ext_modules(self):
+        return True
+
+
+setup(
+    name="commux-b200",
+    version="0.1.0",
+    description="MPI-style tagged p2p and collectives for torch.distributed on B200 (NVLink 5 / NVSwitch)",
+    packages=find_packages(include=["commux_b200", "commux_b200.*", "commux"]),
+    package_data={"commux_b200": ["_C*.so", "_ops*.so", "lib/*.so", "lib/test_commux",
+                                  "include/commux/*.hpp", "include/commux/*.h"]},
+    python_requires=">=3.10",
+    cmdclass={"build_py": BuildNative},
+    distclass=BinaryDistribution,
+    zip_safe=False,
+)

@@ -72,6 +72,13 @@ def test_collectives_cuda():
     check(run("collectives.py", 2, env=dict(CUDA, CMX_A2A="1"), timeout=240))
 
 
+def test_collective_numerics_cuda():
+    # every rank on its own GPU where there are enough (NVLS and peer kernels),
+    # else ranks share GPUs (host-staged path)
+    world = max(2, min(ngpu(), 8))
+    check(run("gpu_coll_numerics.py", world, env=CUDA, timeout=600))
+
+
 def test_smoke_entry():
     r = subprocess.run([sys.executable, os.path.join(ROOT, "__graft_entry__.py")], capture_output=True,
                        text=True, timeout=300)
