@@ -12,6 +12,7 @@
 // reduce_scatter, alltoall_base, Work::getFuture, timeouts, abort.
 
 #include "commux/process_group_ucx.hpp"
+#include "../engine/log.hpp"
 
 #include <ATen/ATen.h>
 #include <ATen/core/ivalue.h>
@@ -610,6 +611,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::batch_p2p(
     std::vector<at::Tensor>& recv_tensors, const std::vector<int>& recv_peers,
     const std::vector<int>& recv_tags, std::vector<at::Tensor>& send_tensors,
     const std::vector<int>& send_peers, const std::vector<int>& send_tags) {
+  TraceRange trace_("commux.batch_p2p");
   TORCH_CHECK(recv_tensors.size() == recv_peers.size() && recv_peers.size() == recv_tags.size() &&
                   send_tensors.size() == send_peers.size() && send_peers.size() == send_tags.size(),
               "commux batch_p2p: tensors, peers and tags must have equal lengths");
@@ -684,16 +686,19 @@ void ProcessGroupUCX::post_now(std::vector<at::Tensor>& tensors, int peer, int t
 
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::send(std::vector<at::Tensor>& tensors, int dstRank,
                                                      int tag) {
+  TraceRange trace_("commux.send");
   return post_p2p(tensors, dstRank, tag, true);
 }
 
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::recv(std::vector<at::Tensor>& tensors, int srcRank,
                                                      int tag) {
+  TraceRange trace_("commux.recv");
   return post_p2p(tensors, srcRank, tag, false);
 }
 
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::recvAnysource(std::vector<at::Tensor>& tensors,
                                                               int tag) {
+  TraceRange trace_("commux.recvAnysource");
   check_same_device_kind(tensors, "recvAnysource");
   // Non-blocking here (the reference probes and blocks, :696-732); the source
   // is known once the first tensor has matched. Tensor i > 0 is then received
@@ -727,6 +732,7 @@ void ProcessGroupUCX::startCoalescing() {
 }
 
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::endCoalescing() {
+  TraceRange trace_("commux.endCoalescing");
   auto& g = *group_;
   std::vector<GroupWindow::Deferred> deferred;
   c10::intrusive_ptr<CommuxWork> work;
@@ -777,6 +783,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::endCoalescing() {
 
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::allreduce(std::vector<at::Tensor>& tensors,
                                                           const c10d::AllreduceOptions& opts) {
+  TraceRange trace_("commux.allreduce");
   check_same_device_kind(tensors, "allreduce");
   RedOp op = validate_op(opts.reduceOp, tensors, "allreduce");
   if (tensors[0].is_cuda()) {
@@ -805,6 +812,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::allreduce(std::vector<at::Tensor
 
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::allreduce_coalesced(
     std::vector<at::Tensor>& tensors, const c10d::AllreduceCoalescedOptions& opts) {
+  TraceRange trace_("commux.allreduce_coalesced");
   c10d::AllreduceOptions o;
   o.reduceOp = opts.reduceOp;
   o.timeout = opts.timeout;
@@ -813,6 +821,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::allreduce_coalesced(
 
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::reduce(std::vector<at::Tensor>& tensors,
                                                        const c10d::ReduceOptions& opts) {
+  TraceRange trace_("commux.reduce");
   check_same_device_kind(tensors, "reduce");
   RedOp op = validate_op(opts.reduceOp, tensors, "reduce");
   int root = static_cast<int>(opts.rootRank);
@@ -843,6 +852,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::reduce(std::vector<at::Tensor>& 
 
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::broadcast(std::vector<at::Tensor>& tensors,
                                                           const c10d::BroadcastOptions& opts) {
+  TraceRange trace_("commux.broadcast");
   check_same_device_kind(tensors, "broadcast");
   int root = static_cast<int>(opts.rootRank);
   TORCH_CHECK(root >= 0 && root < getSize(), "commux broadcast: root out of range");
@@ -870,6 +880,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::broadcast(std::vector<at::Tensor
 }
 
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::barrier(const c10d::BarrierOptions& /*opts*/) {
+  TraceRange trace_("commux.barrier");
   if (getSize() > 1) coll_->barrier();
   return completed_work(engine_.get(), c10d::OpType::BARRIER, {});
 }
@@ -877,6 +888,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::barrier(const c10d::BarrierOptio
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::allgather(
     std::vector<std::vector<at::Tensor>>& outputTensors, std::vector<at::Tensor>& inputTensors,
     const c10d::AllgatherOptions& /*opts*/) {
+  TraceRange trace_("commux.allgather");
   TORCH_CHECK(inputTensors.size() == 1 && outputTensors.size() == 1,
               "commux allgather: one input tensor and one output list per call");
   auto& outs = outputTensors[0];
@@ -925,6 +937,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::allgather(
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::_allgather_base(at::Tensor& outputBuffer,
                                                                 at::Tensor& inputBuffer,
                                                                 const c10d::AllgatherOptions& /*opts*/) {
+  TraceRange trace_("commux.allgather_base");
   TORCH_CHECK(outputBuffer.numel() == inputBuffer.numel() * getSize(),
               "commux _allgather_base: output must hold world_size * input elements");
   TORCH_CHECK(outputBuffer.is_contiguous(), "commux _allgather_base: output must be contiguous");
@@ -957,6 +970,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::_allgather_base(at::Tensor& outp
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::allgather_into_tensor_coalesced(
     std::vector<at::Tensor>& outputs, std::vector<at::Tensor>& inputs,
     const c10d::AllgatherOptions& opts) {
+  TraceRange trace_("commux.allgather_coalesced");
   TORCH_CHECK(outputs.size() == inputs.size(), "commux allgather_into_tensor_coalesced: size mismatch");
   c10::intrusive_ptr<c10d::Work> last;
   auto agg = c10::make_intrusive<CommuxWork>(engine_.get(), c10d::OpType::COALESCED,
@@ -971,6 +985,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::allgather_into_tensor_coalesced(
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::gather(std::vector<std::vector<at::Tensor>>& outputTensors,
                                                        std::vector<at::Tensor>& inputTensors,
                                                        const c10d::GatherOptions& opts) {
+  TraceRange trace_("commux.gather");
   TORCH_CHECK(inputTensors.size() == 1, "commux gather: one input tensor");
   int root = static_cast<int>(opts.rootRank);
   TORCH_CHECK(!inputTensors[0].is_cuda(), "commux gather: CUDA tensors are not supported; use allgather");
@@ -994,6 +1009,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::gather(std::vector<std::vector<a
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::scatter(std::vector<at::Tensor>& outputTensors,
                                                         std::vector<std::vector<at::Tensor>>& inputTensors,
                                                         const c10d::ScatterOptions& opts) {
+  TraceRange trace_("commux.scatter");
   TORCH_CHECK(outputTensors.size() == 1, "commux scatter: one output tensor");
   TORCH_CHECK(!outputTensors[0].is_cuda(), "commux scatter: CUDA tensors are not supported");
   int root = static_cast<int>(opts.rootRank);
@@ -1014,6 +1030,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::scatter(std::vector<at::Tensor>&
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::reduce_scatter(
     std::vector<at::Tensor>& outputTensors, std::vector<std::vector<at::Tensor>>& inputTensors,
     const c10d::ReduceScatterOptions& opts) {
+  TraceRange trace_("commux.reduce_scatter");
   TORCH_CHECK(outputTensors.size() == 1 && inputTensors.size() == 1, "commux reduce_scatter: one output");
   auto& out = outputTensors[0];
   RedOp op = validate_op(opts.reduceOp, {out}, "reduce_scatter");
@@ -1055,6 +1072,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::reduce_scatter(
 c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::_reduce_scatter_base(at::Tensor& outputBuffer,
                                                                      at::Tensor& inputBuffer,
                                                                      const c10d::ReduceScatterOptions& opts) {
+  TraceRange trace_("commux.reduce_scatter_base");
   TORCH_CHECK(inputBuffer.numel() == outputBuffer.numel() * getSize(),
               "commux _reduce_scatter_base: input must hold world_size * output elements");
   RedOp op = validate_op(opts.reduceOp, {outputBuffer}, "reduce_scatter");
@@ -1087,6 +1105,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::alltoall_base(at::Tensor& output
                                                               std::vector<int64_t>& outputSplitSizes,
                                                               std::vector<int64_t>& inputSplitSizes,
                                                               const c10d::AllToAllOptions& /*opts*/) {
+  TraceRange trace_("commux.alltoall");
   const int P = getSize();
   TORCH_CHECK(outputBuffer.is_contiguous(), "commux alltoall: output must be contiguous");
   at::Tensor in = inputBuffer.contiguous();

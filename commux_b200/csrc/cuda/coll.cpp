@@ -1,5 +1,7 @@
 #include "coll.hpp"
 
+#include "engine/log.hpp"
+
 #include <ATen/core/ivalue.h>
 #include <c10/cuda/CUDACachingAllocator.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -7,6 +9,7 @@
 #include <unistd.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 namespace commux {
@@ -87,6 +90,12 @@ CollImpl::CollImpl(CudaTransport* tr, int dev)
   region_bytes_ = env_int("COMMUX_CUDA_WS_BYTES", 64ll << 20);
   region_bytes_ = std::max<std::int64_t>(region_bytes_ & ~std::int64_t(4095), 1 << 20);
   oneshot_bytes_ = env_int("COMMUX_ONESHOT_BYTES", 256 << 10);
+  // COMMUX_ALGO=oneshot|twoshot|nvls forces an algorithm for the reductions
+  // where it applies (the others keep the size-based choice)
+  if (const char* f = std::getenv("COMMUX_ALGO")) {
+    const std::string v(f);
+    forced_algo_ = v == "oneshot" ? kAlgoOneShot : v == "twoshot" ? kAlgoTwoShot : v == "nvls" ? kAlgoNvls : -1;
+  }
   int lo = 0, hi = 0;
   CMX_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
   CMX_CUDA(cudaStreamCreateWithPriority(&stream_, cudaStreamNonBlocking, hi));
@@ -121,7 +130,10 @@ CollImpl::CollImpl(CudaTransport* tr, int dev)
     std::memcpy(&recs[p], v.data(), sizeof(ExchangeRecord));
     if (std::memcmp(recs[p].uuid, ctx_->uuid, 16) == 0) shared_gpu_ = true;
   }
-  if (shared_gpu_) return;  // kernels of two processes on one GPU must not wait on each other
+  if (shared_gpu_) {  // kernels of two processes on one GPU must not wait on each other
+    logf(LogLevel::Info, me_, "device collectives: ranks share a GPU, collectives are staged through the host");
+    return;
+  }
   for (int p = 0; p < P_; ++p) {
     char* base = ws_;
     if (p != me_) {
@@ -134,18 +146,26 @@ CollImpl::CollImpl(CudaTransport* tr, int dev)
   }
   // NVLS: every rank on its own GPU and able to join (the same records on
   // every rank, so the decision and the collective set-up are shared)
-  bool nvls = P_ >= 2;
+  // At 2 ranks NVLS moves (P+1)/P of the message over each NVLink (the
+  // switch also reads and writes this rank's own copy) against 2(P-1)/P for
+  // two-shot, so it only pays from 4 ranks up.
+  bool nvls = P_ >= std::max<std::int64_t>(2, env_int("COMMUX_NVLS_MIN_RANKS", 4));
   for (int p = 0; p < P_; ++p) nvls = nvls && recs[p].nvls_ok != 0;
   nvls_min_bytes_ = env_int("COMMUX_NVLS_MIN_BYTES", 1ll << 20);
   if (nvls) {
     const std::int64_t bytes = std::max<std::int64_t>(env_int("COMMUX_NVLS_BYTES", 2 * region_bytes_), 4 << 20);
     nvls_ = NvlsBuffer::create(eng_, dev, static_cast<std::size_t>(bytes), &nvls_why_);
-    if (!nvls_ && me_ == 0)
-      std::fprintf(stderr, "commux: NVLS collectives unavailable (%s); using peer-to-peer kernels\n",
-                   nvls_why_.c_str());
+    if (!nvls_)
+      logf(LogLevel::Warn, me_, "NVLS collectives unavailable (%s); using peer-to-peer kernels", nvls_why_.c_str());
   } else {
-    nvls_why_ = P_ < 2 ? "one rank" : "COMMUX_NVLS=0 or no multicast support on some rank";
+    nvls_why_ = "too few ranks, COMMUX_NVLS=0, or no multicast support on some rank";
   }
+  logf(LogLevel::Info, me_,
+       "device collectives on GPU %d: workspace 2 x %lld bytes (IPC), one-shot <= %lld bytes, NVLS %s%s "
+       "(>= %lld bytes), COMMUX_ALGO %s",
+       dev_, static_cast<long long>(region_bytes_), static_cast<long long>(oneshot_bytes_),
+       nvls_ ? "on" : "off: ", nvls_ ? "" : nvls_why_.c_str(), static_cast<long long>(nvls_min_bytes_),
+       forced_algo_ < 0 ? "auto" : forced_algo_ == kAlgoOneShot ? "oneshot" : forced_algo_ == kAlgoTwoShot ? "twoshot" : "nvls");
 }
 
 CollImpl::~CollImpl() {
@@ -229,11 +249,19 @@ DevCollPtr CollImpl::run(const std::vector<Launch>& launches) {
     CollArgs a;
     fill(a, l, ins[k], outs[k]);
     std::int64_t bytes = l.n * a.elem_bytes;
+    const bool reduce_like = l.mode == kModeAllreduce || l.mode == kModeReduce;
+    const bool oneshot_fits = reduce_like && l.n * a.elem_bytes * P_ <= region_bytes_ / 2;
+    const bool nvls_fits = nvls_ && l.mode == kModeAllreduce && nvls_supported(a.dtype, a.op);
     int algo = kAlgoTwoShot;
-    if ((l.mode == kModeAllreduce || l.mode == kModeReduce) && bytes <= oneshot_bytes_ &&
-        l.n * a.elem_bytes * P_ <= region_bytes_ / 2)
+    if (forced_algo_ == kAlgoOneShot && oneshot_fits)
       algo = kAlgoOneShot;
-    else if (nvls_ && l.mode == kModeAllreduce && bytes >= nvls_min_bytes_ && nvls_supported(a.dtype, a.op))
+    else if (forced_algo_ == kAlgoNvls && nvls_fits)
+      algo = kAlgoNvls;
+    else if (forced_algo_ == kAlgoTwoShot)
+      algo = kAlgoTwoShot;
+    else if (oneshot_fits && bytes <= oneshot_bytes_)
+      algo = kAlgoOneShot;
+    else if (nvls_fits && bytes >= nvls_min_bytes_)
       algo = kAlgoNvls;
     a.algo = algo;
     int ctas = choose_ctas(l.mode, algo, bytes);

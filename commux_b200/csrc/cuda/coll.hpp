@@ -61,6 +61,7 @@ class CollImpl {
   std::unique_ptr<NvlsBuffer> nvls_;  // null: no NVLS on this group
   std::string nvls_why_;              // why not (empty when enabled or not attempted)
   std::int64_t nvls_min_bytes_ = 0;
+  int forced_algo_ = -1;  // COMMUX_ALGO
   std::int64_t st_calls_ = 0, st_oneshot_ = 0, st_twoshot_ = 0, st_gather_ = 0, st_bytes_ = 0, st_nvls_ = 0;
 };
 

@@ -216,6 +216,49 @@ __device__ __forceinline__ void fold_range(T* out, const T* base, std::int64_t s
   }
 }
 
+// As fold_range, but rank `me`'s operand is read from `own` (this rank's
+// input, never copied into its own slot); the fold order stays 0..P-1.
+template <typename T, int OP>
+__device__ __forceinline__ void fold_range_own(T* out, const T* base, std::int64_t stride, int P, int me,
+                                               const T* own, std::int64_t lo, std::int64_t hi) {
+  using A = typename AccT<T>::type;
+  constexpr int N = Packs<T>::N;
+  if (lo >= hi) return;
+  const bool vec = aligned16(out + lo) && aligned16(base + lo) && aligned16(own + lo) && (stride % N) == 0;
+  std::int64_t full_hi = vec ? lo + ((hi - lo) / N) * N : lo;
+  for (std::int64_t i = lo + static_cast<std::int64_t>(threadIdx.x) * N; i < full_hi;
+       i += static_cast<std::int64_t>(blockDim.x) * N) {
+    A acc[N];
+    for (int p = 0; p < P; ++p) {
+      const T* src = p == me ? own + i : base + p * stride + i;
+      uint4 raw = *reinterpret_cast<const uint4*>(src);
+      const T* v = reinterpret_cast<const T*>(&raw);
+      if (p == 0) {
+#pragma unroll
+        for (int k = 0; k < N; ++k) acc[k] = to_acc<A>(v[k]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < N; ++k) acc[k] = combine<OP>(acc[k], to_acc<A>(v[k]));
+      }
+    }
+    uint4 outraw;
+    T* o = reinterpret_cast<T*>(&outraw);
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+      A r = acc[k];
+      if constexpr (OP == kOpAvg) r = r / static_cast<A>(P);
+      o[k] = from_acc<T>(r);
+    }
+    *reinterpret_cast<uint4*>(out + i) = outraw;
+  }
+  for (std::int64_t i = full_hi + threadIdx.x; i < hi; i += blockDim.x) {
+    A acc = to_acc<A>(me == 0 ? own[i] : base[i]);
+    for (int p = 1; p < P; ++p) acc = combine<OP>(acc, to_acc<A>(p == me ? own[i] : base[p * stride + i]));
+    if constexpr (OP == kOpAvg) acc = acc / static_cast<A>(P);
+    out[i] = from_acc<T>(acc);
+  }
+}
+
 // Piece k of `parts` of [0, n), cut on pack boundaries.
 template <typename T>
 __device__ __forceinline__ void piece(std::int64_t n, int parts, int k, std::int64_t& lo,
@@ -284,8 +327,9 @@ __global__ void __launch_bounds__(kCollThreads) twoshot_kernel(const __grid_cons
     std::int64_t lo, hi;
     piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
     const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
-    // phase 0: my part of segment s -> slot[me] of rank s's A
-    for (int q = 0; q < P; ++q) {
+    // phase 0: my part of segment s -> slot[me] of rank s's A (my own
+    // segment's part stays in `in` and is read from there by the fold)
+    for (int q = 1; q < P; ++q) {
       const int s = (a.me + q) % P;
       const std::int64_t g = static_cast<std::int64_t>(s) * seg + s0;
       const std::int64_t ghi = rs ? g + hi : min(g + hi, total);
@@ -293,25 +337,27 @@ __global__ void __launch_bounds__(kCollThreads) twoshot_kernel(const __grid_cons
     }
     signal(a, 0, seq);
     if (!await(a, 0, seq)) return;
-    // fold my segment
+    // fold my segment: reduce_scatter and allreduce write it straight into
+    // `out` (allreduce then pushes it from there), reduce into my B slot
     const std::int64_t mine = static_cast<std::int64_t>(a.me) * seg + s0;
     const std::int64_t mhi = rs ? hi : min(hi, total - mine);
-    if (rs) {
-      fold_range<T, OP>(out + s0, a_me, seg_cap, P, lo, mhi);
-    } else {
-      fold_range<T, OP>(b_me + a.me * seg_cap, a_me, seg_cap, P, lo, mhi);
+    const bool to_out = rs || a.mode == kModeAllreduce || a.me == a.root;
+    T* folded = to_out ? (rs ? out + s0 : out + mine) : b_me + a.me * seg_cap;
+    fold_range_own<T, OP>(folded, a_me, seg_cap, P, a.me, in + mine, lo, mhi);
+    if (!rs) {
       __syncthreads();
       // phase 1: my folded segment -> slot[me] of B on every rank that needs it
       for (int q = 1; q < P; ++q) {
         const int p = (a.me + q) % P;
         if (a.mode == kModeReduce && p != a.root) continue;
-        copy_range(region_b<T>(a, p) + a.me * seg_cap, b_me + a.me * seg_cap, lo, mhi);
+        copy_range(region_b<T>(a, p) + a.me * seg_cap, folded, lo, mhi);
       }
     }
     signal(a, 1, seq);
     if (!await(a, 1, seq)) return;
     if (rs || (a.mode == kModeReduce && a.me != a.root)) continue;
     for (int p = 0; p < P; ++p) {
+      if (p == a.me) continue;  // folded in place above
       const std::int64_t g = static_cast<std::int64_t>(p) * seg + s0;
       const std::int64_t phi = min(hi, total - g);
       copy_range(out + g, b_me + p * seg_cap - 0, lo, phi);

@@ -127,6 +127,9 @@ std::unique_ptr<NvlsBuffer> NvlsBuffer::create(Engine* eng, int dev, std::size_t
   ap.type = CU_MEM_ALLOCATION_TYPE_PINNED;
   ap.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
   ap.location.id = dev;
+  // a shareable (exported or imported) multicast object binds only memory
+  // that is itself shareable
+  ap.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
   if (err.empty()) {
     mp.size = bytes;
     r = cuMulticastGetGranularity(&mgran, &mp, CU_MULTICAST_GRANULARITY_RECOMMENDED);
@@ -181,16 +184,20 @@ std::unique_ptr<NvlsBuffer> NvlsBuffer::create(Engine* eng, int dev, std::size_t
   } else {
     std::string name = store_get(eng, base + "sock");
     if (name.empty()) fail_here("rank 0 could not create the multicast object");
-    if (err.empty()) {
+    // connect even after a local failure, so rank 0 never waits for us
+    if (!name.empty()) {
       int s = -1;
       sockaddr_un a;
       socklen_t len = abstract_addr(name, &a);
-      while (err.empty()) {
+      for (;;) {
         s = ::socket(AF_UNIX, SOCK_STREAM | SOCK_CLOEXEC, 0);
         if (s >= 0 && ::connect(s, reinterpret_cast<sockaddr*>(&a), len) == 0) break;
         if (s >= 0) ::close(s);
         s = -1;
-        if (std::chrono::steady_clock::now() > deadline) fail_here("nvls: cannot reach rank 0's socket");
+        if (std::chrono::steady_clock::now() > deadline) {
+          fail_here("nvls: cannot reach rank 0's socket");
+          break;
+        }
         std::this_thread::sleep_for(std::chrono::milliseconds(2));
       }
       if (s >= 0) {
@@ -227,7 +234,8 @@ std::unique_ptr<NvlsBuffer> NvlsBuffer::create(Engine* eng, int dev, std::size_t
   if (err.empty()) {
     r = cuMulticastBindMem(b->mc_, 0, b->phys_, 0, size, 0);
     if (r != CUDA_SUCCESS)
-      fail_here(cu_err(r, "cuMulticastBindMem"));
+      fail_here(cu_err(r, "cuMulticastBindMem") + " (size " + std::to_string(size) + ", granularity " +
+                std::to_string(g) + ")");
     else
       b->bound_ = true;
   }

@@ -1,4 +1,5 @@
 #include "engine.hpp"
+#include "log.hpp"
 
 #include <c10/util/Exception.h>
 #include <dlfcn.h>
@@ -279,6 +280,12 @@ void Engine::bootstrap() {
   // Everyone has mapped everyone: drop the names so a crash leaks nothing.
   store_barrier(pfx + "mapped");
   segs_[rank_]->unlink();
+  logf(LogLevel::Info, rank_,
+       "engine up: %d ranks on host %s, shm rings of %llu bytes per peer, eager <= %lld bytes, "
+       "COMMUX_COALESCE=%d COMMUX_GROUP=%d, timeout %lld ms",
+       size_, host, static_cast<unsigned long long>(ring), static_cast<long long>(eager_limit_),
+       env_int("COMMUX_COALESCE", 0) != 0 ? 1 : 0, env_int("COMMUX_GROUP", 0) != 0 ? 1 : 0,
+       static_cast<long long>(timeout_.count()));
 }
 
 // ---------------------------------------------------------------------------

@@ -72,11 +72,18 @@ def test_collectives_cuda():
     check(run("collectives.py", 2, env=dict(CUDA, CMX_A2A="1"), timeout=240))
 
 
-def test_collective_numerics_cuda():
+@pytest.mark.parametrize("variant", ["default", "nvls", "p2p"])
+def test_collective_numerics_cuda(variant):
     # every rank on its own GPU where there are enough (NVLS and peer kernels),
-    # else ranks share GPUs (host-staged path)
+    # else ranks share GPUs (host-staged path); "nvls" forces the multicast
+    # path at any rank count and size, "p2p" turns it off
     world = max(2, min(ngpu(), 8))
-    check(run("gpu_coll_numerics.py", world, env=CUDA, timeout=600))
+    env = dict(CUDA)
+    if variant == "nvls":
+        env.update(COMMUX_NVLS_MIN_RANKS="2", COMMUX_NVLS_MIN_BYTES="0")
+    elif variant == "p2p":
+        env.update(COMMUX_NVLS="0")
+    check(run("gpu_coll_numerics.py", world, env=env, timeout=600))
 
 
 def test_smoke_entry():
