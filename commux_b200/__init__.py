@@ -163,6 +163,14 @@ def p2p_plan(sends=(), recvs=(), group=None):
                        [t for t, _, _ in s], [int(p) for _, p, _ in s], [int(g) for _, _, g in s])
 
 
+def transports(group=None) -> list:
+    """Transport to each rank of ``group``: ``"self"``, ``"shm"`` (shared
+    memory and, for CUDA tensors, NVLink peer memory on this host) or
+    ``"tcp"`` (another host, or ``COMMUX_TRANSPORT=tcp``; CUDA tensors are
+    staged through host memory)."""
+    return list(_C.transports(_backend_of(group, None)))
+
+
 def is_commux(group=None, device="cpu") -> bool:
     """True if ``group`` runs on the commux backend."""
     try:

@@ -504,17 +504,24 @@ std::shared_ptr<DevicePlan> ProcessGroupUCX::p2p_plan(
   for (auto* v : {&recv_tensors, &send_tensors})
     for (auto& t : *v)
       TORCH_CHECK(t.is_cuda(), "commux p2p_plan: persistent plans take CUDA tensors (use batch_p2p on CPU)");
+  for (auto* v : {&recv_peers, &send_peers})
+    for (int p : *v)
+      TORCH_CHECK(p >= 0 && p < getSize() && !engine_->remote(p), "commux p2p_plan: rank ", p,
+                  " is not on this host (persistent plans map peer memory; use batch_p2p)");
   return engine_->device()->create_plan(recv_tensors, recv_peers, recv_tags, send_tensors, send_peers,
                                         send_tags);
 }
 
 bool ProcessGroupUCX::device_coll(const at::Tensor& t) {
+  // peers on other hosts: the device kernels need every peer's memory mapped
+  if (engine_->any_remote()) return false;
   return engine_->device()->device_collectives(t.device().index());
 }
 
 std::vector<at::Tensor> ProcessGroupUCX::to_host(const std::vector<at::Tensor>& ts) {
-  // Host staging for ranks that share a GPU: the device collectives would
-  // need kernels of two processes to wait on each other on one GPU.
+  // Host staging for ranks that share a GPU (the device collectives would
+  // need kernels of two processes to wait on each other on one GPU) and for
+  // groups that span hosts.
   std::vector<at::Tensor> h;
   for (auto& t : ts) h.push_back(t.cpu().contiguous());
   return h;
@@ -652,12 +659,23 @@ void ProcessGroupUCX::post_now(std::vector<at::Tensor>& tensors, int peer, int t
                                std::vector<std::pair<at::Tensor, at::Tensor>>& unpack) {
   std::vector<at::Tensor> keep;
   keep.reserve(tensors.size());
+  // CUDA tensors to or from a rank on another host travel through host
+  // memory (the TCP transport carries host bytes only)
+  const bool stage = peer >= 0 ? engine_->remote(peer) : engine_->any_remote();
   for (auto& t : tensors) {
     // CPU sends go from a contiguous copy (the reference does the same,
     // :586-588); CPU receives into strided views land in a contiguous temp.
     // CUDA sends and receives may be strided views: the device transport
     // gathers and scatters inside its copy kernel.
-    if (t.is_cuda()) {
+    if (t.is_cuda() && stage) {
+      if (is_send) {
+        keep.push_back(t.to(at::kCPU).contiguous());
+      } else {
+        at::Tensor tmp = at::empty(t.sizes(), t.options().device(at::kCPU));
+        unpack.push_back({tmp, t});
+        keep.push_back(tmp);
+      }
+    } else if (t.is_cuda()) {
       keep.push_back(t);
     } else if (is_send) {
       keep.push_back(t.contiguous());
@@ -700,6 +718,14 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::recvAnysource(std::vector<at::Te
                                                               int tag) {
   TraceRange trace_("commux.recvAnysource");
   check_same_device_kind(tensors, "recvAnysource");
+  if (tensors[0].is_cuda() && engine_->any_remote()) {
+    // a sender on another host sends host bytes: receive into host temps
+    std::vector<at::Tensor> host;
+    for (auto& t : tensors) host.push_back(at::empty(t.sizes(), t.options().device(at::kCPU)));
+    auto w = c10::static_intrusive_pointer_cast<CommuxWork>(recvAnysource(host, tag));
+    for (std::size_t i = 0; i < tensors.size(); ++i) w->add_unpack(host[i], tensors[i]);
+    return w;
+  }
   // Non-blocking here (the reference probes and blocks, :696-732); the source
   // is known once the first tensor has matched. Tensor i > 0 is then received
   // from that same source, as the sender sends the whole vector.
@@ -756,18 +782,10 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::endCoalescing() {
   try {
     for (auto& d : deferred) {
       std::vector<ReqPtr> reqs;
-      const std::uint32_t ut = static_cast<std::uint32_t>(d.tag);
-      if (d.keep.size() > 1 && coalesce_enabled()) {
-        tag_t tg = make_ucp_tag(0, ut, 0, false);
-        reqs.push_back(d.is_send ? engine_->post_send(d.keep, d.peer, tg) : engine_->post_recv(d.keep, d.peer, tg));
-      } else {
-        for (std::size_t i = 0; i < d.keep.size(); ++i) {
-          tag_t tg = make_ucp_tag(0, ut, static_cast<std::uint32_t>(i), false);
-          reqs.push_back(d.is_send ? engine_->post_send({d.keep[i]}, d.peer, tg)
-                                   : engine_->post_recv({d.keep[i]}, d.peer, tg));
-        }
-      }
+      std::vector<std::pair<at::Tensor, at::Tensor>> unpack;
+      post_now(d.keep, d.peer, d.tag, d.is_send, reqs, unpack);
       work->add(reqs, d.is_send ? std::vector<at::Tensor>{} : d.keep);
+      for (auto& tv : unpack) work->add_unpack(tv.first, tv.second);
     }
   } catch (...) {
     if (dev) dev->end_batch();

@@ -170,6 +170,7 @@ void Engine::release_for_exit() {
   stop_.store(true);
   wake_progress();
   if (progress_.joinable()) progress_.join();
+  if (links_) links_->stop();
   {
     std::lock_guard<std::mutex> lk(dev_mu_);
     if (dev_) {
@@ -197,6 +198,7 @@ Engine::~Engine() {
   stop_.store(true);
   wake_progress();
   if (progress_.joinable()) progress_.join();
+  if (links_) links_->stop();
   if (dev_) {
     try {
       dev_->shutdown();
@@ -250,6 +252,9 @@ void Engine::bootstrap() {
   ::gethostname(host, sizeof(host) - 1);
   store_->set(pfx + "seg/" + std::to_string(rank_),
               to_bytes(myname + "\n" + host + "\n" + std::to_string(::getpid())));
+  // Same-host peers map each other's segments; peers on other hosts (or every
+  // peer under COMMUX_TRANSPORT=tcp) are reached through TCP links.
+  remote_.assign(static_cast<std::size_t>(size_), false);
   for (int p = 0; p < size_; ++p) {
     if (p == rank_) continue;
     std::string k = pfx + "seg/" + std::to_string(p);
@@ -259,27 +264,39 @@ void Engine::bootstrap() {
     std::string name, phost;
     std::getline(ss, name);
     std::getline(ss, phost);
-    if (phost != host)
-      throw std::runtime_error(
-          "commux: rank " + std::to_string(p) + " runs on host '" + phost +
-          "' but rank " + std::to_string(rank_) + " on '" + host +
-          "'; this backend's transports are intra-node (shared memory + NVLink)");
+    if (tcp::use_tcp(host, phost)) {
+      remote_[p] = true;
+      any_remote_ = true;
+      continue;
+    }
     segs_[p] = std::make_unique<shm::Segment>();
     segs_[p]->open(name);
     if (segs_[p]->header()->instance != instance)
       throw std::runtime_error("commux: segment " + name + " belongs to another group");
   }
+  if (any_remote_) links_ = std::make_unique<tcp::Links>(rank_, size_, ring, remote_, segs_[rank_].get());
   in_.resize(size_);
   out_.resize(size_);
   inflight_.resize(size_);
   for (int p = 0; p < size_; ++p) {
     in_[p].attach(segs_[rank_]->ring_ctl(p), segs_[rank_]->ring_data(p), ring);
     out_[p] = std::make_unique<PeerOut>();
-    out_[p]->ring.attach(segs_[p]->ring_ctl(rank_), segs_[p]->ring_data(rank_), ring);
+    if (remote_[p])
+      out_[p]->ring.attach(links_->out_ctl(p), links_->out_data(p), ring);
+    else
+      out_[p]->ring.attach(segs_[p]->ring_ctl(rank_), segs_[p]->ring_data(rank_), ring);
+  }
+  if (links_) {
+    links_->connect(*store_, pfx, timeout_);
+    links_->start([this] { wake_progress(); },
+                  [this](int p, const std::string& why) { fail_peer(p, why); });
   }
   // Everyone has mapped everyone: drop the names so a crash leaks nothing.
   store_barrier(pfx + "mapped");
   segs_[rank_]->unlink();
+  int ntcp = 0;
+  for (int p = 0; p < size_; ++p) ntcp += remote_[p] ? 1 : 0;
+  logf(LogLevel::Info, rank_, "transports: %d peer(s) over shared memory, %d over TCP", size_ - 1 - ntcp, ntcp);
   logf(LogLevel::Info, rank_,
        "engine up: %d ranks on host %s, shm rings of %llu bytes per peer, eager <= %lld bytes, "
        "COMMUX_COALESCE=%d COMMUX_GROUP=%d, timeout %lld ms",
@@ -315,6 +332,8 @@ ReqPtr Engine::post_send(std::vector<at::Tensor> tensors, int dst, tag_t tag) {
   r->id = next_id_.fetch_add(1);
   r->posted_at = std::chrono::steady_clock::now();
   r->device = !tensors.empty() && tensors[0].is_cuda();
+  TORCH_CHECK(!r->device || !remote(dst),
+              "commux send: CUDA tensors to a rank on another host must be staged through host memory");
   for (auto& t : tensors) {
     TORCH_CHECK(t.is_cuda() == r->device,
                 "commux send: a coalesced message mixes CPU and CUDA tensors");
@@ -439,6 +458,8 @@ ReqPtr Engine::post_recv(std::vector<at::Tensor> tensors, int src, tag_t tag) {
   r->id = next_id_.fetch_add(1);
   r->posted_at = std::chrono::steady_clock::now();
   r->device = !tensors.empty() && tensors[0].is_cuda();
+  TORCH_CHECK(!r->device || (src >= 0 ? !remote(src) : !any_remote_),
+              "commux recv: CUDA tensors from a rank on another host must be staged through host memory");
   for (auto& t : tensors) {
     TORCH_CHECK(t.is_cuda() == r->device,
                 "commux recv: a coalesced message mixes CPU and CUDA tensors");
@@ -804,10 +825,14 @@ bool Engine::flush_out(int dst, bool blocking_lock) {
   if (wrote) {
     po.ring.publish();
     std::atomic_thread_fence(std::memory_order_seq_cst);
-    auto* ph = segs_[dst]->header();
-    if (ph->sleeping.load(std::memory_order_seq_cst)) {
-      ph->doorbell.fetch_add(1);
-      shm::futex_wake(&ph->doorbell, 1);
+    if (remote_[dst]) {
+      links_->notify();
+    } else {
+      auto* ph = segs_[dst]->header();
+      if (ph->sleeping.load(std::memory_order_seq_cst)) {
+        ph->doorbell.fetch_add(1);
+        shm::futex_wake(&ph->doorbell, 1);
+      }
     }
   }
   lk.unlock();
@@ -1113,6 +1138,17 @@ void Engine::abort_group(const std::string& why) {
   bool was = aborted_.exchange(true);
   if (!was) {
     for (int p = 0; p < size_; ++p) {
+      if (remote_[p] && !dead_[p].load()) {
+        auto job = std::make_unique<OutJob>();
+        job->type = proto::kAbort;
+        job->head.resize(sizeof(proto::AbortRec));
+        auto* rec = reinterpret_cast<proto::AbortRec*>(job->head.data());
+        rec->code = 1;
+        std::strncpy(rec->reason, why.c_str(), sizeof(rec->reason) - 1);
+        enqueue(p, std::move(job));
+        flush_out(p, true);
+        continue;
+      }
       if (!segs_[p]) continue;
       auto* h = segs_[p]->header();
       std::uint32_t z = 0;
@@ -1189,7 +1225,7 @@ void Engine::check_liveness() {
     fail_all("commux: group aborted by rank " + std::to_string(who));
   }
   for (int p = 0; p < size_; ++p) {
-    if (p == rank_ || dead_[p].load()) continue;
+    if (p == rank_ || dead_[p].load() || remote_[p]) continue;  // TCP: the socket reports loss
     auto* h = segs_[p]->header();
     if (h->closed.load() != 0) continue;
     if (!pid_alive(static_cast<pid_t>(h->pid))) {

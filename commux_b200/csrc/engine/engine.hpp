@@ -36,6 +36,7 @@
 
 #include "protocol.hpp"
 #include "shm.hpp"
+#include "tcp.hpp"
 
 namespace commux {
 
@@ -186,7 +187,11 @@ class Engine {
   // Internal fault injection hook (counts operations for kill:<rank>:<n>).
   void count_op();
 
-  const shm::SegHeader* peer_header(int p) const { return segs_[p]->header(); }
+  // nullptr for a peer reached over TCP (another host)
+  const shm::SegHeader* peer_header(int p) const { return segs_[p] ? segs_[p]->header() : nullptr; }
+  // Peer p is reached over TCP (another host, or COMMUX_TRANSPORT=tcp).
+  bool remote(int p) const { return !remote_.empty() && remote_[p]; }
+  bool any_remote() const { return any_remote_; }
   shm::SegHeader* my_header() const { return segs_[rank_]->header(); }
 
  private:
@@ -231,7 +236,10 @@ class Engine {
   FaultSpec fault_;
   std::atomic<std::int64_t> op_count_{0};
 
-  std::vector<std::unique_ptr<shm::Segment>> segs_;  // [rank] own, others mapped
+  std::vector<std::unique_ptr<shm::Segment>> segs_;  // [rank] own, others mapped (null: TCP peer)
+  std::vector<bool> remote_;                         // remote_[p]: TCP peer
+  bool any_remote_ = false;
+  std::unique_ptr<tcp::Links> links_;                // TCP peers (null when none)
   std::vector<shm::RingReader> in_;                  // in_[src]
   std::vector<std::unique_ptr<PeerOut>> out_;        // out_[dst]
 

@@ -57,6 +57,12 @@ PYBIND11_MODULE(_C, m) {
     return d;
   });
   m.def("reset_stats", [](const c10::intrusive_ptr<c10d::Backend>& b) { as_commux(b)->reset_stats(); });
+  m.def("transports", [](const c10::intrusive_ptr<c10d::Backend>& b) {
+    auto& e = as_commux(b)->engine();
+    py::list kinds;
+    for (int p = 0; p < e.size(); ++p) kinds.append(p == e.rank() ? "self" : e.remote(p) ? "tcp" : "shm");
+    return kinds;
+  }, "Transport used for each peer rank: 'self', 'shm' (same host) or 'tcp'.");
   py::class_<commux::DevicePlan, std::shared_ptr<commux::DevicePlan>>(m, "P2PPlan")
       .def("start", &commux::DevicePlan::start, py::call_guard<py::gil_scoped_release>(),
            "Enqueue one exchange of the plan's buffers on the current CUDA stream.")

@@ -145,7 +145,7 @@ class HaloExchange:
             if len(self._plans) >= 8:
                 self._plans.clear()
             persistent = None
-            if u.is_cuda and self.use_plans:
+            if u.is_cuda and self.use_plans and "tcp" not in commux_b200.transports(self.group):
                 # matched once; every later exchange of this field is three
                 # stream launches (collective: all ranks reach this together)
                 persistent = commux_b200.p2p_plan(sends=sends, recvs=recvs, group=self.group)

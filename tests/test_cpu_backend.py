@@ -66,3 +66,38 @@ def test_fault_kill_detected():
     res = run("fault.py", 2, "kill", env={"COMMUX_FAULT": "kill:1:1"}, timeout=90)
     assert res[0][0] == 0, res[0][1][-3000:]
     assert res[1][0] == 77, res[1][1][-3000:]
+
+
+# --- the TCP transport (peers on other hosts), forced on this one host -------
+
+TCP = {"COMMUX_TRANSPORT": "tcp"}
+
+
+def test_tcp_torch_dist():
+    check(run("torch_dist.py", 2, env=TCP))
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_tcp_collectives(world):
+    check(run("collectives.py", world, env=TCP, timeout=180))
+
+
+def test_tcp_config1_bit_exact():
+    out = check(run("config1.py", 2, env=TCP, timeout=180))
+    assert "PASSED" in out[0][1]
+
+
+@pytest.mark.parametrize("coalesce,group", [("0", "0"), ("1", "1")])
+def test_tcp_coalesce_and_group(coalesce, group):
+    check(run("coalesce.py", 3, env=dict(TCP, COMMUX_COALESCE=coalesce, COMMUX_GROUP=group)))
+
+
+def test_tcp_halo():
+    check(run("halo.py", 4, env=TCP, timeout=240))
+
+
+def test_tcp_fault_kill_detected():
+    # a peer that exits closes its socket: the survivor's wait raises
+    res = run("fault.py", 2, "kill", env=dict(TCP, COMMUX_FAULT="kill:1:1"), timeout=90)
+    assert res[0][0] == 0, res[0][1][-3000:]
+    assert res[1][0] == 77, res[1][1][-3000:]

@@ -104,3 +104,12 @@ def test_plan_two_ranks():
 @pytest.mark.parametrize("world", [1, 2])
 def test_halo_cuda_batch_path(world):
     check(run("halo.py", world, env=dict(CUDA, COMMUX_HALO_PLAN="0", COMMUX_GROUP="1"), timeout=180))
+
+
+def test_tcp_cuda_p2p_staged():
+    # ranks "on other hosts" (forced TCP): CUDA tensors travel through host memory
+    check(run("gpu_p2p.py", 2, env=dict(CUDA, COMMUX_TRANSPORT="tcp"), timeout=240))
+
+
+def test_tcp_cuda_collectives_staged():
+    check(run("collectives.py", 2, env=dict(CUDA, COMMUX_TRANSPORT="tcp", CMX_A2A="1"), timeout=240))
