@@ -417,11 +417,12 @@ __global__ void __launch_bounds__(kCollThreads) gather_kernel(const __grid_const
 
 __device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
 
-// One 16-byte pack: the switch-side reduction over every rank's copy at the
-// multicast address p, then (AVG) the division by P, stored back through the
-// multicast mapping so that every rank's copy receives it.
+constexpr int kNvlsUnroll = 4;
+
+// The switch-side reduction over every rank's copy of the 16-byte pack at
+// multicast address p, then (AVG) the division by P.
 template <typename T, int OP>
-__device__ __forceinline__ void nvls_pack(char* p, int P) {
+__device__ __forceinline__ uint4 nvls_load(const char* p, int P) {
   std::uint32_t r0, r1, r2, r3;
   if constexpr (std::is_same<T, float>::value) {
     asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0,%1,%2,%3}, [%4];"
@@ -476,10 +477,31 @@ __device__ __forceinline__ void nvls_pack(char* p, int P) {
       }
     }
   }
-  // a store moves bits: the f32 form serves every element type
-  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(__uint_as_float(r0)),
-               "f"(__uint_as_float(r1)), "f"(__uint_as_float(r2)), "f"(__uint_as_float(r3))
+  return make_uint4(r0, r1, r2, r3);
+}
+
+// Store a pack through the multicast mapping (the switch writes it into every
+// rank's copy); a store moves bits, so the f32 form serves every type.
+__device__ __forceinline__ void nvls_store(char* p, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(__uint_as_float(v.x)),
+               "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)), "f"(__uint_as_float(v.w))
                : "memory");
+}
+
+template <typename T, int OP>
+__device__ __forceinline__ void nvls_pack(char* p, int P) {
+  nvls_store(p, nvls_load<T, OP>(p, P));
+}
+
+// U packs `stride` bytes apart: all U reductions are issued before the
+// first store.
+template <typename T, int OP, int U>
+__device__ __forceinline__ void nvls_packs(char* p, std::int64_t stride, int P) {
+  uint4 v[U];
+#pragma unroll
+  for (int k = 0; k < U; ++k) v[k] = nvls_load<T, OP>(p + k * stride, P);
+#pragma unroll
+  for (int k = 0; k < U; ++k) nvls_store(p + k * stride, v[k]);
 }
 
 template <typename T, int OP>
@@ -513,9 +535,14 @@ __global__ void __launch_bounds__(kCollThreads) nvls_kernel(const __grid_constan
       const std::int64_t g = static_cast<std::int64_t>(a.me) * seg + s0;
       const std::int64_t mhi = min(hi, a.n - g);
       char* base = mc + (static_cast<std::int64_t>(a.me) * cap) * static_cast<std::int64_t>(sizeof(T));
-      for (std::int64_t i = lo + static_cast<std::int64_t>(threadIdx.x) * N; i < mhi;
-           i += static_cast<std::int64_t>(blockDim.x) * N)
-        nvls_pack<T, OP>(base + i * static_cast<std::int64_t>(sizeof(T)), P);
+      // kNvlsUnroll packs per thread in flight: a multimem load waits for the
+      // switch's round trip, so one pack per thread would leave NVLink idle
+      const std::int64_t step = static_cast<std::int64_t>(blockDim.x) * N;
+      std::int64_t i = lo + static_cast<std::int64_t>(threadIdx.x) * N;
+      for (; i + (kNvlsUnroll - 1) * step < mhi; i += kNvlsUnroll * step)
+        nvls_packs<T, OP, kNvlsUnroll>(base + i * static_cast<std::int64_t>(sizeof(T)),
+                                       step * static_cast<std::int64_t>(sizeof(T)), P);
+      for (; i < mhi; i += step) nvls_pack<T, OP>(base + i * static_cast<std::int64_t>(sizeof(T)), P);
     }
     signal(a, 1, seq);
     if (!await(a, 1, seq)) return;
