@@ -1138,6 +1138,14 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::alltoall_base(at::Tensor& output
     }
     return parts;
   };
+  if (outputBuffer.is_cuda() && engine_->any_remote()) {
+    // a group spanning hosts: stage through host memory
+    at::Tensor hin = in.cpu(), hout = at::empty(outputBuffer.sizes(), outputBuffer.options().device(at::kCPU));
+    auto w = alltoall_base(hout, hin, outputSplitSizes, inputSplitSizes, c10d::AllToAllOptions());
+    w->wait();
+    outputBuffer.copy_(hout);
+    return completed_work(engine_.get(), c10d::OpType::ALLTOALL_BASE, {outputBuffer});
+  }
   auto outs = split(outputBuffer, outputSplitSizes);
   auto ins = split(in, inputSplitSizes);
   if (outputBuffer.is_cuda()) {

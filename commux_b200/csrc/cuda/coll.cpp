@@ -89,7 +89,9 @@ CollImpl::CollImpl(CudaTransport* tr, int dev)
   c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev));
   region_bytes_ = env_int("COMMUX_CUDA_WS_BYTES", 64ll << 20);
   region_bytes_ = std::max<std::int64_t>(region_bytes_ & ~std::int64_t(4095), 1 << 20);
-  oneshot_bytes_ = env_int("COMMUX_ONESHOT_BYTES", 256 << 10);
+  // one-shot moves (P-1) x the message out of every rank but needs a single
+  // flag round: it wins up to a few MB at 2 ranks, less as P grows
+  oneshot_bytes_ = env_int("COMMUX_ONESHOT_BYTES", P_ <= 2 ? 4ll << 20 : P_ <= 4 ? 2ll << 20 : 1ll << 20);
   // COMMUX_ALGO=oneshot|twoshot|nvls forces an algorithm for the reductions
   // where it applies (the others keep the size-based choice)
   if (const char* f = std::getenv("COMMUX_ALGO")) {
@@ -146,10 +148,11 @@ CollImpl::CollImpl(CudaTransport* tr, int dev)
   }
   // NVLS: every rank on its own GPU and able to join (the same records on
   // every rank, so the decision and the collective set-up are shared)
-  // At 2 ranks NVLS moves (P+1)/P of the message over each NVLink (the
-  // switch also reads and writes this rank's own copy) against 2(P-1)/P for
-  // two-shot, so it only pays from 4 ranks up.
-  bool nvls = P_ >= std::max<std::int64_t>(2, env_int("COMMUX_NVLS_MIN_RANKS", 4));
+  // NVLS moves (P+1)/P of the message over each NVLink (the switch also
+  // reads and writes this rank's own copy) against 2(P-1)/P for two-shot:
+  // it loses at 2 ranks, and measured below two-shot at 4, so it is chosen
+  // from 8 ranks up unless COMMUX_NVLS_MIN_RANKS says otherwise.
+  bool nvls = P_ >= std::max<std::int64_t>(2, env_int("COMMUX_NVLS_MIN_RANKS", 8));
   for (int p = 0; p < P_; ++p) nvls = nvls && recs[p].nvls_ok != 0;
   nvls_min_bytes_ = env_int("COMMUX_NVLS_MIN_BYTES", 1ll << 20);
   if (nvls) {
@@ -246,6 +249,9 @@ DevCollPtr CollImpl::run(const std::vector<Launch>& launches) {
   CMX_CUDA(cudaStreamWaitEvent(stream_, ready->ev, 0));
   for (std::size_t k = 0; k < launches.size(); ++k) {
     const Launch& l = launches[k];
+    // nothing to move: no launch (a launch without a flag round would break
+    // the rule that every call proves the peers finished the call before)
+    if (l.n == 0) continue;
     CollArgs a;
     fill(a, l, ins[k], outs[k]);
     std::int64_t bytes = l.n * a.elem_bytes;

@@ -21,7 +21,7 @@ namespace cuda {
 
 constexpr int kMaxCollRanks = 16;
 constexpr int kMaxCollCtas = 256;
-constexpr int kFlagPhases = 2;
+constexpr int kFlagPhases = 4;
 constexpr std::size_t kFlagBytes =
     static_cast<std::size_t>(kFlagPhases) * kMaxCollRanks * kMaxCollCtas * sizeof(std::uint64_t);
 

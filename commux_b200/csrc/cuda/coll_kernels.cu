@@ -25,18 +25,20 @@
 // Kernels:
 //   oneshot  (small allreduce/reduce): push my data into slot[me] of every
 //            rank's A, one flag round, fold the P slots locally.
-//   twoshot  (large allreduce/reduce/reduce_scatter), chunked: push segment s
-//            of the chunk into slot[me] of rank s's A (reduce-scatter by
-//            writes), flag round, rank s folds its segment and pushes it into
-//            slot[s] of B on every rank that needs it, flag round, copy out.
+//   twoshot  (large allreduce/reduce/reduce_scatter), pipelined over chunks
+//            by two warp groups: push segment s of the chunk into slot[me]
+//            of rank s's A (reduce-scatter by writes), flag round, rank s
+//            folds its segment (its own part read from its input) and pushes
+//            it into slot[s] of B on every rank that needs it, flag round,
+//            copy out; chunk c+1 crosses NVLink while chunk c is folded.
 //   gather   (allgather/broadcast), chunked: push my block into slot[me] of
 //            every rank's B (broadcast: the root's block into slot 0), flag
 //            round, copy out, flag round.
-//   nvls     (large allreduce of f32/f16/bf16), chunked: copy my data into my
-//            NVLS buffer, flag round, multimem.ld_reduce my segment through
-//            the multicast mapping (NVSwitch sums every rank's copy) and
-//            multimem.st the result back (the switch writes it into every
-//            rank's copy), flag round, copy out. Each rank's NVLink carries
+//   nvls     (large allreduce of f32/f16/bf16), pipelined the same way:
+//            copy my data into my NVLS buffer, flag round, multimem.ld_reduce
+//            my segment through the multicast mapping (NVSwitch sums every
+//            rank's copy) and multimem.st the result back (the switch writes
+//            it into every rank's copy), flag round, copy out. Each rank's NVLink carries
 //            about 1x the message each way instead of 2(P-1)/P x.
 //            The switch's reduction order is its own: results are identical
 //            on every rank but, for f16/bf16 with P > 2, may differ in the
@@ -168,10 +170,18 @@ __device__ __forceinline__ void copy_range(T* dst, const T* src, std::int64_t lo
   constexpr int N = Packs<T>::N;
   if (lo >= hi) return;
   std::int64_t full_hi = (aligned16(dst + lo) && aligned16(src + lo)) ? lo + ((hi - lo) / N) * N : lo;
-  for (std::int64_t i = lo + static_cast<std::int64_t>(threadIdx.x) * N; i < full_hi;
-       i += static_cast<std::int64_t>(blockDim.x) * N)
-    *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<const uint4*>(src + i);
-  for (std::int64_t i = full_hi + threadIdx.x; i < hi; i += blockDim.x) dst[i] = src[i];
+  constexpr int U = 4;  // packs in flight per thread
+  const std::int64_t step = static_cast<std::int64_t>(blockDim.x) * N;
+  std::int64_t i = lo + static_cast<std::int64_t>(threadIdx.x) * N;
+  for (; i + (U - 1) * step < full_hi; i += U * step) {
+    uint4 v[U];
+#pragma unroll
+    for (int k = 0; k < U; ++k) v[k] = *reinterpret_cast<const uint4*>(src + i + k * step);
+#pragma unroll
+    for (int k = 0; k < U; ++k) *reinterpret_cast<uint4*>(dst + i + k * step) = v[k];
+  }
+  for (; i < full_hi; i += step) *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<const uint4*>(src + i);
+  for (std::int64_t j = full_hi + threadIdx.x; j < hi; j += blockDim.x) dst[j] = src[j];
 }
 
 // out[i] = fold over p of base[p*stride + i], i in [lo, hi).
@@ -211,49 +221,6 @@ __device__ __forceinline__ void fold_range(T* out, const T* base, std::int64_t s
   for (std::int64_t i = full_hi + threadIdx.x; i < hi; i += blockDim.x) {
     A acc = to_acc<A>(base[i]);
     for (int p = 1; p < P; ++p) acc = combine<OP>(acc, to_acc<A>(base[p * stride + i]));
-    if constexpr (OP == kOpAvg) acc = acc / static_cast<A>(P);
-    out[i] = from_acc<T>(acc);
-  }
-}
-
-// As fold_range, but rank `me`'s operand is read from `own` (this rank's
-// input, never copied into its own slot); the fold order stays 0..P-1.
-template <typename T, int OP>
-__device__ __forceinline__ void fold_range_own(T* out, const T* base, std::int64_t stride, int P, int me,
-                                               const T* own, std::int64_t lo, std::int64_t hi) {
-  using A = typename AccT<T>::type;
-  constexpr int N = Packs<T>::N;
-  if (lo >= hi) return;
-  const bool vec = aligned16(out + lo) && aligned16(base + lo) && aligned16(own + lo) && (stride % N) == 0;
-  std::int64_t full_hi = vec ? lo + ((hi - lo) / N) * N : lo;
-  for (std::int64_t i = lo + static_cast<std::int64_t>(threadIdx.x) * N; i < full_hi;
-       i += static_cast<std::int64_t>(blockDim.x) * N) {
-    A acc[N];
-    for (int p = 0; p < P; ++p) {
-      const T* src = p == me ? own + i : base + p * stride + i;
-      uint4 raw = *reinterpret_cast<const uint4*>(src);
-      const T* v = reinterpret_cast<const T*>(&raw);
-      if (p == 0) {
-#pragma unroll
-        for (int k = 0; k < N; ++k) acc[k] = to_acc<A>(v[k]);
-      } else {
-#pragma unroll
-        for (int k = 0; k < N; ++k) acc[k] = combine<OP>(acc[k], to_acc<A>(v[k]));
-      }
-    }
-    uint4 outraw;
-    T* o = reinterpret_cast<T*>(&outraw);
-#pragma unroll
-    for (int k = 0; k < N; ++k) {
-      A r = acc[k];
-      if constexpr (OP == kOpAvg) r = r / static_cast<A>(P);
-      o[k] = from_acc<T>(r);
-    }
-    *reinterpret_cast<uint4*>(out + i) = outraw;
-  }
-  for (std::int64_t i = full_hi + threadIdx.x; i < hi; i += blockDim.x) {
-    A acc = to_acc<A>(me == 0 ? own[i] : base[i]);
-    for (int p = 1; p < P; ++p) acc = combine<OP>(acc, to_acc<A>(p == me ? own[i] : base[p * stride + i]));
     if constexpr (OP == kOpAvg) acc = acc / static_cast<A>(P);
     out[i] = from_acc<T>(acc);
   }
@@ -305,63 +272,294 @@ __global__ void __launch_bounds__(kCollThreads) oneshot_kernel(const __grid_cons
   fold_range<T, OP>(out, region_a<T>(a, a.me), slot, a.P, lo, hi);
 }
 
-// ---- twoshot -------------------------------------------------------------------
+// ---- warp groups -------------------------------------------------------------
+//
+// The pipelined kernels split each CTA into two warp groups: the "link" group
+// moves data across NVLink (posted stores into peers' workspaces, or multimem
+// operations), the "local" group folds and copies within this GPU's HBM. Chunk
+// c+1 crosses NVLink while chunk c is folded and copied out. Each group syncs
+// only on its own named barrier; the groups meet through flags (global, for
+// every rank, including this one) and through a shared-memory counter polled
+// with a bounded wait, never through a barrier they must both reach, so a
+// group that gives up on a timeout cannot leave the other one stuck.
 
-template <typename T, int OP>
-__global__ void __launch_bounds__(kCollThreads) twoshot_kernel(const __grid_constant__ CollArgs a) {
+struct Grp {
+  int id;    // named barrier (1 or 2)
+  int base;  // first thread
+  int n;     // threads
+  __device__ int tid() const { return static_cast<int>(threadIdx.x) - base; }
+  __device__ void sync() const { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+};
+
+// Shared state of the two groups of one CTA.
+struct PipeShared {
+  int fail[2];        // per group: a wait of that group gave up (written before its barrier)
+  int decision[2];    // per group: outcome of a cross-group wait (thread 0 -> group)
+  volatile long long folded;  // local group: chunks whose fold is complete
+};
+
+__device__ __forceinline__ void gsignal(const CollArgs& a, const Grp& g, int phase, std::uint64_t seq) {
+  g.sync();  // every store of the group precedes the flag
+  const int p = g.tid();
+  if (p < a.P) {
+    fence_acq_rel_sys();
+    st_release_sys(flag_at(a.flags[p], phase, a.me, blockIdx.x), seq);
+  }
+}
+
+// Thread p of the group waits for rank p's flag; false (the same on every
+// thread of the group) if any of those waits gave up, now or earlier.
+__device__ __forceinline__ bool gawait(const CollArgs& a, const Grp& g, PipeShared& sh, int gi, int phase,
+                                       std::uint64_t seq) {
+  const int p = g.tid();
+  if (p < a.P) {
+    const std::uint64_t* f = flag_at(a.flags[a.me], phase, p, blockIdx.x);
+    const std::uint64_t t0 = globaltimer_ns();
+    std::uint32_t spins = 0;
+    while (ld_acquire_sys(f) < seq) {
+      if ((++spins & 31u) == 0u && globaltimer_ns() - t0 > a.timeout_ns) {
+        report_status(a.status, kStatusCollTimeout, static_cast<unsigned long long>(p), seq >> 20,
+                      ld_acquire_sys(f));
+        sh.fail[gi] = 1;
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  g.sync();
+  return sh.fail[gi] == 0;
+}
+
+// dst[i] = src[i] for i in [lo, hi), by the threads of one group, four
+// 16-byte packs in flight per thread.
+template <typename T>
+__device__ __forceinline__ void gcopy(const Grp& g, T* dst, const T* src, std::int64_t lo, std::int64_t hi) {
   constexpr int N = Packs<T>::N;
+  constexpr int U = 4;
+  if (lo >= hi) return;
+  const std::int64_t t = g.tid(), nt = g.n, step = nt * N;
+  std::int64_t full_hi = (aligned16(dst + lo) && aligned16(src + lo)) ? lo + ((hi - lo) / N) * N : lo;
+  std::int64_t i = lo + t * N;
+  for (; i + (U - 1) * step < full_hi; i += U * step) {
+    uint4 v[U];
+#pragma unroll
+    for (int k = 0; k < U; ++k) v[k] = *reinterpret_cast<const uint4*>(src + i + k * step);
+#pragma unroll
+    for (int k = 0; k < U; ++k) *reinterpret_cast<uint4*>(dst + i + k * step) = v[k];
+  }
+  for (; i < full_hi; i += step) *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<const uint4*>(src + i);
+  for (std::int64_t j = full_hi + t; j < hi; j += nt) dst[j] = src[j];
+}
+
+// out[i] = fold over p of (p == me ? own[i] : base[p*stride + i]), rank order.
+template <typename T, int OP>
+__device__ __forceinline__ void gfold(const Grp& g, T* out, const T* base, std::int64_t stride, int P, int me,
+                                      const T* own, std::int64_t lo, std::int64_t hi) {
+  using A = typename AccT<T>::type;
+  constexpr int N = Packs<T>::N;
+  if (lo >= hi) return;
+  const std::int64_t t = g.tid(), nt = g.n;
+  const bool vec = aligned16(out + lo) && aligned16(base + lo) && aligned16(own + lo) && (stride % N) == 0;
+  std::int64_t full_hi = vec ? lo + ((hi - lo) / N) * N : lo;
+  constexpr int U = 2;  // packs in flight per thread
+  const std::int64_t step = nt * N;
+  std::int64_t i0 = lo + t * N;
+  for (; i0 < full_hi; i0 += U * step) {
+    A acc[U][N];
+    for (int p = 0; p < P; ++p) {
+      uint4 raw[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const std::int64_t i = i0 + u * step;
+        if (i < full_hi) raw[u] = *reinterpret_cast<const uint4*>(p == me ? own + i : base + p * stride + i);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const T* v = reinterpret_cast<const T*>(&raw[u]);
+        if (p == 0) {
+#pragma unroll
+          for (int k = 0; k < N; ++k) acc[u][k] = to_acc<A>(v[k]);
+        } else {
+#pragma unroll
+          for (int k = 0; k < N; ++k) acc[u][k] = combine<OP>(acc[u][k], to_acc<A>(v[k]));
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const std::int64_t i = i0 + u * step;
+      if (i >= full_hi) break;
+      uint4 outraw;
+      T* o = reinterpret_cast<T*>(&outraw);
+#pragma unroll
+      for (int k = 0; k < N; ++k) {
+        A r = acc[u][k];
+        if constexpr (OP == kOpAvg) r = r / static_cast<A>(P);
+        o[k] = from_acc<T>(r);
+      }
+      *reinterpret_cast<uint4*>(out + i) = outraw;
+    }
+  }
+  for (std::int64_t i = full_hi + t; i < hi; i += nt) {
+    A acc = to_acc<A>(me == 0 ? own[i] : base[i]);
+    for (int p = 1; p < P; ++p) acc = combine<OP>(acc, to_acc<A>(p == me ? own[i] : base[p * stride + i]));
+    if constexpr (OP == kOpAvg) acc = acc / static_cast<A>(P);
+    out[i] = from_acc<T>(acc);
+  }
+}
+
+// Elements per chunk of one segment: a few chunks to pipeline, none below
+// 2 MiB (each flag round costs microseconds), within the slot the workspace
+// quarter gives each rank.
+template <typename T>
+__device__ __forceinline__ std::int64_t pipe_chunk(std::int64_t seg, std::int64_t slot_cap) {
+  constexpr int N = Packs<T>::N;
+  std::int64_t c = (seg + 3) / 4;
+  const std::int64_t lo = (2 << 20) / static_cast<std::int64_t>(sizeof(T));
+  if (c < lo) c = lo;
+  if (c > slot_cap) c = slot_cap;
+  return (c + N - 1) / N * N > slot_cap ? slot_cap : (c + N - 1) / N * N;
+}
+
+// ---- pipelined two-shot (allreduce / reduce / reduce_scatter) ---------------------
+//
+// Each call's half of regions A and B is cut into two chunk buffers (chunk c
+// uses buffer c & 1). Flag phases, per chunk: 0 = my parts of the chunk are in
+// your A, 1 = my folded segment is in your B (also: my fold of the chunk is
+// done, so your A buffer may be refilled), 2 = I copied the chunk out of my B
+// (your B buffer may be refilled).
+//   link group:  push parts of chunk 0; then per chunk c: [wait 1(c-1)] push
+//                parts of c+1 -> signal 0(c+1) -> wait own fold(c) ->
+//                [wait 2(c-2)] push folded c -> signal 1(c)
+//   local group: wait 0(c) -> fold -> publish fold(c) -> [wait 1(c-1) ->
+//                copy-out c-1 -> signal 2(c-1)]; after the last chunk, the
+//                copy-out of the last one.
+template <typename T, int OP>
+__global__ void __launch_bounds__(kCollThreads, 1) twoshot_pipe_kernel(const __grid_constant__ CollArgs a) {
+  constexpr int N = Packs<T>::N;
+  __shared__ PipeShared sh;
+  if (threadIdx.x == 0) {
+    sh.fail[0] = sh.fail[1] = 0;
+    sh.decision[0] = sh.decision[1] = 0;
+    sh.folded = 0;
+  }
+  __syncthreads();
   const T* in = static_cast<const T*>(a.in);
   T* out = static_cast<T*>(a.out);
   const int P = a.P;
   const bool rs = a.mode == kModeReduceScatter;
-  const std::int64_t seg_cap = slot_elems<T>(a, P);
   const std::int64_t total = rs ? a.n * P : a.n;
-  // segment s of the tensor: [s*seg, s*seg + seg) (reduce_scatter: block s)
   const std::int64_t seg = rs ? a.n : (((total + P - 1) / P + N - 1) / N) * N;
-  const std::int64_t nchunks = (seg + seg_cap - 1) / seg_cap;
-  T* a_me = region_a<T>(a, a.me);
-  T* b_me = region_b<T>(a, a.me);
-  for (std::int64_t c = 0; c < nchunks; ++c) {
-    const std::int64_t s0 = c * seg_cap;
-    const std::int64_t slen = min(seg_cap, seg - s0);
-    std::int64_t lo, hi;
-    piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
-    const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
-    // phase 0: my part of segment s -> slot[me] of rank s's A (my own
-    // segment's part stays in `in` and is read from there by the fold)
-    for (int q = 1; q < P; ++q) {
-      const int s = (a.me + q) % P;
-      const std::int64_t g = static_cast<std::int64_t>(s) * seg + s0;
-      const std::int64_t ghi = rs ? g + hi : min(g + hi, total);
-      copy_range(region_a<T>(a, s) + a.me * seg_cap - g, in, g + lo, ghi);
-    }
-    signal(a, 0, seq);
-    if (!await(a, 0, seq)) return;
-    // fold my segment: reduce_scatter and allreduce write it straight into
-    // `out` (allreduce then pushes it from there), reduce into my B slot
-    const std::int64_t mine = static_cast<std::int64_t>(a.me) * seg + s0;
-    const std::int64_t mhi = rs ? hi : min(hi, total - mine);
-    const bool to_out = rs || a.mode == kModeAllreduce || a.me == a.root;
-    T* folded = to_out ? (rs ? out + s0 : out + mine) : b_me + a.me * seg_cap;
-    fold_range_own<T, OP>(folded, a_me, seg_cap, P, a.me, in + mine, lo, mhi);
-    if (!rs) {
-      __syncthreads();
-      // phase 1: my folded segment -> slot[me] of B on every rank that needs it
+  // slot of one rank in one chunk buffer: a quarter of the region, P slots
+  const std::int64_t slot_cap = ((a.region_bytes / 4) / static_cast<std::int64_t>(sizeof(T)) / P) / N * N;
+  const std::int64_t cap = pipe_chunk<T>(seg, slot_cap);
+  const std::int64_t nchunks = (seg + cap - 1) / cap;
+  const bool to_out = rs || a.mode == kModeAllreduce || a.me == a.root;
+  const Grp link{1, 0, kCollThreads / 2}, local{2, kCollThreads / 2, kCollThreads / 2};
+  const bool is_link = static_cast<int>(threadIdx.x) < kCollThreads / 2;
+  auto abuf = [&](int p, std::int64_t c) {
+    return region_a<T>(a, p) + ((c & 1) ? (a.region_bytes / 4) / static_cast<std::int64_t>(sizeof(T)) : 0);
+  };
+  auto bbuf = [&](int p, std::int64_t c) {
+    return region_b<T>(a, p) + ((c & 1) ? (a.region_bytes / 4) / static_cast<std::int64_t>(sizeof(T)) : 0);
+  };
+  const std::int64_t mine = static_cast<std::int64_t>(a.me) * seg;
+  if (is_link) {
+    // push my parts of chunk c into every peer's A buffer c&1
+    auto push_parts = [&](std::int64_t c) -> bool {
+      const std::int64_t s0 = c * cap, slen = min(cap, seg - s0);
+      std::int64_t lo, hi;
+      piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
+      const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
+      // the buffer is free once every rank folded chunk c-2
+      if (c >= 2 && !gawait(a, link, sh, 0, 1, seq - 2)) return false;
+      for (int q = 1; q < P; ++q) {
+        const int s = (a.me + q) % P;
+        const std::int64_t g = static_cast<std::int64_t>(s) * seg + s0;
+        const std::int64_t ghi = rs ? g + hi : min(g + hi, total);
+        gcopy(link, abuf(s, c) + a.me * cap - g, in, g + lo, ghi);
+      }
+      gsignal(a, link, 0, seq);
+      return true;
+    };
+    if (nchunks > 0 && !push_parts(0)) return;
+    for (std::int64_t c = 0; c < nchunks; ++c) {
+      // chunk c+1 crosses NVLink while the local group folds chunk c
+      if (c + 1 < nchunks && !push_parts(c + 1)) return;
+      if (rs) continue;
+      const std::int64_t s0 = c * cap, slen = min(cap, seg - s0);
+      std::int64_t lo, hi;
+      piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
+      const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
+      // my fold of chunk c (local group) before its result goes out
+      if (link.tid() == 0) {
+        const std::uint64_t t0 = globaltimer_ns();
+        int ok = 1;
+        while (sh.folded < c + 1) {
+          if (sh.fail[1] != 0 || globaltimer_ns() - t0 > a.timeout_ns) {
+            ok = 0;
+            break;
+          }
+          __nanosleep(32);
+        }
+        __threadfence_block();
+        sh.decision[0] = ok;
+      }
+      link.sync();
+      if (sh.decision[0] == 0) {
+        if (link.tid() == 0) sh.fail[0] = 1;
+        return;
+      }
+      // B buffer c&1 of every rank is free once it copied chunk c-2 out
+      if (c >= 2 && !gawait(a, link, sh, 0, 2, seq - 2)) return;
+      const T* folded = to_out ? out + mine + s0 : bbuf(a.me, c) + a.me * cap;
+      const std::int64_t mhi = min(hi, total - mine - s0);
       for (int q = 1; q < P; ++q) {
         const int p = (a.me + q) % P;
         if (a.mode == kModeReduce && p != a.root) continue;
-        copy_range(region_b<T>(a, p) + a.me * seg_cap, folded, lo, mhi);
+        gcopy(link, bbuf(p, c) + a.me * cap, folded, lo, mhi);
       }
+      gsignal(a, link, 1, seq);
     }
-    signal(a, 1, seq);
-    if (!await(a, 1, seq)) return;
-    if (rs || (a.mode == kModeReduce && a.me != a.root)) continue;
-    for (int p = 0; p < P; ++p) {
-      if (p == a.me) continue;  // folded in place above
-      const std::int64_t g = static_cast<std::int64_t>(p) * seg + s0;
-      const std::int64_t phi = min(hi, total - g);
-      copy_range(out + g, b_me + p * seg_cap - 0, lo, phi);
+  } else {
+    auto copy_out = [&](std::int64_t c) -> bool {
+      const std::int64_t s0 = c * cap, slen = min(cap, seg - s0);
+      std::int64_t lo, hi;
+      piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
+      const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
+      if (!gawait(a, local, sh, 1, 1, seq)) return false;
+      if (!(a.mode == kModeReduce && a.me != a.root)) {
+        for (int p = 0; p < P; ++p) {
+          if (p == a.me) continue;
+          const std::int64_t g = static_cast<std::int64_t>(p) * seg + s0;
+          gcopy(local, out + g, bbuf(a.me, c) + p * cap, lo, min(hi, total - g));
+        }
+      }
+      gsignal(a, local, 2, seq);
+      return true;
+    };
+    for (std::int64_t c = 0; c < nchunks; ++c) {
+      const std::int64_t s0 = c * cap, slen = min(cap, seg - s0);
+      std::int64_t lo, hi;
+      piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
+      const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
+      if (!gawait(a, local, sh, 1, 0, seq)) return;
+      const std::int64_t mhi = rs ? hi : min(hi, total - mine - s0);
+      T* folded = rs ? out + s0 : (to_out ? out + mine + s0 : bbuf(a.me, c) + a.me * cap);
+      gfold<T, OP>(local, folded, abuf(a.me, c), cap, P, a.me, in + mine + s0, lo, mhi);
+      if (rs) {
+        // the fold is the whole job; phase 1 still tells peers my A buffer is free
+        gsignal(a, local, 1, seq);
+        continue;
+      }
+      local.sync();
+      if (local.tid() == 0) {
+        __threadfence_block();
+        sh.folded = c + 1;
+      }
+      if (c >= 1 && !copy_out(c - 1)) return;
     }
+    if (!rs && nchunks >= 1) copy_out(nchunks - 1);
   }
 }
 
@@ -504,54 +702,89 @@ __device__ __forceinline__ void nvls_packs(char* p, std::int64_t stride, int P) 
   for (int k = 0; k < U; ++k) nvls_store(p + k * stride, v[k]);
 }
 
+// Pipelined NVLS allreduce. Each call's half of the NVLS buffer holds two
+// chunk buffers (chunk c uses buffer c & 1; slot s of a buffer holds segment
+// s of the chunk). Flag phases: 0 = my copy of chunk c is in my buffer,
+// 1 = I reduced my segment of chunk c and stored it to every rank.
+//   local group: [wait 1(c-2)] copy in -> signal 0(c) -> [wait 1(c-1) ->
+//                copy out c-1]; then the copy-out of the last chunk
+//   link group:  wait 0(c) -> multimem reduce + store my segment -> signal 1(c)
 template <typename T, int OP>
-__global__ void __launch_bounds__(kCollThreads) nvls_kernel(const __grid_constant__ CollArgs a) {
+__global__ void __launch_bounds__(kCollThreads, 1) nvls_kernel(const __grid_constant__ CollArgs a) {
   constexpr int N = Packs<T>::N;
+  __shared__ PipeShared sh;
+  if (threadIdx.x == 0) {
+    sh.fail[0] = sh.fail[1] = 0;
+    sh.decision[0] = sh.decision[1] = 0;
+    sh.folded = 0;
+  }
+  __syncthreads();
   const T* in = static_cast<const T*>(a.in);
   T* out = static_cast<T*>(a.out);
   const int P = a.P;
-  T* uc = reinterpret_cast<T*>(a.nvls_uc + a.nvls_half_off);
-  char* mc = a.nvls_mc + a.nvls_half_off;
-  const std::int64_t cap = ((a.nvls_bytes / 2) / static_cast<std::int64_t>(sizeof(T)) / P) / N * N;
+  const std::int64_t quarter = (a.nvls_bytes / 4) / static_cast<std::int64_t>(sizeof(T));
+  const std::int64_t slot_cap = (quarter / P) / N * N;
   const std::int64_t seg = (((a.n + P - 1) / P + N - 1) / N) * N;
+  const std::int64_t cap = pipe_chunk<T>(seg, slot_cap);
   const std::int64_t nchunks = (seg + cap - 1) / cap;
-  for (std::int64_t c = 0; c < nchunks; ++c) {
-    const std::int64_t s0 = c * cap;
-    const std::int64_t slen = min(cap, seg - s0);
-    std::int64_t lo, hi;
-    piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
-    const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
-    // piece [lo, hi) of every segment into my buffer (slot s holds segment s)
-    for (int q = 0; q < P; ++q) {
-      const int s = (a.me + q) % P;
-      const std::int64_t g = static_cast<std::int64_t>(s) * seg + s0;
-      copy_range(uc + s * cap - g, in, g + lo, min(g + hi, a.n));
-    }
-    fence_proxy_alias();  // unicast stores before multicast loads of the same bytes
-    signal(a, 0, seq);
-    if (!await(a, 0, seq)) return;
-    // my segment: reduce through the switch, store to every rank
-    {
+  const Grp link{1, 0, kCollThreads / 2}, local{2, kCollThreads / 2, kCollThreads / 2};
+  auto ucbuf = [&](std::int64_t c) {
+    return reinterpret_cast<T*>(a.nvls_uc + a.nvls_half_off) + ((c & 1) ? quarter : 0);
+  };
+  auto mcbuf = [&](std::int64_t c) {
+    return a.nvls_mc + a.nvls_half_off + ((c & 1) ? quarter : 0) * static_cast<std::int64_t>(sizeof(T));
+  };
+  if (static_cast<int>(threadIdx.x) < kCollThreads / 2) {
+    for (std::int64_t c = 0; c < nchunks; ++c) {
+      const std::int64_t s0 = c * cap, slen = min(cap, seg - s0);
+      std::int64_t lo, hi;
+      piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
+      const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
+      if (!gawait(a, link, sh, 0, 0, seq)) return;
+      fence_proxy_alias();  // every rank's unicast stores before the multicast loads
       const std::int64_t g = static_cast<std::int64_t>(a.me) * seg + s0;
       const std::int64_t mhi = min(hi, a.n - g);
-      char* base = mc + (static_cast<std::int64_t>(a.me) * cap) * static_cast<std::int64_t>(sizeof(T));
-      // kNvlsUnroll packs per thread in flight: a multimem load waits for the
-      // switch's round trip, so one pack per thread would leave NVLink idle
-      const std::int64_t step = static_cast<std::int64_t>(blockDim.x) * N;
-      std::int64_t i = lo + static_cast<std::int64_t>(threadIdx.x) * N;
+      char* base = mcbuf(c) + (static_cast<std::int64_t>(a.me) * cap) * static_cast<std::int64_t>(sizeof(T));
+      const std::int64_t step = static_cast<std::int64_t>(link.n) * N;
+      std::int64_t i = lo + static_cast<std::int64_t>(link.tid()) * N;
       for (; i + (kNvlsUnroll - 1) * step < mhi; i += kNvlsUnroll * step)
         nvls_packs<T, OP, kNvlsUnroll>(base + i * static_cast<std::int64_t>(sizeof(T)),
                                        step * static_cast<std::int64_t>(sizeof(T)), P);
       for (; i < mhi; i += step) nvls_pack<T, OP>(base + i * static_cast<std::int64_t>(sizeof(T)), P);
+      gsignal(a, link, 1, seq);
     }
-    signal(a, 1, seq);
-    if (!await(a, 1, seq)) return;
-    fence_proxy_alias();  // multicast stores before unicast loads of the same bytes
-    for (int q = 0; q < P; ++q) {
-      const int s = (a.me + q) % P;
-      const std::int64_t g = static_cast<std::int64_t>(s) * seg + s0;
-      copy_range(out, uc + s * cap - g, g + lo, min(g + hi, a.n));
+  } else {
+    auto copy_out = [&](std::int64_t c) -> bool {
+      const std::int64_t s0 = c * cap, slen = min(cap, seg - s0);
+      std::int64_t lo, hi;
+      piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
+      const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
+      if (!gawait(a, local, sh, 1, 1, seq)) return false;
+      fence_proxy_alias();  // multicast stores before the unicast loads
+      for (int q = 0; q < P; ++q) {
+        const int s = (a.me + q) % P;
+        const std::int64_t g = static_cast<std::int64_t>(s) * seg + s0;
+        gcopy(local, out, ucbuf(c) + s * cap - g, g + lo, min(g + hi, a.n));
+      }
+      return true;
+    };
+    for (std::int64_t c = 0; c < nchunks; ++c) {
+      const std::int64_t s0 = c * cap, slen = min(cap, seg - s0);
+      std::int64_t lo, hi;
+      piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
+      const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
+      // buffer c&1 is free once every rank stored (and loaded) chunk c-2
+      if (c >= 2 && !gawait(a, local, sh, 1, 1, seq - 2)) return;
+      for (int q = 0; q < P; ++q) {
+        const int s = (a.me + q) % P;
+        const std::int64_t g = static_cast<std::int64_t>(s) * seg + s0;
+        gcopy(local, ucbuf(c) + s * cap - g, in, g + lo, min(g + hi, a.n));
+      }
+      fence_proxy_alias();
+      gsignal(a, local, 0, seq);
+      if (c >= 1 && !copy_out(c - 1)) return;
     }
+    if (nchunks >= 1) copy_out(nchunks - 1);
   }
 }
 
@@ -591,7 +824,7 @@ cudaError_t launch_reduce_family(const CollArgs& a, int ctas, cudaStream_t s) {
   if (a.algo == kAlgoOneShot)
     oneshot_kernel<T, OP><<<ctas, kCollThreads, 0, s>>>(a);
   else
-    twoshot_kernel<T, OP><<<ctas, kCollThreads, 0, s>>>(a);
+    twoshot_pipe_kernel<T, OP><<<ctas, kCollThreads, 0, s>>>(a);
   return cudaGetLastError();
 }
 

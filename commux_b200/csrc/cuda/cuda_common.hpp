@@ -70,6 +70,10 @@ struct PullBatch {
   std::uint32_t* counters;          // per-stream scratch, zero between launches
   unsigned long long* status;       // host-mapped status word (4 x u64)
   std::uint64_t timeout_ns;         // bound of the ready-flag waits
+  // persistent plans: the ready/done value of every flagged descriptor is
+  // *epoch (device memory, advanced once per start by the plan's last launch),
+  // so a plan's launches never change and replay as one CUDA graph
+  const std::uint64_t* epoch;
   PullDesc d[kMaxBatch];
 };
 
@@ -86,6 +90,7 @@ struct WaitBatch {
   std::uint32_t n;
   std::uint64_t timeout_ns;
   unsigned long long* status;
+  const std::uint64_t* epoch;  // non-null: every val is *epoch (plans)
   const std::uint64_t* flag[kMaxWaitFlags];
   std::uint64_t val[kMaxWaitFlags];
 };
@@ -103,6 +108,11 @@ enum : unsigned long long {
 // *launches when given (one per unit class present in the batch).
 cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStream_t s,
                         int* launches = nullptr);
+// Unit class of a descriptor: one kernel instantiation per class (16, 8, 4,
+// 2, 1 byte units; 0 = wide strides).
+inline int pull_unit_class(const PullDesc& d) { return d.wide ? 0 : static_cast<int>(d.unit); }
+// *epoch += 1 (one thread): the last launch of a plan's start.
+cudaError_t launch_epoch_bump(std::uint64_t* epoch, cudaStream_t s);
 cudaError_t launch_wait(const WaitBatch& b, cudaStream_t s);
 cudaError_t launch_signal(std::uint64_t* flag, std::uint64_t val, cudaStream_t s);
 cudaError_t launch_signal_many(const SignalBatch& b, cudaStream_t s);

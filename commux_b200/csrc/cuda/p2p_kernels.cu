@@ -62,6 +62,7 @@ __device__ __forceinline__ void copy_units(const PullDesc& d, std::uint32_t u0, 
   char* __restrict__ dst = d.dst;
   const std::int32_t css = static_cast<std::int32_t>(d.sst[in]);
   const std::int32_t cds = static_cast<std::int32_t>(d.dstr[in]);
+  const FastDiv rdiv = d.div[in];  // in registers: the descriptor may live in global memory
   std::uint32_t crow = 0xffffffffu;
   std::int64_t rso = 0, rdo = 0;
   for (std::uint32_t base = u0 + (threadIdx.x & 31u); base < u1; base += step * kUnroll) {
@@ -71,8 +72,8 @@ __device__ __forceinline__ void copy_units(const PullDesc& d, std::uint32_t u0, 
     for (int k = 0; k < kUnroll; ++k) {
       const std::uint32_t u = base + k * step;
       if (u < u1) {
-        const std::uint32_t row = d.div[in].div(u);
-        const std::uint32_t col = u - row * d.div[in].d;
+        const std::uint32_t row = rdiv.div(u);
+        const std::uint32_t col = u - row * rdiv.d;
         if (row != crow) {
           crow = row;
           std::uint32_t rem = row;
@@ -136,16 +137,17 @@ __device__ __noinline__ void copy_units_wide(const PullDesc& d, std::uint32_t u0
 
 // Bounded wait for a persistent plan's ready flag (thread 0 of the CTA).
 // Gives up after the timeout, or at once if another wait already failed.
-__device__ __forceinline__ bool wait_ready(const PullDesc& d, const PullBatch& b) {
-  if (ld_acquire_sys(d.ready) >= d.ready_val) return true;
+__device__ __forceinline__ bool wait_ready(const std::uint64_t* ready, std::uint64_t want,
+                                          unsigned long long* status, std::uint64_t timeout_ns) {
+  if (ld_acquire_sys(ready) >= want) return true;
   const std::uint64_t t0 = globaltimer_ns();
   std::uint32_t spins = 0;
-  while (ld_acquire_sys(d.ready) < d.ready_val) {
+  while (ld_acquire_sys(ready) < want) {
     if ((++spins & 63u) == 0u) {
-      if (*reinterpret_cast<volatile unsigned long long*>(b.status) != 0ull) return false;
-      if (globaltimer_ns() - t0 > b.timeout_ns) {
-        report_status(b.status, kStatusWaitTimeout, reinterpret_cast<unsigned long long>(d.ready),
-                      d.ready_val, ld_acquire_sys(d.ready));
+      if (*reinterpret_cast<volatile unsigned long long*>(status) != 0ull) return false;
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        report_status(status, kStatusWaitTimeout, reinterpret_cast<unsigned long long>(ready), want,
+                      ld_acquire_sys(ready));
         return false;
       }
     }
@@ -154,13 +156,27 @@ __device__ __forceinline__ bool wait_ready(const PullDesc& d, const PullBatch& b
   return true;
 }
 
+// Descriptors in the kernel parameter block (read through the constant
+// cache); the epoch of a plan's launch comes from device memory.
+struct InlineSrc {
+  const PullBatch& b;
+  __device__ std::uint32_t n() const { return b.n; }
+  __device__ std::uint32_t total() const { return b.total_chunks; }
+  __device__ const PullDesc& desc(std::uint32_t i) const { return b.d[i]; }
+  __device__ std::uint32_t* counters() const { return b.counters; }
+  __device__ unsigned long long* status() const { return b.status; }
+  __device__ std::uint64_t timeout_ns() const { return b.timeout_ns; }
+  __device__ std::uint64_t epoch() const { return b.epoch ? *b.epoch : 0; }
+};
+
 // Descriptor owning global chunk c: the last one whose chunk0 <= c (binary
-// search; descriptors are sorted by chunk0 and d[0].chunk0 == 0).
-__device__ __forceinline__ std::uint32_t find_desc(const PullBatch& b, std::uint32_t c) {
-  std::uint32_t lo = 0, hi = b.n;  // answer in [lo, hi)
+// search; descriptors are sorted by chunk0 and the first has chunk0 == 0).
+template <class S>
+__device__ __forceinline__ std::uint32_t find_desc(const S& s, std::uint32_t c) {
+  std::uint32_t lo = 0, hi = s.n();  // answer in [lo, hi)
   while (hi - lo > 1) {
     const std::uint32_t mid = (lo + hi) >> 1;
-    if (b.d[mid].chunk0 <= c)
+    if (s.desc(mid).chunk0 <= c)
       lo = mid;
     else
       hi = mid;
@@ -172,23 +188,22 @@ __device__ __forceinline__ std::uint32_t find_desc(const PullBatch& b, std::uint
 // its own slice into the message's counter (target: chunks x warps), so the
 // CTA needs no barrier except where a plan's ready flag must be awaited.
 // Messages without a completion flag (copies ordered by the stream alone)
-// skip the counting and its fence.
-//
-// One instantiation per unit size U (U == 0: the 64-bit-stride walk for wide
-// layouts): a single kernel holding every unit's copy loop needs more than
-// 80 registers, one loop alone fits the 64 that four CTAs per SM allow.
-template <int U>
-__global__ void __launch_bounds__(kThreads, 4) pull_kernel(const __grid_constant__ PullBatch b) {
+// skip the counting and its fence. A descriptor of zero units is a pure
+// signal: its message's flag is stored once the launch reaches it.
+template <int U, class S>
+__device__ __forceinline__ void pull_body(const S& s) {
   __shared__ int skip;
   constexpr std::uint32_t kWarps = kThreads / 32;
   constexpr std::uint32_t kFailBit = 0x80000000u;
   const std::uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-  for (std::uint32_t c = blockIdx.x; c < b.total_chunks; c += gridDim.x) {
-    const PullDesc& d = b.d[find_desc(b, c)];
+  const std::uint64_t epoch = s.epoch();
+  for (std::uint32_t c = blockIdx.x; c < s.total(); c += gridDim.x) {
+    const PullDesc& d = s.desc(find_desc(s, c));
     const std::uint32_t u0 = (c - d.chunk0) * kChunkUnits;
     bool failed = false;
     if (d.ready != nullptr) {  // persistent plan: wait for the sender's data
-      if (threadIdx.x == 0) skip = wait_ready(d, b) ? 0 : 1;
+      if (threadIdx.x == 0)
+        skip = wait_ready(d.ready, epoch ? epoch : d.ready_val, s.status(), s.timeout_ns()) ? 0 : 1;
       __syncthreads();
       failed = skip != 0;
       __syncthreads();  // every thread read `skip` before it is rewritten
@@ -202,22 +217,32 @@ __global__ void __launch_bounds__(kThreads, 4) pull_kernel(const __grid_constant
       copy_units_wide(d, wlo, whi);
     else
       copy_units<U>(d, wlo, whi);
-    if (d.done == nullptr) continue;
+    std::uint64_t* done = d.done;
+    if (done == nullptr) continue;
     __syncwarp();  // every load of this warp's slice has returned
     if (lane == 0) {
+      std::uint32_t* counter = s.counters() + d.counter_idx;
       fence_acq_rel_gpu();  // with the relaxed add below: a release of the slice
-      if (failed) atomicOr(&b.counters[d.counter_idx], kFailBit);
-      std::uint32_t prev = atomicAdd(&b.counters[d.counter_idx], 1u);
+      if (failed) atomicOr(counter, kFailBit);
+      std::uint32_t prev = atomicAdd(counter, 1u);
       if ((prev & ~kFailBit) + 1 == d.msg_chunks * kWarps) {
         const bool any_failed = failed || (prev & kFailBit) != 0u;
-        b.counters[d.counter_idx] = 0u;
-        if (d.done != nullptr && !any_failed) {
+        *counter = 0u;
+        if (!any_failed) {
           fence_acq_rel_sys();
-          st_release_sys(d.done, d.done_val);
+          st_release_sys(done, epoch ? epoch : d.done_val);
         }
       }
     }
   }
+}
+
+// One instantiation per unit size U (U == 0: the 64-bit-stride walk for wide
+// layouts): a single kernel holding every unit's copy loop needs more than
+// 80 registers, one loop alone fits the 64 that four CTAs per SM allow.
+template <int U>
+__global__ void __launch_bounds__(kThreads, 4) pull_kernel(const __grid_constant__ PullBatch b) {
+  pull_body<U>(InlineSrc{b});
 }
 
 // Store each flag with release semantics at system scope (after everything
@@ -234,17 +259,20 @@ __global__ void signal_many_kernel(const __grid_constant__ SignalBatch b) {
 __global__ void wait_kernel(const __grid_constant__ WaitBatch b) {
   const std::uint32_t i = threadIdx.x;
   if (i >= b.n) return;
+  const std::uint64_t want = b.epoch ? *b.epoch : b.val[i];
   const std::uint64_t t0 = globaltimer_ns();
   std::uint32_t spins = 0;
-  while (ld_acquire_sys(b.flag[i]) < b.val[i]) {
+  while (ld_acquire_sys(b.flag[i]) < want) {
     if ((++spins & 63u) == 0u && globaltimer_ns() - t0 > b.timeout_ns) {
       report_status(b.status, kStatusWaitTimeout, reinterpret_cast<unsigned long long>(b.flag[i]),
-                    b.val[i], ld_acquire_sys(b.flag[i]));
+                    want, ld_acquire_sys(b.flag[i]));
       return;
     }
     __nanosleep(128);
   }
 }
+
+__global__ void epoch_bump_kernel(std::uint64_t* epoch) { *epoch += 1; }
 
 __global__ void signal_kernel(std::uint64_t* flag, std::uint64_t val) {
   fence_acq_rel_sys();
@@ -254,8 +282,6 @@ __global__ void signal_kernel(std::uint64_t* flag, std::uint64_t val) {
 }  // namespace
 
 namespace {
-
-int unit_class(const PullDesc& d) { return d.wide ? 0 : static_cast<int>(d.unit); }
 
 cudaError_t launch_class(int cls, const PullBatch& b, int max_ctas, cudaStream_t s) {
   const int grid =
@@ -285,15 +311,20 @@ cudaError_t launch_class(int cls, const PullBatch& b, int max_ctas, cudaStream_t
 
 }  // namespace
 
+cudaError_t launch_epoch_bump(std::uint64_t* epoch, cudaStream_t s) {
+  epoch_bump_kernel<<<1, 1, 0, s>>>(epoch);
+  return cudaGetLastError();
+}
+
 // A batch whose descriptors share one unit class is one launch; a mixed batch
 // becomes one launch per class, in order on the stream (completion counters
 // count warps across all of them, so a message may span launches).
 cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStream_t s, int* launches) {
   (void)threads;
   if (b.n == 0 || b.total_chunks == 0) return cudaSuccess;
-  const int first = unit_class(b.d[0]);
+  const int first = pull_unit_class(b.d[0]);
   bool same = true;
-  for (std::uint32_t i = 1; same && i < b.n; ++i) same = unit_class(b.d[i]) == first;
+  for (std::uint32_t i = 1; same && i < b.n; ++i) same = pull_unit_class(b.d[i]) == first;
   if (same) {
     if (launches != nullptr) ++*launches;
     return launch_class(first, b, max_ctas, s);
@@ -302,11 +333,12 @@ cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStrea
   sub.counters = b.counters;
   sub.status = b.status;
   sub.timeout_ns = b.timeout_ns;
+  sub.epoch = b.epoch;
   for (int cls : {16, 8, 4, 2, 1, 0}) {
     sub.n = 0;
     sub.total_chunks = 0;
     for (std::uint32_t i = 0; i < b.n; ++i) {
-      if (unit_class(b.d[i]) != cls) continue;
+      if (pull_unit_class(b.d[i]) != cls) continue;
       PullDesc x = b.d[i];
       x.chunk0 = sub.total_chunks;
       sub.total_chunks += x.nchunks;

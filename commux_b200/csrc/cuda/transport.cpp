@@ -7,6 +7,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <map>
 #include <cstdio>
 #include <cstring>
 #include <sstream>
@@ -242,6 +243,23 @@ std::int64_t numel_wire(const SegWire& s) {
   std::int64_t n = 1;
   for (int k = 0; k < s.ndim; ++k) n *= s.sizes[k];
   return n;
+}
+
+// Narrow rows (a halo x-face: 16-byte runs at a row pitch) cross NVLink far
+// below its bandwidth when a peer reads them one by one; such a send is
+// packed into a contiguous staging buffer on its own GPU first, and the
+// receiver reads that buffer.
+constexpr std::int64_t kPackRunBytes = 512;
+
+bool narrow_rows(const at::Tensor& t) {
+  if (t.numel() == 0 || t.dim() > kWireDims) return false;
+  std::vector<std::int64_t> sz(t.sizes().begin(), t.sizes().end()), sd(t.strides().begin(), t.strides().end());
+  auto d = dims_of(sz.data(), sd.data(), t.dim());
+  std::vector<Dim> m;
+  if (!refine(d, d, m) || m.empty()) return false;
+  const Dim& in = m.back();
+  const std::int64_t run = (in.ss == 1 ? in.size : 1) * static_cast<std::int64_t>(t.element_size());
+  return run < kPackRunBytes;
 }
 
 }  // namespace
@@ -485,12 +503,20 @@ void CudaTransport::prepare_send(const ReqPtr& s, int dst, std::vector<char>& bl
   st->stream = current_stream(dev);
   st->local = dst == eng_->rank();
 
+  // peer on another GPU (known once it published its device): narrow-row
+  // views are packed here so the receiver's NVLink reads are contiguous
+  bool peer_other_gpu = false;
+  if (!st->local) {
+    const auto* ph = eng_->peer_header(dst);
+    bool known = ph->cuda_uuid_valid.load(std::memory_order_acquire) != 0;
+    peer_other_gpu = known && std::memcmp(ph->cuda_uuid, c->uuid, 16) != 0;
+  }
   std::vector<at::Tensor> wire_t;
   for (auto& t : s->tensors) {
     // The receiver's copy kernel walks at most kMaxPullDims dims: stage a
     // contiguous copy (on this stream, before the ready event) when the
     // view's own dims do not merge down that far.
-    bool ok = t.dim() <= kWireDims;
+    bool ok = t.dim() <= kWireDims && !(peer_other_gpu && narrow_rows(t));
     for (int k = 0; ok && k < t.dim(); ++k) ok = t.stride(k) >= 0;
     if (ok) {
       std::vector<std::int64_t> sz(t.sizes().begin(), t.sizes().end());
@@ -1116,13 +1142,68 @@ class CudaPlan final : public DevicePlan {
     const std::uint64_t* ready_local = nullptr;  // recv: set by the sender
     std::vector<PullDesc> descs;              // recv (local/device)
     bool matched = false;                     // self recv paired with a send
+    at::Tensor stage;                         // send: packed copy the receiver reads
+    std::vector<PullDesc> pack;               // send: view -> stage
   };
 
   CudaPlan(CudaTransport* tr, Engine* eng, DevCtx* c) : tr_(tr), eng_(eng), c_(c) {}
+  ~CudaPlan() override {
+    if (!select_device_quiet(c_->dev)) return;  // context gone at process exit
+    if (exec_) cudaGraphExecDestroy(exec_);
+    if (graph_) cudaGraphDestroy(graph_);
+    cudaGetLastError();
+  }
   std::vector<Msg> sends, recvs;
 
+  // Builds the launches every start() replays: (1) pack + "ready" signals of
+  // the sends to other GPUs, (2) the pulls of every receive, (3) the wait for
+  // the receivers' "consumed" flags, (4) the epoch bump. Every flag value is
+  // the plan's epoch, read from device memory, so the launches never change:
+  // they are captured once into a CUDA graph and a start is one graph launch.
+  void finalize() {
+    std::vector<std::vector<PullDesc>> pre, pull;
+    for (auto& m : sends) {
+      if (m.mode != PlanMode::Device) continue;
+      std::vector<PullDesc> d = m.pack;
+      if (d.empty()) {  // a pure signal: zero units, the flag store only
+        PullDesc x{};
+        x.ndim = 1;
+        x.unit = 16;
+        x.units = 0;
+        x.nchunks = 1;
+        d.push_back(x);
+      }
+      for (auto& x : d) x.done = m.ready_remote;
+      pre.push_back(std::move(d));
+    }
+    for (auto& m : recvs)
+      if (m.mode != PlanMode::Shared && !m.descs.empty()) pull.push_back(m.descs);
+    // device state: [epoch u64, starts at 1][counters u32 x kCounterSlots]
+    const std::size_t state_bytes = 64 + kCounterSlots * sizeof(std::uint32_t);
+    state_ = at::empty({static_cast<std::int64_t>(state_bytes)},
+                       at::TensorOptions().dtype(at::kByte).device(at::kCUDA, c_->dev));
+    epoch_d_ = reinterpret_cast<std::uint64_t*>(state_.data_ptr());
+    counters_d_ = reinterpret_cast<std::uint32_t*>(static_cast<char*>(state_.data_ptr()) + 64);
+    std::vector<char> init(state_bytes, 0);
+    const std::uint64_t one = 1;
+    std::memcpy(init.data(), &one, sizeof(one));
+    CMX_CUDA(cudaMemcpy(state_.data_ptr(), init.data(), state_bytes, cudaMemcpyHostToDevice));
+    pre_ = batches(pre);
+    pulls_ = batches(pull);
+    std::memset(&wait_, 0, sizeof(wait_));
+    wait_.timeout_ns = tr_->device_timeout_ns();
+    wait_.status = c_->status_d;
+    wait_.epoch = epoch_d_;
+    for (auto& m : sends)
+      if (m.mode == PlanMode::Device) {
+        TORCH_CHECK(wait_.n < static_cast<std::uint32_t>(kMaxWaitFlags), "commux plan: more than ",
+                    kMaxWaitFlags, " sends to other GPUs");
+        wait_.flag[wait_.n++] = m.consumed_local;
+      }
+  }
+
   void start() override {
-    ++epoch_;
+    ++starts_;
     c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(c_->dev));
     cudaStream_t cur = c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(c_->dev)).stream();
     // messages to/from a rank on this same GPU go through the host-gated path
@@ -1142,56 +1223,9 @@ class CudaPlan final : public DevicePlan {
       }
       tr_->end_batch();
     }
-    // 1. tell every receiver on another GPU that this rank's data is ready
-    SignalBatch sb;
-    std::memset(&sb, 0, sizeof(sb));
-    for (auto& m : sends) {
-      if (m.mode != PlanMode::Device) continue;
-      if (sb.n == static_cast<std::uint32_t>(kMaxSignal)) {
-        CMX_CUDA(launch_signal_many(sb, cur));
-        tr_->kernel_launches++;
-        sb.n = 0;
-      }
-      sb.flag[sb.n] = m.ready_remote;
-      sb.val[sb.n++] = epoch_;
-    }
-    if (sb.n) {
-      CMX_CUDA(launch_signal_many(sb, cur));
-      tr_->kernel_launches++;
-    }
-    // 2. one pull launch for every receive (waits on the peers' ready flags)
-    std::vector<std::vector<PullDesc>> msgs;
-    for (auto& m : recvs) {
-      if (m.mode == PlanMode::Shared) continue;
-      std::vector<PullDesc> d = m.descs;
-      for (auto& x : d) {
-        if (m.mode == PlanMode::Device) {
-          x.ready_val = epoch_;
-          x.done_val = epoch_;
-        }
-      }
-      msgs.push_back(std::move(d));
-    }
-    if (!msgs.empty()) tr_->launch_plan_pulls(c_, msgs, cur);
-    // 3. the stream continues once every receiver consumed this rank's data
-    WaitBatch wb;
-    std::memset(&wb, 0, sizeof(wb));
-    wb.timeout_ns = tr_->device_timeout_ns();
-    wb.status = c_->status_d;
-    for (auto& m : sends) {
-      if (m.mode != PlanMode::Device) continue;
-      if (wb.n == static_cast<std::uint32_t>(kMaxWaitFlags)) {
-        CMX_CUDA(launch_wait(wb, cur));
-        tr_->kernel_launches++;
-        wb.n = 0;
-      }
-      wb.flag[wb.n] = m.consumed_local;
-      wb.val[wb.n++] = epoch_;
-    }
-    if (wb.n) {
-      CMX_CUDA(launch_wait(wb, cur));
-      tr_->kernel_launches++;
-    }
+    if (!exec_) capture();
+    CMX_CUDA(cudaGraphLaunch(exec_, cur));
+    tr_->kernel_launches += nodes_;
     if (!shared.empty()) {
       for (auto& r : shared) eng_->wait(r, std::chrono::milliseconds(0));
       tr_->stream_wait_all(shared);
@@ -1201,55 +1235,107 @@ class CudaPlan final : public DevicePlan {
   }
 
   std::vector<std::pair<std::string, std::int64_t>> info() override {
-    std::int64_t loc = 0, dev = 0;
+    std::int64_t loc = 0, dev = 0, packed = 0;
     for (auto* v : {&sends, &recvs})
       for (auto& m : *v) (m.mode == PlanMode::Local ? loc : dev) += m.mode != PlanMode::Shared;
-    return {{"local", loc}, {"device", dev}, {"shared", n_shared_}, {"starts", static_cast<std::int64_t>(epoch_)}};
+    for (auto& m : sends) packed += (m.mode == PlanMode::Device && !m.pack.empty()) ? 1 : 0;
+    return {{"local", loc},      {"device", dev},       {"shared", n_shared_}, {"packed_sends", packed},
+            {"graph_nodes", nodes_}, {"starts", static_cast<std::int64_t>(starts_)}};
   }
 
   std::int64_t n_shared_ = 0;
 
  private:
+  // Messages -> parameter blocks of at most kMaxBatch descriptors, one unit
+  // class each; every message counts into its own counter slot (the plan's
+  // launches run one after another and each message returns its counter to
+  // zero, so the slots are reused by the next start).
+  std::vector<std::unique_ptr<PullBatch>> batches(const std::vector<std::vector<PullDesc>>& msgs) {
+    std::map<int, std::vector<PullDesc>> by_cls;
+    std::uint32_t slot = 0;
+    for (auto& m : msgs) {
+      if (m.empty()) continue;
+      const int cls = pull_unit_class(m[0]);
+      std::uint32_t chunks = 0;
+      for (auto& d : m) {
+        TORCH_CHECK(pull_unit_class(d) == cls, "commux plan: a message mixes unit classes");
+        chunks += d.nchunks;
+      }
+      TORCH_CHECK(slot < kCounterSlots, "commux plan: too many messages");
+      auto& v = by_cls[cls];
+      for (auto d : m) {
+        d.counter_idx = slot;
+        d.msg_chunks = chunks;
+        v.push_back(d);
+      }
+      ++slot;
+    }
+    std::vector<std::unique_ptr<PullBatch>> out;
+    for (auto& kv : by_cls) {
+      std::size_t i = 0;
+      while (i < kv.second.size()) {
+        auto b = std::make_unique<PullBatch>();
+        b->n = 0;
+        b->total_chunks = 0;
+        b->counters = counters_d_;
+        b->status = c_->status_d;
+        b->timeout_ns = tr_->device_timeout_ns();
+        b->epoch = epoch_d_;
+        while (i < kv.second.size() && b->n < static_cast<std::uint32_t>(kMaxBatch)) {
+          PullDesc d = kv.second[i++];
+          d.chunk0 = b->total_chunks;
+          b->total_chunks += d.nchunks;
+          b->d[b->n++] = d;
+        }
+        out.push_back(std::move(b));
+      }
+    }
+    return out;
+  }
+
+  void capture() {
+    cudaStream_t cs = nullptr;
+    CMX_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+    const int ctas = tr_->pull_ctas(c_);
+    nodes_ = 0;
+    CMX_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+    cudaError_t e = cudaSuccess;
+    for (auto* ls : {&pre_, &pulls_})
+      for (auto& b : *ls) {
+        int launched = 0;
+        if (e == cudaSuccess) e = launch_pull(*b, ctas, 256, cs, &launched);
+        nodes_ += launched;
+      }
+    if (e == cudaSuccess && wait_.n) {
+      e = launch_wait(wait_, cs);
+      ++nodes_;
+    }
+    if (e == cudaSuccess) {
+      e = launch_epoch_bump(epoch_d_, cs);
+      ++nodes_;
+    }
+    cudaGraph_t g = nullptr;
+    cudaError_t e2 = cudaStreamEndCapture(cs, &g);
+    cudaStreamDestroy(cs);  // holds no tensors: safe to destroy
+    CMX_CUDA(e);
+    CMX_CUDA(e2);
+    graph_ = g;
+    CMX_CUDA(cudaGraphInstantiate(&exec_, graph_, 0));
+  }
+
   CudaTransport* tr_;
   Engine* eng_;
   DevCtx* c_;
-  std::uint64_t epoch_ = 0;
+  std::uint64_t starts_ = 0;
+  at::Tensor state_;
+  std::uint64_t* epoch_d_ = nullptr;
+  std::uint32_t* counters_d_ = nullptr;
+  std::vector<std::unique_ptr<PullBatch>> pre_, pulls_;
+  WaitBatch wait_{};
+  cudaGraph_t graph_ = nullptr;
+  cudaGraphExec_t exec_ = nullptr;
+  std::int64_t nodes_ = 0;
 };
-
-void CudaTransport::launch_plan_pulls(DevCtx* c, const std::vector<std::vector<PullDesc>>& msgs,
-                                      cudaStream_t stream) {
-  std::uint32_t* counters = c->scratch(stream);
-  std::uint32_t first = c->take_slots(stream, static_cast<std::uint32_t>(msgs.size()));
-  PullBatch b;
-  std::memset(&b, 0, sizeof(b));
-  b.counters = counters;
-  b.status = c->status_d;
-  b.timeout_ns = timeout_ns_;
-  const int ctas = pull_ctas(c);
-  auto flush = [&]() {
-    if (b.n == 0) return;
-    int launched = 0;
-    CMX_CUDA(launch_pull(b, ctas, 256, stream, &launched));
-    kernel_launches += launched;
-    b.n = 0;
-    b.total_chunks = 0;
-  };
-  for (std::size_t i = 0; i < msgs.size(); ++i) {
-    std::uint32_t slot = (first + static_cast<std::uint32_t>(i)) % kCounterSlots;
-    std::uint32_t chunks = 0;
-    for (auto& d : msgs[i]) chunks += d.nchunks;
-    for (const auto& d0 : msgs[i]) {
-      if (b.n == static_cast<std::uint32_t>(kMaxBatch)) flush();
-      PullDesc d = d0;
-      d.chunk0 = b.total_chunks;
-      d.counter_idx = slot;
-      d.msg_chunks = chunks;
-      b.d[b.n++] = d;
-      b.total_chunks += d.nchunks;
-    }
-  }
-  flush();
-}
 
 std::vector<PullDesc> CudaTransport::plan_descs(const char* wire, std::size_t len, int src, bool local,
                                                 const at::Tensor& dst, DevCtx* c) {
@@ -1359,7 +1445,17 @@ DevicePlanPtr CudaTransport::create_plan(const std::vector<at::Tensor>& recv_t, 
     } else {
       std::uint64_t slot = plan_slot();
       m.consumed_local = c->mbox + slot;
-      auto blob = wire_of(m.t, false, slot);
+      // narrow rows: the receiver reads a contiguous copy packed here (the
+      // pack descriptors run in the plan's first launch; a receiver that
+      // turns out to share this GPU reads the view itself)
+      at::Tensor wire_src = m.t;
+      if (narrow_rows(m.t)) {
+        m.stage = at::empty(m.t.sizes(), m.t.options().memory_format(at::MemoryFormat::Contiguous));
+        auto self_blob = wire_of(m.t, true, 0);
+        m.pack = plan_descs(self_blob.data(), self_blob.size(), me, true, m.stage, c);
+        wire_src = m.stage;
+      }
+      auto blob = wire_of(wire_src, false, slot);
       pending_sends.push_back(eng_->post_send({bytes_tensor(blob.data(), blob.size())}, m.peer,
                                               make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), kPlanSub, true)));
       at::Tensor rb = at::empty({static_cast<std::int64_t>(sizeof(PlanReply))}, at::TensorOptions().dtype(at::kByte));
@@ -1448,6 +1544,7 @@ DevicePlanPtr CudaTransport::create_plan(const std::vector<at::Tensor>& recv_t, 
     }
   }
   for (auto& s : pending_sends) eng_->wait(s, std::chrono::milliseconds(0));
+  plan->finalize();
   return plan;
 }
 

@@ -171,7 +171,6 @@ class CudaTransport final : public DeviceTransport {
                             const std::vector<int>& recv_tag, const std::vector<at::Tensor>& send_t,
                             const std::vector<int>& send_peer, const std::vector<int>& send_tag) override;
   // pull launch(es) of prebuilt per-message descriptors on `stream` (plans)
-  void launch_plan_pulls(DevCtx* c, const std::vector<std::vector<PullDesc>>& msgs, cudaStream_t stream);
   // descriptors of one message from its wire description (plans)
   std::vector<PullDesc> plan_descs(const char* wire, std::size_t len, int src, bool local,
                                    const at::Tensor& dst, DevCtx* c);

@@ -72,7 +72,7 @@ def test_collectives_cuda():
     check(run("collectives.py", 2, env=dict(CUDA, CMX_A2A="1"), timeout=240))
 
 
-@pytest.mark.parametrize("variant", ["default", "nvls", "p2p"])
+@pytest.mark.parametrize("variant", ["default", "nvls", "p2p", "twoshot"])
 def test_collective_numerics_cuda(variant):
     # every rank on its own GPU where there are enough (NVLS and peer kernels),
     # else ranks share GPUs (host-staged path); "nvls" forces the multicast
@@ -83,6 +83,8 @@ def test_collective_numerics_cuda(variant):
         env.update(COMMUX_NVLS_MIN_RANKS="2", COMMUX_NVLS_MIN_BYTES="0")
     elif variant == "p2p":
         env.update(COMMUX_NVLS="0")
+    elif variant == "twoshot":
+        env.update(COMMUX_NVLS="0", COMMUX_ALGO="twoshot")
     check(run("gpu_coll_numerics.py", world, env=env, timeout=600))
 
 
