@@ -6,8 +6,9 @@ SUM/MAX/AVG, on every GPU of the launch (torchrun --nproc-per-node N). Each
 point is timed with CUDA events on the caller's stream (max over ranks, after
 warm-up, inputs re-used: sizes above the 126 MB L2 stream from HBM) and
 reported as algorithm bandwidth and bus bandwidth (allreduce: 2(P-1)/P x size
-/ time; reduce/broadcast: size / time). NCCL runs in the same process on a
-second process group as the comparator.
+/ time; reduce/broadcast: size / time) and as the fraction of the NVLink
+roofline (bus bandwidth / 770 GB/s, the measured peer-copy rate per direction).
+NCCL runs in the same process on a second process group as the comparator.
 
     torchrun --nproc-per-node 8 benchmarks/collectives_sweep.py --max-bytes 1073741824
 """
@@ -100,6 +101,9 @@ def main():
                         busbw = algbw * (2 * (world - 1) / world if coll == "allreduce" else 1.0)
                         row[f"{gname}_us"] = round(ms * 1e3, 2)
                         row[f"{gname}_busbw_GBps"] = round(busbw, 2)
+                        # NVLink roofline: bus bandwidth against the measured
+                        # 770 GB/s per direction of one GPU's links
+                        row[f"{gname}_frac_of_nvlink"] = round(busbw / 770.0, 3)
                     if rank == 0:
                         print(json.dumps(row), flush=True)
                     results.append(row)

@@ -91,6 +91,11 @@ CollImpl::CollImpl(CudaTransport* tr, int dev)
   region_bytes_ = std::max<std::int64_t>(region_bytes_ & ~std::int64_t(4095), 1 << 20);
   // one-shot moves (P-1) x the message out of every rank but needs a single
   // flag round: it wins up to a few MB at 2 ranks, less as P grows
+  if (env_int("COMMUX_COLL_TRACE", 0) != 0) {
+    CMX_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&trace_h_),
+                           kTracePoints * kTraceChunks * sizeof(unsigned long long), cudaHostAllocMapped));
+    CMX_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&trace_d_), trace_h_, 0));
+  }
   oneshot_bytes_ = env_int("COMMUX_ONESHOT_BYTES", P_ <= 2 ? 4ll << 20 : P_ <= 4 ? 2ll << 20 : 1ll << 20);
   // COMMUX_ALGO=oneshot|twoshot|nvls forces an algorithm for the reductions
   // where it applies (the others keep the size-based choice)
@@ -171,8 +176,42 @@ CollImpl::CollImpl(CudaTransport* tr, int dev)
        forced_algo_ < 0 ? "auto" : forced_algo_ == kAlgoOneShot ? "oneshot" : forced_algo_ == kAlgoTwoShot ? "twoshot" : "nvls");
 }
 
+// COMMUX_COLL_TRACE=1: after each collective (synchronously), one line per
+// call with the phase durations of CTA 0, averaged over the chunks: push =
+// stores into peers' workspaces, sig = the flag store (waits for those
+// stores to land), wait = until every peer's flag arrived, fold, push2 =
+// folded segment out, wait2, out = copy-out.
+void CollImpl::report_trace(int algo, int mode, std::int64_t bytes, int ctas) {
+  CMX_CUDA(cudaStreamSynchronize(stream_));
+  const unsigned long long* t = trace_h_;
+  double sum[kTracePoints] = {0};
+  int nch = 0;
+  for (int c = 0; c < kTraceChunks; ++c) {
+    const unsigned long long* r = t + c * kTracePoints;
+    if (r[0] == 0) break;
+    for (int k = 1; k < kTracePoints; ++k)
+      if (r[k] != 0 && r[k - 1] != 0) sum[k] += static_cast<double>(r[k] - r[k - 1]) / 1000.0;
+    ++nch;
+  }
+  if (nch == 0) return;
+  double total = 0;
+  for (int c = nch - 1; c >= 0; --c) {
+    const unsigned long long* r = t + c * kTracePoints;
+    unsigned long long last = 0;
+    for (int k = kTracePoints - 1; k >= 0 && last == 0; --k) last = r[k];
+    total = static_cast<double>(last - t[0]) / 1000.0;
+    break;
+  }
+  std::fprintf(stderr,
+               "[commux trace rank %d] algo %d mode %d bytes %lld ctas %d chunks %d total %.1f us | per chunk: "
+               "push %.1f sig %.1f wait %.1f fold %.1f push2 %.1f wait2 %.1f out %.1f\n",
+               me_, algo, mode, static_cast<long long>(bytes), ctas, nch, total, sum[1] / nch, sum[2] / nch,
+               sum[3] / nch, sum[4] / nch, sum[5] / nch, sum[6] / nch, sum[7] / nch);
+}
+
 CollImpl::~CollImpl() {
   if (!select_device_quiet(dev_)) return;  // context gone at process exit
+  if (trace_h_) cudaFreeHost(trace_h_);
   if (stream_) cudaStreamSynchronize(stream_);
   nvls_.reset();
   for (int p = 0; p < P_; ++p)
@@ -185,13 +224,19 @@ CollImpl::~CollImpl() {
 int CollImpl::choose_ctas(int mode, int algo, std::int64_t bytes) const {
   static const std::int64_t forced = env_int("COMMUX_COLL_CTAS", 0);
   if (forced > 0) return static_cast<int>(std::min<std::int64_t>(forced, kMaxCollCtas));
-  const int cap = std::min(ctx_->sm_count, kMaxCollCtas);
+  // Every CTA of a launch must be resident at once (CTA b waits for CTA b of
+  // the peers): the copy kernels fit two 512-thread CTAs per SM (<= 64
+  // registers), the NVLS kernel one. Two per SM measured 8-10 % faster than
+  // one on large two-shot allreduces (1 GiB at 2 GPUs: 2.06 vs 2.23 ms).
+  const int one = std::min(ctx_->sm_count, kMaxCollCtas);
+  const int two = std::min(2 * ctx_->sm_count, kMaxCollCtas);
+  if (algo == kAlgoNvls) return one;
   if (mode == kModeAllreduce || mode == kModeReduce || mode == kModeReduceScatter) {
     if (algo == kAlgoOneShot)
-      return static_cast<int>(std::max<std::int64_t>(1, std::min<std::int64_t>(cap / 2, bytes / (16 << 10))));
-    return cap;
+      return static_cast<int>(std::max<std::int64_t>(1, std::min<std::int64_t>(one, bytes / (16 << 10))));
+    return two;
   }
-  return static_cast<int>(std::max<std::int64_t>(1, std::min<std::int64_t>(cap, bytes / (16 << 10))));
+  return static_cast<int>(std::max<std::int64_t>(1, std::min<std::int64_t>(two, bytes / (16 << 10))));
 }
 
 void CollImpl::fill(CollArgs& a, const Launch& l, const at::Tensor& in, const at::Tensor& out) {
@@ -216,6 +261,7 @@ void CollImpl::fill(CollArgs& a, const Launch& l, const at::Tensor& in, const at
   a.seq_base = epoch_ << 20;
   a.timeout_ns = tr_->device_timeout_ns();
   a.status = ctx_->status_d;
+  a.trace = trace_d_;
   if (nvls_) {
     a.nvls_uc = nvls_->uc();
     a.nvls_mc = nvls_->mc();
@@ -271,8 +317,10 @@ DevCollPtr CollImpl::run(const std::vector<Launch>& launches) {
       algo = kAlgoNvls;
     a.algo = algo;
     int ctas = choose_ctas(l.mode, algo, bytes);
+    if (trace_h_ != nullptr) std::memset(trace_h_, 0, kTracePoints * kTraceChunks * sizeof(unsigned long long));
     CMX_CUDA(launch_coll(a, ctas, stream_));
     tr_->kernel_launches++;
+    if (trace_h_ != nullptr) report_trace(algo, l.mode, bytes, ctas);
     st_calls_++;
     st_bytes_ += bytes;
     if (l.mode == kModeAllgather || l.mode == kModeBroadcast)

@@ -62,6 +62,9 @@ class CollImpl {
   std::string nvls_why_;              // why not (empty when enabled or not attempted)
   std::int64_t nvls_min_bytes_ = 0;
   int forced_algo_ = -1;  // COMMUX_ALGO
+  unsigned long long* trace_h_ = nullptr;  // COMMUX_COLL_TRACE (host-mapped)
+  unsigned long long* trace_d_ = nullptr;
+  void report_trace(int algo, int mode, std::int64_t bytes, int ctas);
   std::int64_t st_calls_ = 0, st_oneshot_ = 0, st_twoshot_ = 0, st_gather_ = 0, st_bytes_ = 0, st_nvls_ = 0;
 };
 

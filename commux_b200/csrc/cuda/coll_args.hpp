@@ -20,7 +20,7 @@ namespace commux {
 namespace cuda {
 
 constexpr int kMaxCollRanks = 16;
-constexpr int kMaxCollCtas = 256;
+constexpr int kMaxCollCtas = 512;
 constexpr int kFlagPhases = 4;
 constexpr std::size_t kFlagBytes =
     static_cast<std::size_t>(kFlagPhases) * kMaxCollRanks * kMaxCollCtas * sizeof(std::uint64_t);
@@ -62,7 +62,14 @@ struct CollArgs {
   char* nvls_mc;
   std::int64_t nvls_bytes;     // whole buffer
   std::int64_t nvls_half_off;  // bytes: 0 or nvls_bytes / 2
+  // COMMUX_COLL_TRACE: CTA 0 stamps %globaltimer at the phase boundaries of
+  // each chunk into trace[chunk * kTracePoints + point] (host-mapped);
+  // nullptr otherwise
+  unsigned long long* trace;
 };
+
+constexpr int kTracePoints = 8;
+constexpr int kTraceChunks = 64;
 
 // True when the NVLS kernel supports (dtype, op): SUM and AVG of
 // f32/f16/bf16, MIN and MAX of f16/bf16 (the multimem reductions NVSwitch

@@ -255,7 +255,7 @@ __device__ __forceinline__ std::int64_t slot_elems(const CollArgs& a, int nslots
 // ---- oneshot -------------------------------------------------------------------
 
 template <typename T, int OP>
-__global__ void __launch_bounds__(kCollThreads) oneshot_kernel(const __grid_constant__ CollArgs a) {
+__global__ void __launch_bounds__(kCollThreads, 2) oneshot_kernel(const __grid_constant__ CollArgs a) {
   const T* in = static_cast<const T*>(a.in);
   T* out = static_cast<T*>(a.out);
   std::int64_t lo, hi;
@@ -421,152 +421,84 @@ __device__ __forceinline__ std::int64_t pipe_chunk(std::int64_t seg, std::int64_
   return (c + N - 1) / N * N > slot_cap ? slot_cap : (c + N - 1) / N * N;
 }
 
-// ---- pipelined two-shot (allreduce / reduce / reduce_scatter) ---------------------
-//
-// Each call's half of regions A and B is cut into two chunk buffers (chunk c
-// uses buffer c & 1). Flag phases, per chunk: 0 = my parts of the chunk are in
-// your A, 1 = my folded segment is in your B (also: my fold of the chunk is
-// done, so your A buffer may be refilled), 2 = I copied the chunk out of my B
-// (your B buffer may be refilled).
-//   link group:  push parts of chunk 0; then per chunk c: [wait 1(c-1)] push
-//                parts of c+1 -> signal 0(c+1) -> wait own fold(c) ->
-//                [wait 2(c-2)] push folded c -> signal 1(c)
-//   local group: wait 0(c) -> fold -> publish fold(c) -> [wait 1(c-1) ->
-//                copy-out c-1 -> signal 2(c-1)]; after the last chunk, the
-//                copy-out of the last one.
+// ---- twoshot (phases in sequence per CTA) -------------------------------------------------------------------
+
+// Phase stamp of CTA 0 (COMMUX_COLL_TRACE): point k of chunk c.
+__device__ __forceinline__ void stamp(const CollArgs& a, std::int64_t c, int k) {
+  if (a.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0 && c < kTraceChunks)
+    a.trace[c * kTracePoints + k] = globaltimer_ns();
+}
+
 template <typename T, int OP>
-__global__ void __launch_bounds__(kCollThreads, 1) twoshot_pipe_kernel(const __grid_constant__ CollArgs a) {
+__global__ void __launch_bounds__(kCollThreads, 2) twoshot_kernel(const __grid_constant__ CollArgs a) {
   constexpr int N = Packs<T>::N;
-  __shared__ PipeShared sh;
-  if (threadIdx.x == 0) {
-    sh.fail[0] = sh.fail[1] = 0;
-    sh.decision[0] = sh.decision[1] = 0;
-    sh.folded = 0;
-  }
-  __syncthreads();
   const T* in = static_cast<const T*>(a.in);
   T* out = static_cast<T*>(a.out);
   const int P = a.P;
   const bool rs = a.mode == kModeReduceScatter;
+  const std::int64_t seg_cap = slot_elems<T>(a, P);
   const std::int64_t total = rs ? a.n * P : a.n;
+  // segment s of the tensor: [s*seg, s*seg + seg) (reduce_scatter: block s)
   const std::int64_t seg = rs ? a.n : (((total + P - 1) / P + N - 1) / N) * N;
-  // slot of one rank in one chunk buffer: a quarter of the region, P slots
-  const std::int64_t slot_cap = ((a.region_bytes / 4) / static_cast<std::int64_t>(sizeof(T)) / P) / N * N;
-  const std::int64_t cap = pipe_chunk<T>(seg, slot_cap);
-  const std::int64_t nchunks = (seg + cap - 1) / cap;
-  const bool to_out = rs || a.mode == kModeAllreduce || a.me == a.root;
-  const Grp link{1, 0, kCollThreads / 2}, local{2, kCollThreads / 2, kCollThreads / 2};
-  const bool is_link = static_cast<int>(threadIdx.x) < kCollThreads / 2;
-  auto abuf = [&](int p, std::int64_t c) {
-    return region_a<T>(a, p) + ((c & 1) ? (a.region_bytes / 4) / static_cast<std::int64_t>(sizeof(T)) : 0);
-  };
-  auto bbuf = [&](int p, std::int64_t c) {
-    return region_b<T>(a, p) + ((c & 1) ? (a.region_bytes / 4) / static_cast<std::int64_t>(sizeof(T)) : 0);
-  };
-  const std::int64_t mine = static_cast<std::int64_t>(a.me) * seg;
-  if (is_link) {
-    // push my parts of chunk c into every peer's A buffer c&1
-    auto push_parts = [&](std::int64_t c) -> bool {
-      const std::int64_t s0 = c * cap, slen = min(cap, seg - s0);
-      std::int64_t lo, hi;
-      piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
-      const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
-      // the buffer is free once every rank folded chunk c-2
-      if (c >= 2 && !gawait(a, link, sh, 0, 1, seq - 2)) return false;
-      for (int q = 1; q < P; ++q) {
-        const int s = (a.me + q) % P;
-        const std::int64_t g = static_cast<std::int64_t>(s) * seg + s0;
-        const std::int64_t ghi = rs ? g + hi : min(g + hi, total);
-        gcopy(link, abuf(s, c) + a.me * cap - g, in, g + lo, ghi);
-      }
-      gsignal(a, link, 0, seq);
-      return true;
-    };
-    if (nchunks > 0 && !push_parts(0)) return;
-    for (std::int64_t c = 0; c < nchunks; ++c) {
-      // chunk c+1 crosses NVLink while the local group folds chunk c
-      if (c + 1 < nchunks && !push_parts(c + 1)) return;
-      if (rs) continue;
-      const std::int64_t s0 = c * cap, slen = min(cap, seg - s0);
-      std::int64_t lo, hi;
-      piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
-      const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
-      // my fold of chunk c (local group) before its result goes out
-      if (link.tid() == 0) {
-        const std::uint64_t t0 = globaltimer_ns();
-        int ok = 1;
-        while (sh.folded < c + 1) {
-          if (sh.fail[1] != 0 || globaltimer_ns() - t0 > a.timeout_ns) {
-            ok = 0;
-            break;
-          }
-          __nanosleep(32);
-        }
-        __threadfence_block();
-        sh.decision[0] = ok;
-      }
-      link.sync();
-      if (sh.decision[0] == 0) {
-        if (link.tid() == 0) sh.fail[0] = 1;
-        return;
-      }
-      // B buffer c&1 of every rank is free once it copied chunk c-2 out
-      if (c >= 2 && !gawait(a, link, sh, 0, 2, seq - 2)) return;
-      const T* folded = to_out ? out + mine + s0 : bbuf(a.me, c) + a.me * cap;
-      const std::int64_t mhi = min(hi, total - mine - s0);
+  const std::int64_t nchunks = (seg + seg_cap - 1) / seg_cap;
+  T* a_me = region_a<T>(a, a.me);
+  T* b_me = region_b<T>(a, a.me);
+  for (std::int64_t c = 0; c < nchunks; ++c) {
+    const std::int64_t s0 = c * seg_cap;
+    const std::int64_t slen = min(seg_cap, seg - s0);
+    std::int64_t lo, hi;
+    piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
+    const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
+    stamp(a, c, 0);
+    // phase 0: my part of segment s -> slot[me] of rank s's A (my own
+    // segment's part stays in `in` and is read from there by the fold)
+    for (int q = 1; q < P; ++q) {
+      const int s = (a.me + q) % P;
+      const std::int64_t g = static_cast<std::int64_t>(s) * seg + s0;
+      const std::int64_t ghi = rs ? g + hi : min(g + hi, total);
+      copy_range(region_a<T>(a, s) + a.me * seg_cap - g, in, g + lo, ghi);
+    }
+    stamp(a, c, 1);
+    signal(a, 0, seq);
+    stamp(a, c, 2);
+    if (!await(a, 0, seq)) return;
+    stamp(a, c, 3);
+    // fold my segment: reduce_scatter and allreduce write it straight into
+    // `out` (allreduce then pushes it from there), reduce into my B slot
+    const std::int64_t mine = static_cast<std::int64_t>(a.me) * seg + s0;
+    const std::int64_t mhi = rs ? hi : min(hi, total - mine);
+    const bool to_out = rs || a.mode == kModeAllreduce || a.me == a.root;
+    T* folded = to_out ? (rs ? out + s0 : out + mine) : b_me + a.me * seg_cap;
+    gfold<T, OP>(Grp{0, 0, static_cast<int>(blockDim.x)}, folded, a_me, seg_cap, P, a.me, in + mine, lo, mhi);
+    stamp(a, c, 4);
+    if (!rs) {
+      __syncthreads();
+      // phase 1: my folded segment -> slot[me] of B on every rank that needs it
       for (int q = 1; q < P; ++q) {
         const int p = (a.me + q) % P;
         if (a.mode == kModeReduce && p != a.root) continue;
-        gcopy(link, bbuf(p, c) + a.me * cap, folded, lo, mhi);
+        copy_range(region_b<T>(a, p) + a.me * seg_cap, folded, lo, mhi);
       }
-      gsignal(a, link, 1, seq);
     }
-  } else {
-    auto copy_out = [&](std::int64_t c) -> bool {
-      const std::int64_t s0 = c * cap, slen = min(cap, seg - s0);
-      std::int64_t lo, hi;
-      piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
-      const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
-      if (!gawait(a, local, sh, 1, 1, seq)) return false;
-      if (!(a.mode == kModeReduce && a.me != a.root)) {
-        for (int p = 0; p < P; ++p) {
-          if (p == a.me) continue;
-          const std::int64_t g = static_cast<std::int64_t>(p) * seg + s0;
-          gcopy(local, out + g, bbuf(a.me, c) + p * cap, lo, min(hi, total - g));
-        }
-      }
-      gsignal(a, local, 2, seq);
-      return true;
-    };
-    for (std::int64_t c = 0; c < nchunks; ++c) {
-      const std::int64_t s0 = c * cap, slen = min(cap, seg - s0);
-      std::int64_t lo, hi;
-      piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
-      const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
-      if (!gawait(a, local, sh, 1, 0, seq)) return;
-      const std::int64_t mhi = rs ? hi : min(hi, total - mine - s0);
-      T* folded = rs ? out + s0 : (to_out ? out + mine + s0 : bbuf(a.me, c) + a.me * cap);
-      gfold<T, OP>(local, folded, abuf(a.me, c), cap, P, a.me, in + mine + s0, lo, mhi);
-      if (rs) {
-        // the fold is the whole job; phase 1 still tells peers my A buffer is free
-        gsignal(a, local, 1, seq);
-        continue;
-      }
-      local.sync();
-      if (local.tid() == 0) {
-        __threadfence_block();
-        sh.folded = c + 1;
-      }
-      if (c >= 1 && !copy_out(c - 1)) return;
+    stamp(a, c, 5);
+    signal(a, 1, seq);
+    if (!await(a, 1, seq)) return;
+    stamp(a, c, 6);
+    if (rs || (a.mode == kModeReduce && a.me != a.root)) continue;
+    for (int p = 0; p < P; ++p) {
+      if (p == a.me) continue;  // folded in place above
+      const std::int64_t g = static_cast<std::int64_t>(p) * seg + s0;
+      const std::int64_t phi = min(hi, total - g);
+      copy_range(out + g, b_me + p * seg_cap - 0, lo, phi);
     }
-    if (!rs && nchunks >= 1) copy_out(nchunks - 1);
+    stamp(a, c, 7);
   }
 }
 
 // ---- gather (allgather / broadcast) ------------------------------------------
 
 template <typename T>
-__global__ void __launch_bounds__(kCollThreads) gather_kernel(const __grid_constant__ CollArgs a) {
+__global__ void __launch_bounds__(kCollThreads, 2) gather_kernel(const __grid_constant__ CollArgs a) {
   const T* in = static_cast<const T*>(a.in);
   T* out = static_cast<T*>(a.out);
   const int P = a.P;
@@ -824,7 +756,7 @@ cudaError_t launch_reduce_family(const CollArgs& a, int ctas, cudaStream_t s) {
   if (a.algo == kAlgoOneShot)
     oneshot_kernel<T, OP><<<ctas, kCollThreads, 0, s>>>(a);
   else
-    twoshot_pipe_kernel<T, OP><<<ctas, kCollThreads, 0, s>>>(a);
+    twoshot_kernel<T, OP><<<ctas, kCollThreads, 0, s>>>(a);
   return cudaGetLastError();
 }
 

@@ -15,6 +15,7 @@ constexpr int kMaxBatch = 128;       // descriptors per pull launch (by value)
 constexpr int kMaxWaitFlags = 128;   // flags per wait launch (one thread each)
 constexpr std::uint32_t kCounterSlots = 1024;  // per-stream message counters
 constexpr std::uint32_t kChunkUnits = 1024;  // units per CTA work item (16 KB of 16 B units)
+constexpr int kMaxEntrySignals = 64;  // flags a pull launch stores at entry
 
 // 32-bit division by an invariant divisor through a multiply-high and a shift
 // (Granlund & Montgomery, "Division by invariant integers using
@@ -74,6 +75,11 @@ struct PullBatch {
   // *epoch (device memory, advanced once per start by the plan's last launch),
   // so a plan's launches never change and replay as one CUDA graph
   const std::uint64_t* epoch;
+  // flags stored (release, system scope) by the first CTA at kernel entry,
+  // value *epoch: the "data ready" signals of a plan whose sends need no
+  // packing ride on its pull launch instead of a launch of their own
+  std::uint32_t nsig;
+  std::uint64_t* sig[kMaxEntrySignals];
   PullDesc d[kMaxBatch];
 };
 
@@ -91,6 +97,7 @@ struct WaitBatch {
   std::uint64_t timeout_ns;
   unsigned long long* status;
   const std::uint64_t* epoch;  // non-null: every val is *epoch (plans)
+  std::uint64_t* bump;         // non-null: *bump += 1 once every wait is over
   const std::uint64_t* flag[kMaxWaitFlags];
   std::uint64_t val[kMaxWaitFlags];
 };

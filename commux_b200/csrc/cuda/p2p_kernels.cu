@@ -167,6 +167,12 @@ struct InlineSrc {
   __device__ unsigned long long* status() const { return b.status; }
   __device__ std::uint64_t timeout_ns() const { return b.timeout_ns; }
   __device__ std::uint64_t epoch() const { return b.epoch ? *b.epoch : 0; }
+  __device__ void entry_signals(std::uint64_t epoch) const {
+    if (blockIdx.x == 0 && threadIdx.x < b.nsig) {
+      fence_acq_rel_sys();
+      st_release_sys(b.sig[threadIdx.x], epoch);
+    }
+  }
 };
 
 // Descriptor owning global chunk c: the last one whose chunk0 <= c (binary
@@ -197,6 +203,7 @@ __device__ __forceinline__ void pull_body(const S& s) {
   constexpr std::uint32_t kFailBit = 0x80000000u;
   const std::uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const std::uint64_t epoch = s.epoch();
+  s.entry_signals(epoch);
   for (std::uint32_t c = blockIdx.x; c < s.total(); c += gridDim.x) {
     const PullDesc& d = s.desc(find_desc(s, c));
     const std::uint32_t u0 = (c - d.chunk0) * kChunkUnits;
@@ -272,6 +279,26 @@ __global__ void wait_kernel(const __grid_constant__ WaitBatch b) {
   }
 }
 
+// As wait_kernel, then (plans) advance the epoch once every lane is done.
+__global__ void wait_bump_kernel(const __grid_constant__ WaitBatch b) {
+  const std::uint32_t i = threadIdx.x;
+  if (i < b.n) {
+    const std::uint64_t want = *b.epoch;
+    const std::uint64_t t0 = globaltimer_ns();
+    std::uint32_t spins = 0;
+    while (ld_acquire_sys(b.flag[i]) < want) {
+      if ((++spins & 63u) == 0u && globaltimer_ns() - t0 > b.timeout_ns) {
+        report_status(b.status, kStatusWaitTimeout, reinterpret_cast<unsigned long long>(b.flag[i]), want,
+                      ld_acquire_sys(b.flag[i]));
+        break;
+      }
+      __nanosleep(128);
+    }
+  }
+  __syncthreads();
+  if (i == 0) *b.bump += 1;
+}
+
 __global__ void epoch_bump_kernel(std::uint64_t* epoch) { *epoch += 1; }
 
 __global__ void signal_kernel(std::uint64_t* flag, std::uint64_t val) {
@@ -334,6 +361,8 @@ cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStrea
   sub.status = b.status;
   sub.timeout_ns = b.timeout_ns;
   sub.epoch = b.epoch;
+  sub.nsig = 0;  // entry signals go with the first class launched
+  bool first_launch = true;
   for (int cls : {16, 8, 4, 2, 1, 0}) {
     sub.n = 0;
     sub.total_chunks = 0;
@@ -345,6 +374,13 @@ cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStrea
       sub.d[sub.n++] = x;
     }
     if (sub.n == 0 || sub.total_chunks == 0) continue;
+    if (first_launch) {
+      sub.nsig = b.nsig;
+      for (std::uint32_t k = 0; k < b.nsig; ++k) sub.sig[k] = b.sig[k];
+      first_launch = false;
+    } else {
+      sub.nsig = 0;
+    }
     if (launches != nullptr) ++*launches;
     cudaError_t e = launch_class(cls, sub, max_ctas, s);
     if (e != cudaSuccess) return e;
@@ -353,6 +389,10 @@ cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStrea
 }
 
 cudaError_t launch_wait(const WaitBatch& b, cudaStream_t s) {
+  if (b.bump != nullptr) {
+    wait_bump_kernel<<<1, kMaxWaitFlags, 0, s>>>(b);
+    return cudaGetLastError();
+  }
   if (b.n == 0) return cudaSuccess;
   wait_kernel<<<1, kMaxWaitFlags, 0, s>>>(b);
   return cudaGetLastError();

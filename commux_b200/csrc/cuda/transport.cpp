@@ -1156,14 +1156,27 @@ class CudaPlan final : public DevicePlan {
   std::vector<Msg> sends, recvs;
 
   // Builds the launches every start() replays: (1) pack + "ready" signals of
-  // the sends to other GPUs, (2) the pulls of every receive, (3) the wait for
-  // the receivers' "consumed" flags, (4) the epoch bump. Every flag value is
+  // the sends to other GPUs (without packing, the signals are stored by the
+  // first pull launch at entry instead), (2) the pulls of every receive, (3)
+  // the wait for the receivers' "consumed" flags, ending with the epoch bump.
+  // Every flag value is
   // the plan's epoch, read from device memory, so the launches never change:
   // they are captured once into a CUDA graph and a start is one graph launch.
   void finalize() {
     std::vector<std::vector<PullDesc>> pre, pull;
+    std::vector<std::uint64_t*> ready_only;  // device sends that need no packing
+    bool any_pack = false;
+    for (auto& m : sends)
+      if (m.mode == PlanMode::Device) {
+        any_pack |= !m.pack.empty();
+        if (m.pack.empty()) ready_only.push_back(m.ready_remote);
+      }
+    for (auto& m : recvs)
+      if (m.mode != PlanMode::Shared && !m.descs.empty()) pull.push_back(m.descs);
+    // without packing, the "ready" signals ride on the first pull launch
+    const bool entry_signals = !any_pack && !pull.empty() && ready_only.size() <= kMaxEntrySignals;
     for (auto& m : sends) {
-      if (m.mode != PlanMode::Device) continue;
+      if (m.mode != PlanMode::Device || entry_signals) continue;
       std::vector<PullDesc> d = m.pack;
       if (d.empty()) {  // a pure signal: zero units, the flag store only
         PullDesc x{};
@@ -1176,8 +1189,6 @@ class CudaPlan final : public DevicePlan {
       for (auto& x : d) x.done = m.ready_remote;
       pre.push_back(std::move(d));
     }
-    for (auto& m : recvs)
-      if (m.mode != PlanMode::Shared && !m.descs.empty()) pull.push_back(m.descs);
     // device state: [epoch u64, starts at 1][counters u32 x kCounterSlots]
     const std::size_t state_bytes = 64 + kCounterSlots * sizeof(std::uint32_t);
     state_ = at::empty({static_cast<std::int64_t>(state_bytes)},
@@ -1190,10 +1201,15 @@ class CudaPlan final : public DevicePlan {
     CMX_CUDA(cudaMemcpy(state_.data_ptr(), init.data(), state_bytes, cudaMemcpyHostToDevice));
     pre_ = batches(pre);
     pulls_ = batches(pull);
+    if (entry_signals) {
+      pulls_[0]->nsig = static_cast<std::uint32_t>(ready_only.size());
+      for (std::size_t k = 0; k < ready_only.size(); ++k) pulls_[0]->sig[k] = ready_only[k];
+    }
     std::memset(&wait_, 0, sizeof(wait_));
     wait_.timeout_ns = tr_->device_timeout_ns();
     wait_.status = c_->status_d;
     wait_.epoch = epoch_d_;
+    wait_.bump = epoch_d_;  // the wait launch also advances the epoch
     for (auto& m : sends)
       if (m.mode == PlanMode::Device) {
         TORCH_CHECK(wait_.n < static_cast<std::uint32_t>(kMaxWaitFlags), "commux plan: more than ",
@@ -1281,6 +1297,7 @@ class CudaPlan final : public DevicePlan {
         b->status = c_->status_d;
         b->timeout_ns = tr_->device_timeout_ns();
         b->epoch = epoch_d_;
+        b->nsig = 0;
         while (i < kv.second.size() && b->n < static_cast<std::uint32_t>(kMaxBatch)) {
           PullDesc d = kv.second[i++];
           d.chunk0 = b->total_chunks;
@@ -1306,12 +1323,8 @@ class CudaPlan final : public DevicePlan {
         if (e == cudaSuccess) e = launch_pull(*b, ctas, 256, cs, &launched);
         nodes_ += launched;
       }
-    if (e == cudaSuccess && wait_.n) {
+    if (e == cudaSuccess) {  // waits (if any), then the epoch bump
       e = launch_wait(wait_, cs);
-      ++nodes_;
-    }
-    if (e == cudaSuccess) {
-      e = launch_epoch_bump(epoch_d_, cs);
       ++nodes_;
     }
     cudaGraph_t g = nullptr;
