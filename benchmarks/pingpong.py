@@ -9,8 +9,10 @@ published V=2/16 at 8 KiB per tensor in src/process_group_ucx.cpp:139-141).
 
 Modes: ``pertensor`` (one message per tensor), ``coalesced`` (one message for
 the V tensors; needs COMMUX_COALESCE=1 in the environment, which changes the
-wire format on every rank), ``plan`` (a persistent plan started every
-iteration), ``batch`` (one batch_p2p per direction).
+wire format on every rank), ``window`` (torch's batch_isend_irecv, i.e. the
+backend's coalescing window; set COMMUX_GROUP=1 to defer the posts to its end),
+``plan`` (a persistent plan started every iteration), ``batch`` (one
+batch_p2p per direction).
 
     torchrun --nproc-per-node 2 benchmarks/pingpong.py --device cuda --mode plan
 """
@@ -31,12 +33,12 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--device", default="cuda", choices=["cuda", "cpu"])
-    ap.add_argument("--mode", default="pertensor", choices=["pertensor", "coalesced", "plan", "batch"])
-    ap.add_argument("--V", default="1,2,8,16,64,512")
-    ap.add_argument("--sizes", default="4096,8192,65536,1048576,4194304")
+    ap.add_argument("--mode", default="pertensor", choices=["pertensor", "coalesced", "window", "plan", "batch"])
+    ap.add_argument("--V", default="1,8,64,512")
+    ap.add_argument("--sizes", default="4096,65536,1048576,4194304")
     ap.add_argument("--iters", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--max-total-bytes", type=int, default=1 << 30)
+    ap.add_argument("--max-total-bytes", type=int, default=2 << 30)
     args = ap.parse_args()
 
     import torch
@@ -81,6 +83,24 @@ def main():
                 if args.mode == "plan":
                     plans[0].start()
                     plans[1].start()
+                elif args.mode == "window":
+                    other = 1 - rank
+                    if rank == 0:
+                        ws = dist.batch_isend_irecv([dist.P2POp(dist.isend, t, other, tag=900 + k)
+                                                     for k, t in enumerate(sv)])
+                        for w in ws:
+                            w.wait()
+                        ws = dist.batch_isend_irecv([dist.P2POp(dist.irecv, t, other, tag=1900 + k)
+                                                     for k, t in enumerate(rv)])
+                    else:
+                        ws = dist.batch_isend_irecv([dist.P2POp(dist.irecv, t, other, tag=900 + k)
+                                                     for k, t in enumerate(rv)])
+                        for w in ws:
+                            w.wait()
+                        ws = dist.batch_isend_irecv([dist.P2POp(dist.isend, t, other, tag=1900 + k)
+                                                     for k, t in enumerate(sv)])
+                    for w in ws:
+                        w.wait()
                 elif args.mode == "batch":
                     if rank == 0:
                         commux.batch_p2p(sends=[(t, 1, 900 + k) for k, t in enumerate(sv)]).wait()
@@ -109,7 +129,8 @@ def main():
                 print(json.dumps({"mode": args.mode, "device": args.device, "V": V, "bytes_per_tensor": nbytes,
                                   "roundtrip_us_p50": round(statistics.median(lat), 2),
                                   "roundtrip_us_min": round(min(lat), 2),
-                                  "coalesce": os.environ.get("COMMUX_COALESCE", "0")}), flush=True)
+                                  "coalesce": os.environ.get("COMMUX_COALESCE", "0"),
+                                  "group": os.environ.get("COMMUX_GROUP", "0")}), flush=True)
             dist.barrier()
     dist.destroy_process_group()
 

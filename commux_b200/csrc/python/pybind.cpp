@@ -4,6 +4,8 @@
 
 #include <pybind11/chrono.h>
 #include <pybind11/stl.h>
+
+#include "clocks.hpp"
 #include <torch/csrc/utils/pybind.h>
 
 #include <chrono>
@@ -57,6 +59,18 @@ PYBIND11_MODULE(_C, m) {
     return d;
   });
   m.def("reset_stats", [](const c10::intrusive_ptr<c10d::Backend>& b) { as_commux(b)->reset_stats(); });
+  py::class_<commux::clocks::Sampler>(m, "ClockSampler")
+      .def(py::init<const std::string&, int>(), py::arg("gpu"), py::arg("interval_us") = 1000)
+      .def("start", &commux::clocks::Sampler::start)
+      .def("stop",
+           [](commux::clocks::Sampler& s) {
+             py::list out;
+             for (auto& x : s.stop())
+               out.append(py::make_tuple(x.t_us, x.sm_mhz, x.sm_max_mhz, x.reasons, x.power_mw));
+             return out;
+           },
+           "Stop and return [(t_us, sm_mhz, sm_max_mhz, reasons, power_mw), ...].")
+      .def_property_readonly("error", &commux::clocks::Sampler::error);
   m.def("transports", [](const c10::intrusive_ptr<c10d::Backend>& b) {
     auto& e = as_commux(b)->engine();
     py::list kinds;

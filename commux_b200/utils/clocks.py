@@ -1,10 +1,12 @@
 """Sample GPU clocks and throttle reasons while a benchmark runs (read-only).
 
-A background thread polls NVML every ``interval_ms`` (default 2 ms, so even a
-timed region of a few milliseconds gets samples) for the SM clock, the
-maximum SM clock, power, utilisation and the active clock-event reasons, and
-summarises the samples taken under load: median SM clock, maximum SM clock,
-and every throttle reason that was active. Nothing here changes a GPU
+A native thread (``commux_b200._C.ClockSampler``, C++, no GIL) polls NVML
+every ``interval_ms`` (default 1 ms) for the SM clock, the maximum SM clock,
+power and the active clock-event reasons; every sample falls inside the timed
+region, so all of them count as "under load". Without the native module a
+Python thread polls through pynvml instead and uses utilisation >= 50 % to mark
+samples under load. The summary gives the median SM clock, the maximum SM
+clock and every throttle reason that was active. Nothing here changes a GPU
 setting; only query functions are called.
 """
 
@@ -24,7 +26,7 @@ _REASONS = {  # NVML clock-event reason bits
 
 
 class ClockSampler:
-    def __init__(self, gpu_ids: list[str], interval_ms: float = 2.0, raw_path: str | None = None):
+    def __init__(self, gpu_ids: list[str], interval_ms: float = 1.0, raw_path: str | None = None):
         self.gpu_ids = gpu_ids
         self.interval = interval_ms / 1e3
         self.raw_path = raw_path
@@ -36,6 +38,19 @@ class ClockSampler:
         self.error = None
 
     def start(self) -> "ClockSampler":
+        # native sampler (C++ thread, no GIL): a sample per interval even when
+        # the Python thread is busy launching work
+        try:
+            from commux_b200 import _C
+
+            self._native = [_C.ClockSampler(g, int(self.interval * 1e6)) for g in self.gpu_ids]
+            if self._native and not any(n.error for n in self._native):
+                for n in self._native:
+                    n.start()
+                return self
+        except Exception:
+            pass
+        self._native = None
         try:
             import pynvml
 
@@ -75,6 +90,20 @@ class ClockSampler:
             time.sleep(self.interval)
 
     def stop(self) -> dict | None:
+        if getattr(self, "_native", None):
+            rows = []
+            for n in self._native:
+                for t_us, sm, smax, reasons, mw in n.stop():
+                    # every native sample falls inside the timed region:
+                    # utilisation 100 marks it "under load"
+                    rows.append((t_us / 1e6, sm, smax, 100, reasons, mw / 1000.0))
+            self._rows = rows
+            if self.raw_path:
+                with open(self.raw_path, "w") as f:
+                    f.write("t,sm_mhz,sm_max_mhz,util,reasons_mask,power_w\n")
+                    for r in rows:
+                        f.write(",".join(str(x) for x in r) + "\n")
+            return summarize(rows)
         if self._thread is None:
             return None
         self._sample()  # at least one sample at the end of the region
