@@ -135,6 +135,18 @@ def main() -> None:
     launches = cuda_launches() - launches0
     clocks = sampler.stop()
 
+    # diagnostic: the same exchange back to back, no stencil in between (the
+    # in-step exchange also absorbs the ranks' skew after each update)
+    xev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K)]
+    torch.cuda.synchronize()
+    dist.barrier()
+    for k in range(K):
+        xev[k][0].record()
+        model.exchange()
+        xev[k][1].record()
+    torch.cuda.synchronize()
+    xonly = rank_max([xev[k][0].elapsed_time(xev[k][1]) for k in range(K)])
+
     exch = [ev[k][0].elapsed_time(ev[k][1]) for k in range(K)]
     step = [ev[k][0].elapsed_time(ev[k][2]) for k in range(K)]
     total = ev[0][0].elapsed_time(ev[K - 1][2])
@@ -198,6 +210,7 @@ def main() -> None:
                 "seq_len": 0,
                 "parallelism": f"domain decomposition {dims[0]}x{dims[1]}x{dims[2]} (periodic)",
                 "halo_bytes_per_step_per_rank": bytes_rank,
+                "exchange_only_us_p50": round(statistics.median(xonly) * 1e3, 2),
                 "halo_bytes_per_step_job": bytes_job,
                 "exchange_us_p50": round(statistics.median(exch_max) * 1e3, 2),
                 "exchange_us_min": round(min(exch_max) * 1e3, 2),

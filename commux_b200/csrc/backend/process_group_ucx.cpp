@@ -555,6 +555,7 @@ std::vector<std::pair<std::string, std::int64_t>> ProcessGroupUCX::stats() const
       {"records_in", s.records_in.load()},
       {"records_out", s.records_out.load()},
       {"host_copies", s.host_copies.load()},
+      {"single_copy_msgs", s.single_copy_msgs.load()},
       {"faults_injected", s.faults_injected.load()},
   };
   if (auto* d = engine_->device(false))
@@ -566,7 +567,7 @@ void ProcessGroupUCX::reset_stats() {
   auto& s = engine_->stats();
   for (auto* a : {&s.sends, &s.recvs, &s.bytes_sent, &s.bytes_recv, &s.eager_msgs, &s.rndv_msgs,
                   &s.device_msgs, &s.unexpected_msgs, &s.unexpected_peak, &s.ring_full_stalls,
-                  &s.futex_sleeps, &s.records_in, &s.records_out, &s.host_copies,
+                  &s.futex_sleeps, &s.records_in, &s.records_out, &s.host_copies, &s.single_copy_msgs,
                   &s.faults_injected})
     a->store(0);
 }

@@ -83,14 +83,6 @@ struct PullBatch {
   PullDesc d[kMaxBatch];
 };
 
-// Flags a signal launch stores (release, system scope), one thread each.
-constexpr int kMaxSignal = 128;
-struct SignalBatch {
-  std::uint32_t n;
-  std::uint64_t* flag[kMaxSignal];
-  std::uint64_t val[kMaxSignal];
-};
-
 // Flags a wait kernel polls (all in this GPU's own memory, written remotely).
 struct WaitBatch {
   std::uint32_t n;
@@ -118,11 +110,7 @@ cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStrea
 // Unit class of a descriptor: one kernel instantiation per class (16, 8, 4,
 // 2, 1 byte units; 0 = wide strides).
 inline int pull_unit_class(const PullDesc& d) { return d.wide ? 0 : static_cast<int>(d.unit); }
-// *epoch += 1 (one thread): the last launch of a plan's start.
-cudaError_t launch_epoch_bump(std::uint64_t* epoch, cudaStream_t s);
 cudaError_t launch_wait(const WaitBatch& b, cudaStream_t s);
-cudaError_t launch_signal(std::uint64_t* flag, std::uint64_t val, cudaStream_t s);
-cudaError_t launch_signal_many(const SignalBatch& b, cudaStream_t s);
 
 }  // namespace cuda
 }  // namespace commux

@@ -252,15 +252,6 @@ __global__ void __launch_bounds__(kThreads, 4) pull_kernel(const __grid_constant
   pull_body<U>(InlineSrc{b});
 }
 
-// Store each flag with release semantics at system scope (after everything
-// the stream did before): "data ready" signals of persistent plans.
-__global__ void signal_many_kernel(const __grid_constant__ SignalBatch b) {
-  const std::uint32_t i = threadIdx.x;
-  if (i >= b.n) return;
-  fence_acq_rel_sys();
-  st_release_sys(b.flag[i], b.val[i]);
-}
-
 // One warp: lane i waits until *flag[i] >= val[i], giving up after the
 // timeout (status word set, kernel returns; never traps).
 __global__ void wait_kernel(const __grid_constant__ WaitBatch b) {
@@ -299,13 +290,6 @@ __global__ void wait_bump_kernel(const __grid_constant__ WaitBatch b) {
   if (i == 0) *b.bump += 1;
 }
 
-__global__ void epoch_bump_kernel(std::uint64_t* epoch) { *epoch += 1; }
-
-__global__ void signal_kernel(std::uint64_t* flag, std::uint64_t val) {
-  fence_acq_rel_sys();
-  st_release_sys(flag, val);
-}
-
 }  // namespace
 
 namespace {
@@ -337,11 +321,6 @@ cudaError_t launch_class(int cls, const PullBatch& b, int max_ctas, cudaStream_t
 }
 
 }  // namespace
-
-cudaError_t launch_epoch_bump(std::uint64_t* epoch, cudaStream_t s) {
-  epoch_bump_kernel<<<1, 1, 0, s>>>(epoch);
-  return cudaGetLastError();
-}
 
 // A batch whose descriptors share one unit class is one launch; a mixed batch
 // becomes one launch per class, in order on the stream (completion counters
@@ -395,17 +374,6 @@ cudaError_t launch_wait(const WaitBatch& b, cudaStream_t s) {
   }
   if (b.n == 0) return cudaSuccess;
   wait_kernel<<<1, kMaxWaitFlags, 0, s>>>(b);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_signal_many(const SignalBatch& b, cudaStream_t s) {
-  if (b.n == 0) return cudaSuccess;
-  signal_many_kernel<<<1, kMaxSignal, 0, s>>>(b);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_signal(std::uint64_t* flag, std::uint64_t val, cudaStream_t s) {
-  signal_kernel<<<1, 1, 0, s>>>(flag, val);
   return cudaGetLastError();
 }
 

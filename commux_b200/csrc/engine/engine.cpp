@@ -1,4 +1,6 @@
 #include "engine.hpp"
+
+#include <sys/uio.h>
 #include "log.hpp"
 
 #include <c10/util/Exception.h>
@@ -148,6 +150,9 @@ Engine::Engine(c10::intrusive_ptr<c10d::Store> store, int rank, int size,
   wait_poll_ms_ = static_cast<int>(env_int("COMMUX_WAIT_POLL_MS", 1));
   if (wait_poll_ms_ <= 0) wait_poll_ms_ = 1;
   fault_ = FaultSpec::from_env();
+  cma_enabled_ = env_int("COMMUX_CMA", 1) != 0;
+  cma_off_.reset(new std::atomic<bool>[static_cast<std::size_t>(size)]);
+  for (int p = 0; p < size; ++p) cma_off_[p].store(false);
   bootstrap();
   last_liveness_ = std::chrono::steady_clock::now();
   progress_ = std::thread([this] { progress_loop(); });
@@ -434,11 +439,19 @@ ReqPtr Engine::post_send(std::vector<at::Tensor> tensors, int dst, tag_t tag) {
       sends_waiting_[r->id] = r;
     }
     job->type = proto::kRts;
-    job->head.resize(sizeof(proto::RtsRec));
+    // a same-host receiver may copy straight out of these segments
+    const bool cma = cma_enabled_ && !remote(dst) && r->host.size() <= proto::kCmaSegs;
+    const std::uint32_t nseg = cma ? static_cast<std::uint32_t>(r->host.size()) : 0u;
+    job->head.assign(sizeof(proto::RtsRec) + nseg * sizeof(proto::CmaSeg), 0);
     auto* rec = reinterpret_cast<proto::RtsRec*>(job->head.data());
     rec->key = r->key;
     rec->total = r->total;
     rec->send_id = r->id;
+    rec->pid = static_cast<std::int32_t>(::getpid());
+    rec->nseg = nseg;
+    auto* segs = reinterpret_cast<proto::CmaSeg*>(rec + 1);
+    for (std::uint32_t i = 0; i < nseg; ++i)
+      segs[i] = {reinterpret_cast<std::uint64_t>(r->host[i].ptr), r->host[i].bytes};
   }
   enqueue(dst, std::move(job));
   flush_out(dst, false);
@@ -479,6 +492,7 @@ ReqPtr Engine::post_recv(std::vector<at::Tensor> tensors, int src, tag_t tag) {
 
   UnexpPtr u;
   bool flush_to = false;
+  bool cma = false;
   {
     std::lock_guard<std::mutex> lk(mu_);
     u = match_unexpected(src, r->key);
@@ -497,11 +511,28 @@ ReqPtr Engine::post_recv(std::vector<at::Tensor> tensors, int src, tag_t tag) {
         // fall through: reject below
       } else if (u->total > r->total) {
         // reject: tell the sender (recv id 0)
+      } else if (!u->data.empty() && !cma_off_[u->src].load()) {
+        cma = true;  // single-copy read, outside the lock
       } else {
         start_rndv_recv(r, u->src, u->msg_id, u->total);
         flush_to = true;
       }
     }
+  }
+  if (cma) {
+    const auto* segs = reinterpret_cast<const proto::CmaSeg*>(u->data.data());
+    const auto nseg = static_cast<std::uint32_t>(u->data.size() / sizeof(proto::CmaSeg));
+    if (cma_read(u->src, r, u->pid, segs, nseg, u->total)) {
+      send_fin(u->src, u->msg_id, 0);
+      complete(r);
+      return r;
+    }
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      start_rndv_recv(r, u->src, u->msg_id, u->total);
+    }
+    flush_out(u->src, false);
+    return r;
   }
   if (flush_to) {
     flush_out(u->src, false);
@@ -1000,7 +1031,10 @@ void Engine::on_frag(int src, const proto::FragRec* rec) {
 
 void Engine::on_rts(int src, const proto::RtsRec* rec) {
   ReqPtr r;
-  bool started = false;
+  bool started = false, cma = false;
+  const auto* segs = reinterpret_cast<const proto::CmaSeg*>(rec + 1);
+  const bool has_segs = rec->nseg > 0 && rec->nseg <= proto::kCmaSegs &&
+                        rec->h.len >= sizeof(proto::RtsRec) + rec->nseg * sizeof(proto::CmaSeg);
   {
     std::lock_guard<std::mutex> lk(mu_);
     r = match_posted(src, rec->key);
@@ -1011,6 +1045,10 @@ void Engine::on_rts(int src, const proto::RtsRec* rec) {
       u->type = proto::kRts;
       u->total = rec->total;
       u->msg_id = rec->send_id;
+      u->pid = rec->pid;
+      if (has_segs)
+        u->data.assign(reinterpret_cast<const char*>(segs),
+                       reinterpret_cast<const char*>(segs + rec->nseg));
       unexpected_[rec->key].push_back(u);
       ++unexpected_count_;
       stats_.unexpected_msgs++;
@@ -1018,10 +1056,26 @@ void Engine::on_rts(int src, const proto::RtsRec* rec) {
     }
     r->source = src;
     if (!r->device && rec->total <= r->total) {
-      // DATA fragments carry the sender's total; record it for completion.
-      start_rndv_recv(r, src, rec->send_id, rec->total);
-      started = true;
+      if (has_segs && !cma_off_[src].load()) {
+        cma = true;  // single-copy read, outside the lock
+      } else {
+        // DATA fragments carry the sender's total; record it for completion.
+        start_rndv_recv(r, src, rec->send_id, rec->total);
+        started = true;
+      }
     }
+  }
+  if (cma) {
+    if (cma_read(src, r, rec->pid, segs, rec->nseg, rec->total)) {
+      send_fin(src, rec->send_id, 0);
+      complete(r);
+      return;
+    }
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      start_rndv_recv(r, src, rec->send_id, rec->total);
+    }
+    started = true;
   }
   if (started) {
     flush_out(src, true);
@@ -1112,7 +1166,53 @@ void Engine::on_fin(int src, const proto::FinRec* rec) {
                 " received this CUDA tensor into a CPU buffer (device mismatch)");
     return;
   }
+  if (!s->device) {  // host rendezvous finished by the receiver's single-copy read
+    complete(s);
+    return;
+  }
   if (dev_) dev_->on_fin(s, rec->status);
+}
+
+bool Engine::cma_read(int src, const ReqPtr& r, std::int32_t pid, const proto::CmaSeg* segs, std::uint32_t nseg,
+                      std::uint64_t total) {
+  // walk the sender's segments and this request's host segments together
+  std::uint32_t si = 0;
+  std::uint64_t soff = 0, done = 0;
+  std::size_t li = 0;
+  std::uint64_t loff = 0;
+  while (done < total) {
+    while (si < nseg && soff >= segs[si].bytes) {
+      ++si;
+      soff = 0;
+    }
+    while (li < r->host.size() && loff >= r->host[li].bytes) {
+      ++li;
+      loff = 0;
+    }
+    if (si >= nseg || li >= r->host.size()) break;
+    std::uint64_t n = std::min({segs[si].bytes - soff, r->host[li].bytes - loff, total - done});
+    iovec liov{r->host[li].ptr + loff, static_cast<std::size_t>(n)};
+    iovec riov{reinterpret_cast<void*>(segs[si].addr + soff), static_cast<std::size_t>(n)};
+    ssize_t got = ::process_vm_readv(static_cast<pid_t>(pid), &liov, 1, &riov, 1, 0);
+    if (got <= 0) {
+      // refused (ptrace policy, seccomp, another host): this peer uses the
+      // two-copy path from now on
+      cma_off_[src].store(true);
+      logf(LogLevel::Info, rank_, "single-copy reads from rank %d refused (%s); using the ring", src,
+           std::strerror(errno));
+      return false;
+    }
+    soff += static_cast<std::uint64_t>(got);
+    loff += static_cast<std::uint64_t>(got);
+    done += static_cast<std::uint64_t>(got);
+  }
+  if (done != total) {
+    cma_off_[src].store(true);
+    return false;
+  }
+  stats_.single_copy_msgs++;
+  stats_.bytes_recv += static_cast<std::int64_t>(total);
+  return true;
 }
 
 void Engine::on_abort(int src, const proto::AbortRec* rec) {

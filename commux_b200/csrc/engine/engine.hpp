@@ -80,7 +80,8 @@ struct Unexpected {
   std::uint16_t type = 0;     // proto::kEager / kRts / kDrts
   std::uint64_t total = 0;
   std::uint64_t msg_id = 0;   // sender's id
-  std::vector<char> data;     // eager payload / device blob
+  std::vector<char> data;     // eager payload / device blob / single-copy segments
+  std::int32_t pid = 0;       // rendezvous: sender pid for a single-copy read
   std::uint64_t arrived = 0;  // eager bytes landed
   bool complete = false;      // all eager bytes landed
   ReqPtr bound;               // recv matched while bytes were still landing
@@ -95,6 +96,7 @@ struct Stats {
   std::atomic<std::int64_t> ring_full_stalls{0}, futex_sleeps{0};
   std::atomic<std::int64_t> records_in{0}, records_out{0};
   std::atomic<std::int64_t> host_copies{0};
+  std::atomic<std::int64_t> single_copy_msgs{0};  // host rendezvous read with process_vm_readv
   std::atomic<std::int64_t> faults_injected{0};
 };
 
@@ -214,6 +216,11 @@ class Engine {
   void on_drts(int src, const proto::DrtsRec* rec);
   void on_fin(int src, const proto::FinRec* rec);
   void on_abort(int src, const proto::AbortRec* rec);
+  // Single-copy rendezvous: read the sender's segments straight into r's
+  // host buffers; false (and the peer marked CTS-only) when the kernel
+  // refuses the cross-process read.
+  bool cma_read(int src, const ReqPtr& r, std::int32_t pid, const proto::CmaSeg* segs, std::uint32_t nseg,
+                std::uint64_t total);
 
   // matching helpers (mu_ held)
   ReqPtr match_posted(int src, tag_t key);
@@ -238,6 +245,8 @@ class Engine {
 
   std::vector<std::unique_ptr<shm::Segment>> segs_;  // [rank] own, others mapped (null: TCP peer)
   std::vector<bool> remote_;                         // remote_[p]: TCP peer
+  std::unique_ptr<std::atomic<bool>[]> cma_off_;     // single-copy refused for peer p
+  bool cma_enabled_ = true;                          // COMMUX_CMA
   bool any_remote_ = false;
   std::unique_ptr<tcp::Links> links_;                // TCP peers (null when none)
   std::vector<shm::RingReader> in_;                  // in_[src]

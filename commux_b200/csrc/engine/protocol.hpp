@@ -53,11 +53,25 @@ struct FragRec {
   // payload follows
 };
 
+// Host rendezvous. When the sender's bytes are in at most kCmaSegs host
+// segments, the record also lists them (address, length) with the sender's
+// pid: a receiver on the same host may then copy them straight out of the
+// sender's memory (process_vm_readv) and answer with a FIN instead of a CTS.
+constexpr std::uint32_t kCmaSegs = 16;
+
+struct CmaSeg {
+  std::uint64_t addr;
+  std::uint64_t bytes;
+};
+
 struct RtsRec {
   shm::WireHdr h;
   std::uint64_t key;
   std::uint64_t total;
   std::uint64_t send_id;
+  std::int32_t pid;     // sender's pid (single-copy read)
+  std::uint32_t nseg;   // CmaSeg entries that follow (0: CTS path only)
+  // CmaSeg seg[nseg] follow
 };
 
 struct CtsRec {
