@@ -29,7 +29,7 @@ def build(build_dir: str | None = None, jobs: int | None = None, verbose: bool =
     build_dir = build_dir or os.path.join(REPO, "build" if not sanitize else f"build-{sanitize}")
     os.makedirs(build_dir, exist_ok=True)
     if cuda is None:
-        cuda = _has_cuda_sources() and os.path.exists("/usr/local/cuda/bin/nvcc")
+        cuda = _has_cuda_sources() and os.path.exists("/usr/local/cuda/bin/nvcc") and not sanitize
     gen = ["-G", "Ninja"] if shutil.which("ninja") else []
     cfg = ["cmake", "-S", REPO, "-B", build_dir, *gen,
            f"-DPython3_EXECUTABLE={sys.executable}",
@@ -37,7 +37,8 @@ def build(build_dir: str | None = None, jobs: int | None = None, verbose: bool =
            f"-DCOMMUX_DEVICE_CHECKS={'ON' if device_checks else 'OFF'}",
            "-DCMAKE_BUILD_TYPE=Release"]
     if sanitize:
-        cfg.append(f"-DCOMMUX_SANITIZE={sanitize}")
+        # host libraries and the C++ test driver only, inside the build tree
+        cfg += [f"-DCOMMUX_SANITIZE={sanitize}", "-DCOMMUX_BUILD_PYTHON=OFF"]
     env = dict(os.environ)
     env.setdefault("CUDACXX", "/usr/local/cuda/bin/nvcc")
     # Use the system compiler, which links the shared libstdc++ that torch

@@ -153,7 +153,7 @@ class CommuxWork : public c10d::Work {
 
   int sourceRank() const override {
     if (source_rank_ >= 0) return source_rank_;
-    return reqs_.size() == 1 ? reqs_[0]->source : -1;
+    return reqs_.size() == 1 ? reqs_[0]->source.load() : -1;
   }
 
   std::vector<at::Tensor> result() override { return outs_; }

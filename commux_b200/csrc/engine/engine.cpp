@@ -696,7 +696,8 @@ void Engine::wait(const ReqPtr& r, std::chrono::milliseconds timeout) {
         lk.lock();
         break;
       }
-      int pr = r->kind == ReqKind::Send ? r->peer : (r->source >= 0 ? r->source : r->peer);
+      const int srcr = r->source.load();
+      int pr = r->kind == ReqKind::Send ? r->peer : (srcr >= 0 ? srcr : r->peer);
       if (pr >= 0 && dead_[pr].load()) {
         lk.unlock();
         fail(r, "commux: peer rank " + std::to_string(pr) + " failed");

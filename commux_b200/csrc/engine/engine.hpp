@@ -66,7 +66,7 @@ struct Request {
   std::vector<at::Tensor> tensors;  // data (kept alive until completion)
   std::vector<HostSeg> host;        // host byte segments, in order
   std::uint64_t total = 0;          // bytes
-  int source = -1;                  // recv: rank the message came from
+  std::atomic<int> source{-1};      // recv: rank the message came from (read by waiters)
   std::uint64_t landed = 0;         // recv: payload bytes written
   std::shared_ptr<void> dev;        // device-transport state
   std::chrono::steady_clock::time_point posted_at;

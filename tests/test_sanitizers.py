@@ -1,0 +1,45 @@
+"""The host engine under ThreadSanitizer: an instrumented build of libcommux
+and the C++ test driver (its own build tree, the package keeps the production
+libraries), run as 2 ranks over shared memory and over TCP, including the
+multi-threaded posting and parked-waiter tests. Any data race report fails."""
+
+import os
+import subprocess
+import sys
+
+import pytest
+
+from mp import ROOT, free_port
+
+BUILD = os.path.join(ROOT, "build-thread")
+BIN = os.path.join(BUILD, "lib", "test_commux")
+
+
+@pytest.fixture(scope="module")
+def tsan_driver():
+    r = subprocess.run([sys.executable, "-m", "commux_b200.build", "--sanitize", "thread"], cwd=ROOT,
+                       capture_output=True, text=True, timeout=1500)
+    if r.returncode != 0 or not os.path.exists(BIN):
+        pytest.skip("ThreadSanitizer build unavailable: " + (r.stdout + r.stderr)[-500:])
+    return BIN
+
+
+@pytest.mark.parametrize("transport", ["shm", "tcp"])
+def test_engine_has_no_data_races(tsan_driver, transport):
+    port = free_port()
+    env = dict(os.environ, COMMUX_MT="1", COMMUX_DEADLOCK="1", COMMUX_TRANSPORT=transport,
+               TSAN_OPTIONS="halt_on_error=0 report_signal_unsafe=0")
+    procs = [subprocess.Popen([tsan_driver, str(r), "2", "127.0.0.1", str(port)], env=env,
+                              stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True) for r in range(2)]
+    outs = []
+    for p in procs:
+        try:
+            outs.append((p.communicate(timeout=600)[0], p.returncode))
+        except subprocess.TimeoutExpired:
+            for q in procs:
+                q.kill()
+            raise
+    for out, rc in outs:
+        assert "WARNING: ThreadSanitizer" not in out, out[-4000:]
+        assert rc == 0, out[-3000:]
+    assert "ALL TESTS PASSED" in outs[0][0]
