@@ -1323,7 +1323,11 @@ class CudaPlan final : public DevicePlan {
         if (e == cudaSuccess) e = launch_pull(*b, ctas, 256, cs, &launched);
         nodes_ += launched;
       }
-    if (e == cudaSuccess) {  // waits (if any), then the epoch bump
+    // waits (if any), then the epoch bump; a plan whose every message stays
+    // on this GPU has no flags, so no epoch to advance and no launch here
+    bool flags = wait_.n > 0;
+    for (auto& m : recvs) flags |= m.mode == PlanMode::Device;
+    if (e == cudaSuccess && flags) {
       e = launch_wait(wait_, cs);
       ++nodes_;
     }
