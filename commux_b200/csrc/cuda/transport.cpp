@@ -176,8 +176,7 @@ void emit_descs(const char* sp, char* dp, std::vector<Dim> dims, std::int64_t el
   std::int64_t step0 = std::max<std::int64_t>(1, static_cast<std::int64_t>(kMaxUnitsPerDesc) / per0);
   for (std::int64_t s0 = 0; s0 < dims[0].size; s0 += step0) {
     std::int64_t n0 = std::min(step0, dims[0].size - s0);
-    PullDesc d;
-    std::memset(&d, 0, sizeof(d));
+    PullDesc d{};
     d.src = sp + s0 * dims[0].ss;
     d.dst = dp + s0 * dims[0].ds;
     d.ndim = static_cast<std::uint32_t>(dims.size());
@@ -743,9 +742,7 @@ void CudaTransport::build_descs(const ReqPtr& r, const char* blob, std::size_t l
     }
   }
   if (out.empty()) {
-    PullDesc d;
-    std::memset(&d, 0, sizeof(d));
-    for (int k = 0; k < kMaxPullDims; ++k) d.div[k] = FastDiv(1);
+    PullDesc d{};
     d.ndim = 1;
     d.unit = 1;
     d.units = 0;
@@ -837,8 +834,7 @@ void CudaTransport::launch_batch(DevCtx* c, std::vector<PendingPull>& pulls, cud
   std::uint32_t* counters = c->scratch(stream);
   std::uint32_t nmsg = static_cast<std::uint32_t>(pulls.size());
   std::uint32_t next = c->take_slots(stream, nmsg);
-  PullBatch b;
-  std::memset(&b, 0, sizeof(b));
+  PullBatch b{};
   b.counters = counters;
   b.status = c->status_d;
   const int ctas = pull_ctas(c);

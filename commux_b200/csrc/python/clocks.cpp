@@ -78,17 +78,24 @@ void Sampler::start() {
   stop_.store(false);
   thread_ = std::thread([this] {
     Nvml& n = nvml();
-    while (!stop_.load()) {
+    // the clock and the event reasons every sample; the maximum clock and
+    // the power (slower queries) on every 16th, carried in between
+    unsigned int smax = 0, power = 0;
+    for (std::uint64_t k = 0; !stop_.load(); ++k) {
       Sample s;
       s.t_us = std::chrono::duration_cast<std::chrono::microseconds>(
                    std::chrono::steady_clock::now().time_since_epoch())
                    .count();
       unsigned int v = 0;
       if (n.clock(dev_, kNvmlClockSm, &v) == 0) s.sm_mhz = v;
-      if (n.max_clock(dev_, kNvmlClockSm, &v) == 0) s.sm_max_mhz = v;
       unsigned long long rs = 0;
       if (n.reasons(dev_, &rs) == 0) s.reasons = rs;
-      if (n.power(dev_, &v) == 0) s.power_mw = v;
+      if (k % 16 == 0) {
+        if (n.max_clock(dev_, kNvmlClockSm, &v) == 0) smax = v;
+        if (n.power(dev_, &v) == 0) power = v;
+      }
+      s.sm_max_mhz = smax;
+      s.power_mw = power;
       {
         std::lock_guard<std::mutex> lk(mu_);
         samples_.push_back(s);
