@@ -35,6 +35,12 @@ def test_config1_bit_exact_4ranks():
     check(run("config1.py", 4, timeout=240))
 
 
+def test_config1_two_copy_rendezvous():
+    # same workload with the single-copy read switched off (ring + CTS path)
+    out = check(run("config1.py", 2, env={"COMMUX_CMA": "0"}, timeout=180))
+    assert "PASSED" in out[0][1]
+
+
 @pytest.mark.parametrize("coalesce,group", [("0", "0"), ("1", "0"), ("0", "1"), ("1", "1")])
 def test_coalesce_and_group(coalesce, group):
     check(run("coalesce.py", 3, env={"COMMUX_COALESCE": coalesce, "COMMUX_GROUP": group}))
