@@ -75,6 +75,9 @@ struct PullBatch {
   // *epoch (device memory, advanced once per start by the plan's last launch),
   // so a plan's launches never change and replay as one CUDA graph
   const std::uint64_t* epoch;
+  // COMMUX_PLAN_TRACE: [0] = earliest CTA start, [1] = latest CTA end
+  // (%globaltimer, ns; host-mapped, atomics), nullptr otherwise
+  unsigned long long* trace;
   // flags stored (release, system scope) by the first CTA at kernel entry,
   // value *epoch: the "data ready" signals of a plan whose sends need no
   // packing ride on its pull launch instead of a launch of their own
@@ -90,6 +93,7 @@ struct WaitBatch {
   unsigned long long* status;
   const std::uint64_t* epoch;  // non-null: every val is *epoch (plans)
   std::uint64_t* bump;         // non-null: *bump += 1 once every wait is over
+  unsigned long long* trace;   // as PullBatch::trace
   const std::uint64_t* flag[kMaxWaitFlags];
   std::uint64_t val[kMaxWaitFlags];
 };

@@ -167,6 +167,14 @@ struct InlineSrc {
   __device__ unsigned long long* status() const { return b.status; }
   __device__ std::uint64_t timeout_ns() const { return b.timeout_ns; }
   __device__ std::uint64_t epoch() const { return b.epoch ? *b.epoch : 0; }
+  __device__ void trace_start() const {
+    if (b.trace != nullptr && threadIdx.x == 0) atomicMin(b.trace, globaltimer_ns());
+  }
+  __device__ void trace_end() const {
+    if (b.trace == nullptr) return;
+    __syncthreads();
+    if (threadIdx.x == 0) atomicMax(b.trace + 1, globaltimer_ns());
+  }
   __device__ void entry_signals(std::uint64_t epoch) const {
     if (blockIdx.x == 0 && threadIdx.x < b.nsig) {
       fence_acq_rel_sys();
@@ -203,6 +211,7 @@ __device__ __forceinline__ void pull_body(const S& s) {
   constexpr std::uint32_t kFailBit = 0x80000000u;
   const std::uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const std::uint64_t epoch = s.epoch();
+  s.trace_start();
   s.entry_signals(epoch);
   for (std::uint32_t c = blockIdx.x; c < s.total(); c += gridDim.x) {
     const PullDesc& d = s.desc(find_desc(s, c));
@@ -242,6 +251,7 @@ __device__ __forceinline__ void pull_body(const S& s) {
       }
     }
   }
+  s.trace_end();
 }
 
 // One instantiation per unit size U (U == 0: the 64-bit-stride walk for wide
@@ -273,6 +283,7 @@ __global__ void wait_kernel(const __grid_constant__ WaitBatch b) {
 // As wait_kernel, then (plans) advance the epoch once every lane is done.
 __global__ void wait_bump_kernel(const __grid_constant__ WaitBatch b) {
   const std::uint32_t i = threadIdx.x;
+  if (b.trace != nullptr && i == 0) atomicMin(b.trace, globaltimer_ns());
   if (i < b.n) {
     const std::uint64_t want = *b.epoch;
     const std::uint64_t t0 = globaltimer_ns();
@@ -287,7 +298,10 @@ __global__ void wait_bump_kernel(const __grid_constant__ WaitBatch b) {
     }
   }
   __syncthreads();
-  if (i == 0) *b.bump += 1;
+  if (i == 0) {
+    *b.bump += 1;
+    if (b.trace != nullptr) atomicMax(b.trace + 1, globaltimer_ns());
+  }
 }
 
 }  // namespace
@@ -340,6 +354,7 @@ cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStrea
   sub.status = b.status;
   sub.timeout_ns = b.timeout_ns;
   sub.epoch = b.epoch;
+  sub.trace = b.trace;
   sub.nsig = 0;  // entry signals go with the first class launched
   bool first_launch = true;
   for (int cls : {16, 8, 4, 2, 1, 0}) {

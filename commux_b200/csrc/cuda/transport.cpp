@@ -1147,6 +1147,7 @@ class CudaPlan final : public DevicePlan {
     if (!select_device_quiet(c_->dev)) return;  // context gone at process exit
     if (exec_) cudaGraphExecDestroy(exec_);
     if (graph_) cudaGraphDestroy(graph_);
+    if (trace_h_) cudaFreeHost(trace_h_);
     cudaGetLastError();
   }
   std::vector<Msg> sends, recvs;
@@ -1212,6 +1213,20 @@ class CudaPlan final : public DevicePlan {
                     kMaxWaitFlags, " sends to other GPUs");
         wait_.flag[wait_.n++] = m.consumed_local;
       }
+    // COMMUX_PLAN_TRACE: span of every launch of a start (earliest CTA start,
+    // latest CTA end), printed after each start (which then synchronises)
+    if (env_int("COMMUX_PLAN_TRACE", 0) != 0) {
+      const std::size_t n = pre_.size() + pulls_.size() + 1;
+      CMX_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&trace_h_), n * 2 * sizeof(unsigned long long),
+                             cudaHostAllocMapped));
+      unsigned long long* d = nullptr;
+      CMX_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&d), trace_h_, 0));
+      std::size_t k = 0;
+      for (auto* ls : {&pre_, &pulls_})
+        for (auto& b : *ls) b->trace = d + 2 * k++;
+      wait_.trace = d + 2 * k;
+      trace_n_ = n;
+    }
   }
 
   void start() override {
@@ -1236,8 +1251,14 @@ class CudaPlan final : public DevicePlan {
       tr_->end_batch();
     }
     if (!exec_) capture();
+    if (trace_h_ != nullptr)
+      for (std::size_t k = 0; k < trace_n_; ++k) {
+        trace_h_[2 * k] = ~0ull;
+        trace_h_[2 * k + 1] = 0;
+      }
     CMX_CUDA(cudaGraphLaunch(exec_, cur));
     tr_->kernel_launches += nodes_;
+    if (trace_h_ != nullptr) report_trace(cur);
     if (!shared.empty()) {
       for (auto& r : shared) eng_->wait(r, std::chrono::milliseconds(0));
       tr_->stream_wait_all(shared);
@@ -1258,6 +1279,27 @@ class CudaPlan final : public DevicePlan {
   std::int64_t n_shared_ = 0;
 
  private:
+  void report_trace(cudaStream_t cur) {
+    CMX_CUDA(cudaStreamSynchronize(cur));
+    unsigned long long t0 = ~0ull;
+    for (std::size_t k = 0; k < trace_n_; ++k) t0 = std::min(t0, trace_h_[2 * k]);
+    std::string line;
+    char buf[96];
+    std::size_t k = 0;
+    auto span = [&](const char* what) {
+      const unsigned long long a = trace_h_[2 * k], b = trace_h_[2 * k + 1];
+      ++k;
+      if (a == ~0ull) return;  // launch left out of this plan's graph
+      std::snprintf(buf, sizeof(buf), " %s %.1f-%.1f", what, (a - t0) / 1e3, (b - t0) / 1e3);
+      line += buf;
+    };
+    for (std::size_t i = 0; i < pre_.size(); ++i) span("pack");
+    for (std::size_t i = 0; i < pulls_.size(); ++i) span("pull");
+    span("wait");
+    std::fprintf(stderr, "[commux plan trace rank %d] start %llu, us from the first CTA:%s\n", eng_->rank(),
+                 static_cast<unsigned long long>(starts_), line.c_str());
+  }
+
   // Messages -> parameter blocks of at most kMaxBatch descriptors, one unit
   // class each; every message counts into its own counter slot (the plan's
   // launches run one after another and each message returns its counter to
@@ -1348,6 +1390,8 @@ class CudaPlan final : public DevicePlan {
   cudaGraph_t graph_ = nullptr;
   cudaGraphExec_t exec_ = nullptr;
   std::int64_t nodes_ = 0;
+  unsigned long long* trace_h_ = nullptr;  // COMMUX_PLAN_TRACE (host-mapped)
+  std::size_t trace_n_ = 0;
 };
 
 std::vector<PullDesc> CudaTransport::plan_descs(const char* wire, std::size_t len, int src, bool local,
