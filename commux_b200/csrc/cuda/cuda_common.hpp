@@ -75,9 +75,11 @@ struct PullBatch {
   // *epoch (device memory, advanced once per start by the plan's last launch),
   // so a plan's launches never change and replay as one CUDA graph
   const std::uint64_t* epoch;
-  // COMMUX_PLAN_TRACE: [0] = earliest CTA start, [1] = latest CTA end
-  // (%globaltimer, ns; host-mapped, atomics), nullptr otherwise
+  // COMMUX_PLAN_TRACE: [0] = start of CTA 0, [1] = end of the last CTA
+  // (%globaltimer, ns; host-mapped); trace_count (device memory) finds the
+  // last CTA. nullptr otherwise
   unsigned long long* trace;
+  unsigned int* trace_count;
   // flags stored (release, system scope) by the first CTA at kernel entry,
   // value *epoch: the "data ready" signals of a plan whose sends need no
   // packing ride on its pull launch instead of a launch of their own
@@ -93,7 +95,7 @@ struct WaitBatch {
   unsigned long long* status;
   const std::uint64_t* epoch;  // non-null: every val is *epoch (plans)
   std::uint64_t* bump;         // non-null: *bump += 1 once every wait is over
-  unsigned long long* trace;   // as PullBatch::trace
+  unsigned long long* trace;   // as PullBatch::trace (one CTA)
   const std::uint64_t* flag[kMaxWaitFlags];
   std::uint64_t val[kMaxWaitFlags];
 };

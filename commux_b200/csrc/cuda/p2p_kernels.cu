@@ -168,12 +168,18 @@ struct InlineSrc {
   __device__ std::uint64_t timeout_ns() const { return b.timeout_ns; }
   __device__ std::uint64_t epoch() const { return b.epoch ? *b.epoch : 0; }
   __device__ void trace_start() const {
-    if (b.trace != nullptr && threadIdx.x == 0) atomicMin(b.trace, globaltimer_ns());
+    if (b.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0) b.trace[0] = globaltimer_ns();
   }
   __device__ void trace_end() const {
     if (b.trace == nullptr) return;
     __syncthreads();
-    if (threadIdx.x == 0) atomicMax(b.trace + 1, globaltimer_ns());
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(b.trace_count, 1u) == gridDim.x - 1) {  // the last CTA of the launch
+        b.trace[1] = globaltimer_ns();
+        *b.trace_count = 0u;
+      }
+    }
   }
   __device__ void entry_signals(std::uint64_t epoch) const {
     if (blockIdx.x == 0 && threadIdx.x < b.nsig) {
@@ -283,7 +289,7 @@ __global__ void wait_kernel(const __grid_constant__ WaitBatch b) {
 // As wait_kernel, then (plans) advance the epoch once every lane is done.
 __global__ void wait_bump_kernel(const __grid_constant__ WaitBatch b) {
   const std::uint32_t i = threadIdx.x;
-  if (b.trace != nullptr && i == 0) atomicMin(b.trace, globaltimer_ns());
+  if (b.trace != nullptr && i == 0) b.trace[0] = globaltimer_ns();
   if (i < b.n) {
     const std::uint64_t want = *b.epoch;
     const std::uint64_t t0 = globaltimer_ns();
@@ -300,7 +306,7 @@ __global__ void wait_bump_kernel(const __grid_constant__ WaitBatch b) {
   __syncthreads();
   if (i == 0) {
     *b.bump += 1;
-    if (b.trace != nullptr) atomicMax(b.trace + 1, globaltimer_ns());
+    if (b.trace != nullptr) b.trace[1] = globaltimer_ns();
   }
 }
 
@@ -355,6 +361,7 @@ cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStrea
   sub.timeout_ns = b.timeout_ns;
   sub.epoch = b.epoch;
   sub.trace = b.trace;
+  sub.trace_count = b.trace_count;
   sub.nsig = 0;  // entry signals go with the first class launched
   bool first_launch = true;
   for (int cls : {16, 8, 4, 2, 1, 0}) {

@@ -1160,31 +1160,54 @@ class CudaPlan final : public DevicePlan {
   // the plan's epoch, read from device memory, so the launches never change:
   // they are captured once into a CUDA graph and a start is one graph launch.
   void finalize() {
-    std::vector<std::vector<PullDesc>> pre, pull;
-    std::vector<std::uint64_t*> ready_only;  // device sends that need no packing
-    bool any_pack = false;
-    for (auto& m : sends)
-      if (m.mode == PlanMode::Device) {
-        any_pack |= !m.pack.empty();
-        if (m.pack.empty()) ready_only.push_back(m.ready_remote);
+    // Sends to another GPU: packed ones (their "ready" is stored by the last
+    // warp of the pack), the rest signal "ready" at the entry of the plan's
+    // first launch.
+    std::vector<std::vector<PullDesc>> packs, pull;
+    std::vector<std::uint64_t*> ready_only;
+    for (auto& m : sends) {
+      if (m.mode != PlanMode::Device) continue;
+      if (m.pack.empty()) {
+        ready_only.push_back(m.ready_remote);
+        continue;
       }
+      std::vector<PullDesc> d = m.pack;
+      for (auto& x : d) x.done = m.ready_remote;
+      packs.push_back(std::move(d));
+    }
     for (auto& m : recvs)
       if (m.mode != PlanMode::Shared && !m.descs.empty()) pull.push_back(m.descs);
-    // without packing, the "ready" signals ride on the first pull launch
-    const bool entry_signals = !any_pack && !pull.empty() && ready_only.size() <= kMaxEntrySignals;
-    for (auto& m : sends) {
-      if (m.mode != PlanMode::Device || entry_signals) continue;
-      std::vector<PullDesc> d = m.pack;
-      if (d.empty()) {  // a pure signal: zero units, the flag store only
-        PullDesc x{};
-        x.ndim = 1;
-        x.unit = 16;
-        x.units = 0;
-        x.nchunks = 1;
-        d.push_back(x);
-      }
-      for (auto& x : d) x.done = m.ready_remote;
-      pre.push_back(std::move(d));
+    // The packs ride in the pull launch, ahead of every pull chunk, when all
+    // of them share the pull launch's unit class: each CTA (all resident,
+    // the grid is capped at residency) finishes its pack chunks before it
+    // waits on any peer's "ready". Otherwise they get a launch of their own
+    // before the pulls.
+    bool merge = !packs.empty() && !pull.empty();
+    // one launch only: a pack split into a later launch of the peer, behind
+    // pulls that wait, could leave two ranks waiting on each other
+    std::size_t ndesc = 0;
+    for (auto* v : {&packs, &pull})
+      for (auto& m : *v) ndesc += m.size();
+    merge = merge && ndesc <= static_cast<std::size_t>(kMaxBatch);
+    if (merge) {
+      const int cls = pull_unit_class(pull[0][0]);
+      for (auto& m : pull) merge = merge && pull_unit_class(m[0]) == cls;
+      for (auto& m : packs) merge = merge && pull_unit_class(m[0]) == cls;
+    }
+    std::vector<std::vector<PullDesc>> pre;
+    if (merge) {
+      pull.insert(pull.begin(), packs.begin(), packs.end());
+    } else {
+      pre = packs;
+    }
+    // no launch at all would carry the entry signals: a pure-signal launch
+    if (pre.empty() && pull.empty() && !ready_only.empty()) {
+      PullDesc x{};
+      x.ndim = 1;
+      x.unit = 16;
+      x.units = 0;
+      x.nchunks = 1;
+      pre.push_back({x});
     }
     // device state: [epoch u64, starts at 1][counters u32 x kCounterSlots]
     const std::size_t state_bytes = 64 + kCounterSlots * sizeof(std::uint32_t);
@@ -1198,9 +1221,12 @@ class CudaPlan final : public DevicePlan {
     CMX_CUDA(cudaMemcpy(state_.data_ptr(), init.data(), state_bytes, cudaMemcpyHostToDevice));
     pre_ = batches(pre);
     pulls_ = batches(pull);
-    if (entry_signals) {
-      pulls_[0]->nsig = static_cast<std::uint32_t>(ready_only.size());
-      for (std::size_t k = 0; k < ready_only.size(); ++k) pulls_[0]->sig[k] = ready_only[k];
+    if (!ready_only.empty()) {
+      TORCH_CHECK(ready_only.size() <= static_cast<std::size_t>(kMaxEntrySignals), "commux plan: more than ",
+                  kMaxEntrySignals, " unpacked sends to other GPUs");
+      PullBatch& first = pre_.empty() ? *pulls_[0] : *pre_[0];
+      first.nsig = static_cast<std::uint32_t>(ready_only.size());
+      for (std::size_t k = 0; k < ready_only.size(); ++k) first.sig[k] = ready_only[k];
     }
     std::memset(&wait_, 0, sizeof(wait_));
     wait_.timeout_ns = tr_->device_timeout_ns();
@@ -1222,8 +1248,14 @@ class CudaPlan final : public DevicePlan {
       unsigned long long* d = nullptr;
       CMX_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&d), trace_h_, 0));
       std::size_t k = 0;
+      // the last message-counter slot is the launches' CTA counter (reset
+      // by the last CTA of each launch)
+      std::uint32_t* count = counters_d_ + (kCounterSlots - 1);
       for (auto* ls : {&pre_, &pulls_})
-        for (auto& b : *ls) b->trace = d + 2 * k++;
+        for (auto& b : *ls) {
+          b->trace = d + 2 * k++;
+          b->trace_count = count;
+        }
       wait_.trace = d + 2 * k;
       trace_n_ = n;
     }
@@ -1289,7 +1321,7 @@ class CudaPlan final : public DevicePlan {
     auto span = [&](const char* what) {
       const unsigned long long a = trace_h_[2 * k], b = trace_h_[2 * k + 1];
       ++k;
-      if (a == ~0ull) return;  // launch left out of this plan's graph
+      if (a == ~0ull || b == 0) return;  // launch left out of this plan's graph
       std::snprintf(buf, sizeof(buf), " %s %.1f-%.1f", what, (a - t0) / 1e3, (b - t0) / 1e3);
       line += buf;
     };
@@ -1315,7 +1347,7 @@ class CudaPlan final : public DevicePlan {
         TORCH_CHECK(pull_unit_class(d) == cls, "commux plan: a message mixes unit classes");
         chunks += d.nchunks;
       }
-      TORCH_CHECK(slot < kCounterSlots, "commux plan: too many messages");
+      TORCH_CHECK(slot < kCounterSlots - 1, "commux plan: too many messages");
       auto& v = by_cls[cls];
       for (auto d : m) {
         d.counter_idx = slot;
@@ -1351,7 +1383,9 @@ class CudaPlan final : public DevicePlan {
   void capture() {
     cudaStream_t cs = nullptr;
     CMX_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
-    const int ctas = tr_->pull_ctas(c_);
+    // every CTA resident at once: a CTA never waits on a peer while another
+    // CTA of the launch that still has pack work waits for an SM
+    const int ctas = std::min(tr_->pull_ctas(c_), 4 * c_->sm_count);
     nodes_ = 0;
     CMX_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
     cudaError_t e = cudaSuccess;
