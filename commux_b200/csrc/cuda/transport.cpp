@@ -1383,9 +1383,12 @@ class CudaPlan final : public DevicePlan {
   void capture() {
     cudaStream_t cs = nullptr;
     CMX_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
-    // every CTA resident at once: a CTA never waits on a peer while another
-    // CTA of the launch that still has pack work waits for an SM
-    const int ctas = std::min(tr_->pull_ctas(c_), 4 * c_->sm_count);
+    // a launch whose CTAs wait on peers keeps every CTA resident at once, so
+    // a CTA never waits while another CTA of the launch that still has pack
+    // work waits for an SM; launches without waits keep the wider grid
+    bool waits = false;
+    for (auto& m : recvs) waits |= m.mode == PlanMode::Device;
+    const int ctas = waits ? std::min(tr_->pull_ctas(c_), 4 * c_->sm_count) : tr_->pull_ctas(c_);
     nodes_ = 0;
     CMX_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
     cudaError_t e = cudaSuccess;
