@@ -1145,6 +1145,9 @@ class CudaPlan final : public DevicePlan {
   CudaPlan(CudaTransport* tr, Engine* eng, DevCtx* c) : tr_(tr), eng_(eng), c_(c) {}
   ~CudaPlan() override {
     if (!select_device_quiet(c_->dev)) return;  // context gone at process exit
+    // the last start may still run: its buffers (state_, staging) must not be
+    // handed to other work before it is done
+    if (last_stream_ != nullptr) cudaStreamSynchronize(last_stream_);
     if (exec_) cudaGraphExecDestroy(exec_);
     if (graph_) cudaGraphDestroy(graph_);
     if (trace_h_) cudaFreeHost(trace_h_);
@@ -1283,6 +1286,7 @@ class CudaPlan final : public DevicePlan {
       tr_->end_batch();
     }
     if (!exec_) capture();
+    last_stream_ = cur;
     if (trace_h_ != nullptr)
       for (std::size_t k = 0; k < trace_n_; ++k) {
         trace_h_[2 * k] = ~0ull;
@@ -1429,6 +1433,7 @@ class CudaPlan final : public DevicePlan {
   std::int64_t nodes_ = 0;
   unsigned long long* trace_h_ = nullptr;  // COMMUX_PLAN_TRACE (host-mapped)
   std::size_t trace_n_ = 0;
+  cudaStream_t last_stream_ = nullptr;      // stream of the last start
 };
 
 std::vector<PullDesc> CudaTransport::plan_descs(const char* wire, std::size_t len, int src, bool local,
