@@ -26,7 +26,9 @@ def _has_cuda_sources() -> bool:
 
 def build(build_dir: str | None = None, jobs: int | None = None, verbose: bool = False,
           sanitize: str = "", device_checks: bool = False, cuda: bool | None = None) -> None:
-    build_dir = build_dir or os.path.join(REPO, "build" if not sanitize else f"build-{sanitize}")
+    if build_dir is None:
+        build_dir = os.path.join(REPO, f"build-{sanitize}" if sanitize else
+                                 "build-devchecks" if device_checks else "build")
     os.makedirs(build_dir, exist_ok=True)
     if cuda is None:
         cuda = _has_cuda_sources() and os.path.exists("/usr/local/cuda/bin/nvcc") and not sanitize
@@ -39,6 +41,10 @@ def build(build_dir: str | None = None, jobs: int | None = None, verbose: bool =
     if sanitize:
         # host libraries and the C++ test driver only, inside the build tree
         cfg += [f"-DCOMMUX_SANITIZE={sanitize}", "-DCOMMUX_BUILD_PYTHON=OFF"]
+    elif device_checks:
+        # the libraries with bounds-checking kernels, inside the build tree
+        # (<build_dir>/lib); the package keeps the production kernels
+        cfg += ["-DCOMMUX_BUILD_PYTHON=OFF"]
     env = dict(os.environ)
     env.setdefault("CUDACXX", "/usr/local/cuda/bin/nvcc")
     # Use the system compiler, which links the shared libstdc++ that torch

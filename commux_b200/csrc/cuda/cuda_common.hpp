@@ -63,6 +63,13 @@ struct PullDesc {
   // this GPU's memory that the sender's stream sets); nullptr: no wait
   const std::uint64_t* ready;
   std::uint64_t ready_val;
+#if defined(COMMUX_DEVICE_CHECKS)
+  // bounds-check build: the byte offsets from src / dst that the copy may
+  // touch, [lo, hi). A unit outside them is skipped and reported in the
+  // status word (kStatusBadDescriptor) instead of being accessed. lo == hi
+  // == 0 (a value-initialised descriptor): no limit declared.
+  std::int64_t src_lo, src_hi, dst_lo, dst_hi;
+#endif
 };
 
 struct PullBatch {
@@ -87,6 +94,8 @@ struct PullBatch {
   std::uint64_t* sig[kMaxEntrySignals];
   PullDesc d[kMaxBatch];
 };
+// passed by value as a __grid_constant__ kernel parameter (limit 32764 bytes)
+static_assert(sizeof(PullBatch) <= 32764, "PullBatch exceeds the kernel parameter space");
 
 // Flags a wait kernel polls (all in this GPU's own memory, written remotely).
 struct WaitBatch {

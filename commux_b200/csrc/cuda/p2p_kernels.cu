@@ -49,12 +49,37 @@ __device__ __forceinline__ void unit_offsets(const PullDesc& d, std::uint32_t u,
   dof += static_cast<std::int64_t>(rem) * static_cast<S>(d.dstr[0]);
 }
 
+// Bounds-check build: true when the `bytes` bytes at byte offsets `so`
+// (source) and `dof` (destination) lie inside the descriptor's declared
+// limits; otherwise records the first violation (source address, offsets) in
+// the status word and the caller skips the unit. Always true in the
+// production build.
+__device__ __forceinline__ bool unit_ok(const PullDesc& d, std::int64_t so, std::int64_t dof,
+                                        std::int64_t bytes, unsigned long long* status) {
+#if defined(COMMUX_DEVICE_CHECKS)
+  const bool s_ok = (d.src_lo == 0 && d.src_hi == 0) || (so >= d.src_lo && so + bytes <= d.src_hi);
+  const bool d_ok = (d.dst_lo == 0 && d.dst_hi == 0) || (dof >= d.dst_lo && dof + bytes <= d.dst_hi);
+  if (s_ok && d_ok) return true;
+  report_status(status, kStatusBadDescriptor, reinterpret_cast<unsigned long long>(d.src),
+                static_cast<unsigned long long>(so), static_cast<unsigned long long>(dof));
+  return false;
+#else
+  (void)d;
+  (void)so;
+  (void)dof;
+  (void)bytes;
+  (void)status;
+  return true;
+#endif
+}
+
 // One warp copies units [u0, u1): lane l takes u0 + l, u0 + l + 32, ...,
 // kUnroll loads in flight before the stores. A unit is (row, column) of the
 // innermost dim; a lane re-derives the row's offsets over the outer dims only
 // when its row changes, so most units cost one division.
 template <int U>
-__device__ __forceinline__ void copy_units(const PullDesc& d, std::uint32_t u0, std::uint32_t u1) {
+__device__ __forceinline__ void copy_units(const PullDesc& d, std::uint32_t u0, std::uint32_t u1,
+                                           unsigned long long* status) {
   using V = typename VecT<U>::T;
   constexpr std::uint32_t step = 32;
   constexpr int in = kMaxPullDims - 1;
@@ -68,6 +93,7 @@ __device__ __forceinline__ void copy_units(const PullDesc& d, std::uint32_t u0, 
   for (std::uint32_t base = u0 + (threadIdx.x & 31u); base < u1; base += step * kUnroll) {
     V v[kUnroll];
     std::int64_t dofs[kUnroll];
+    std::uint32_t skip = 0;
 #pragma unroll
     for (int k = 0; k < kUnroll; ++k) {
       const std::uint32_t u = base + k * step;
@@ -91,13 +117,17 @@ __device__ __forceinline__ void copy_units(const PullDesc& d, std::uint32_t u0, 
           rdo += static_cast<std::int64_t>(rem) * static_cast<std::int32_t>(d.dstr[0]);
         }
         dofs[k] = rdo + static_cast<std::int64_t>(col) * cds;
-        v[k] = *reinterpret_cast<const V*>(src + rso + static_cast<std::int64_t>(col) * css);
+        const std::int64_t so = rso + static_cast<std::int64_t>(col) * css;
+        if (unit_ok(d, so, dofs[k], U, status))
+          v[k] = *reinterpret_cast<const V*>(src + so);
+        else
+          skip |= 1u << k;  // bounds-check build only: no load, no store
       }
     }
 #pragma unroll
     for (int k = 0; k < kUnroll; ++k) {
       const std::uint32_t u = base + k * step;
-      if (u < u1) *reinterpret_cast<V*>(dst + dofs[k]) = v[k];
+      if (u < u1 && (skip & (1u << k)) == 0u) *reinterpret_cast<V*>(dst + dofs[k]) = v[k];
     }
   }
 }
@@ -111,10 +141,12 @@ __device__ __forceinline__ void copy_one(const char* s, char* d) {
 // Descriptors with a stride of 2 GiB or more: one unit at a time, 64-bit
 // strides (layouts this wide are rare; kept out of line so the common loop
 // keeps its registers).
-__device__ __noinline__ void copy_units_wide(const PullDesc& d, std::uint32_t u0, std::uint32_t u1) {
+__device__ __noinline__ void copy_units_wide(const PullDesc& d, std::uint32_t u0, std::uint32_t u1,
+                                             unsigned long long* status) {
   for (std::uint32_t u = u0 + (threadIdx.x & 31u); u < u1; u += 32) {
     std::int64_t so, dof;
     unit_offsets<std::int64_t>(d, u, so, dof);
+    if (!unit_ok(d, so, dof, d.unit, status)) continue;
     switch (d.unit) {
       case 16:
         copy_one<16>(d.src + so, d.dst + dof);
@@ -236,9 +268,9 @@ __device__ __forceinline__ void pull_body(const S& s) {
     const std::uint32_t per = (end - u0 + kWarps - 1) / kWarps;
     const std::uint32_t wlo = min(end, u0 + warp * per), whi = min(end, wlo + per);
     if constexpr (U == 0)
-      copy_units_wide(d, wlo, whi);
+      copy_units_wide(d, wlo, whi, s.status());
     else
-      copy_units<U>(d, wlo, whi);
+      copy_units<U>(d, wlo, whi, s.status());
     std::uint64_t* done = d.done;
     if (done == nullptr) continue;
     __syncwarp();  // every load of this warp's slice has returned

@@ -208,8 +208,9 @@ void emit_descs(const char* sp, char* dp, std::vector<Dim> dims, std::int64_t el
 // Host-side bounds check of every descriptor before launch: the bytes a
 // descriptor touches must lie inside the source allocation (the IPC mapping)
 // and the destination storage. A layout bug then raises here instead of
-// reaching the GPU as an out-of-bounds access.
-void check_desc(const PullDesc& d, std::uintptr_t src_lo, std::uintptr_t src_hi,
+// reaching the GPU as an out-of-bounds access. The bounds-check build also
+// hands the same limits to the kernel, which checks every unit it copies.
+void check_desc(PullDesc& d, std::uintptr_t src_lo, std::uintptr_t src_hi,
                 std::uintptr_t dst_lo, std::uintptr_t dst_hi) {
   if (d.units == 0) return;
   std::int64_t s_min = 0, s_max = 0, d_min = 0, d_max = 0;
@@ -227,6 +228,12 @@ void check_desc(const PullDesc& d, std::uintptr_t src_lo, std::uintptr_t src_hi,
   if (!ok)
     throw std::runtime_error("commux: internal error, a copy descriptor leaves its buffers "
                              "(layout bug caught before launch)");
+#if defined(COMMUX_DEVICE_CHECKS)
+  d.src_lo = static_cast<std::intptr_t>(src_lo) - sp;
+  d.src_hi = static_cast<std::intptr_t>(src_hi) - sp;
+  d.dst_lo = static_cast<std::intptr_t>(dst_lo) - dp;
+  d.dst_hi = static_cast<std::intptr_t>(dst_hi) - dp;
+#endif
 }
 
 bool contiguous_wire(const SegWire& s) {
@@ -1041,6 +1048,10 @@ std::string CudaTransport::device_error() {
       os << "commux: a device-side wait on GPU " << kv.first << " gave up after "
          << timeout_ns_ / 1000000 << " ms (flag 0x" << std::hex << st[1] << std::dec
          << " wanted " << st[2] << ", saw " << st[3] << "); the peer never completed its side";
+    else if (code == kStatusBadDescriptor)
+      os << "commux: a copy on GPU " << kv.first << " left its declared bounds (source 0x" << std::hex
+         << st[1] << std::dec << ", byte offsets " << static_cast<long long>(st[2]) << " / "
+         << static_cast<long long>(st[3]) << "); the unit was skipped";
     else if (code == kStatusCollTimeout)
       os << "commux: a device collective on GPU " << kv.first << " timed out waiting for rank "
          << st[1] << " (barrier epoch " << st[2] << ")";

@@ -115,3 +115,19 @@ def test_tcp_cuda_p2p_staged():
 
 def test_tcp_cuda_collectives_staged():
     check(run("collectives.py", 2, env=dict(CUDA, COMMUX_TRANSPORT="tcp", CMX_A2A="1"), timeout=240))
+
+
+def test_device_bounds_checks():
+    """The bounds-check build (kernels test every unit against the limits the
+    host derived, and report instead of touching memory outside them) passes
+    its self-test; the production library has the checks compiled out."""
+    lib = os.path.join(ROOT, "build-devchecks", "lib", "libcommux_cuda.so")
+    if not os.path.exists(lib):
+        r = subprocess.run([sys.executable, "-m", "commux_b200.build", "--device-checks"], cwd=ROOT,
+                           capture_output=True, text=True, timeout=1200)
+        assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    worker = os.path.join(ROOT, "tests", "workers", "device_checks.py")
+    prod = os.path.join(ROOT, "commux_b200", "lib", "libcommux_cuda.so")
+    for which, path in (("checked", lib), ("production", prod)):
+        r = subprocess.run([sys.executable, worker, which, path], capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0 and "PASS" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
