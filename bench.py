@@ -38,6 +38,23 @@ METRIC = "tagged halo-exchange GB/s (26-direction, 1024^3 fp64, halo 2, 7-point 
 BASELINE_VALUE = None  # the reference publishes no halo-exchange GB/s number
 
 
+NVLINK_GBS = 770.0  # measured peer copy per direction on this B200 model (GB/s)
+
+
+def measured_hbm_gbs() -> tuple[float, str]:
+    """HBM copy rate for the roofline: MEASURED_PEAKS.json beside this file
+    when present, else an earlier measurement of the same B200 model."""
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            v = float(json.load(f)["hbm_gbs"])
+        if v > 0:
+            return v, "of measured"
+    except (OSError, ValueError, KeyError, TypeError):
+        pass
+    return 6650.0, "of fallback"
+
+
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -107,6 +124,7 @@ def main() -> None:
     model = Jacobi3D(gn, halo=args.halo, dims=dims, dtype=dtype, seed=0)
     bytes_rank = model.halo_bytes
     bytes_job = int(rank_sum([bytes_rank])[0])
+    remote_rank = int(rank_max([model.halo.remote_bytes(model.u.element_size(), rank)])[0])
 
     def cuda_launches():
         s = commux.stats(device="cpu")
@@ -188,6 +206,12 @@ def main() -> None:
     e2e_wall_max = rank_max([e2e_wall])[0]
 
     value = bytes_job * K / (exch_sum_max * 1e-3) / 1e9
+    # roofline of one exchange: the bytes that cross NVLink into the busiest
+    # rank at the measured peer-copy rate, or every byte read and written
+    # once in this GPU's HBM at the measured copy rate, whichever is slower
+    hbm_gbs, hbm_src = measured_hbm_gbs()
+    floor_us = max(remote_rank / NVLINK_GBS / 1e3, 2 * bytes_rank / hbm_gbs / 1e3)
+    exch_p50_us = statistics.median(exch_max) * 1e3
     e2e_value = bytes_job * Ke / e2e_wall_max / 1e9
     if rank == 0:
         line = {
@@ -212,7 +236,13 @@ def main() -> None:
                 "halo_bytes_per_step_per_rank": bytes_rank,
                 "exchange_only_us_p50": round(statistics.median(xonly) * 1e3, 2),
                 "halo_bytes_per_step_job": bytes_job,
-                "exchange_us_p50": round(statistics.median(exch_max) * 1e3, 2),
+                "exchange_us_p50": round(exch_p50_us, 2),
+                "roofline": {"nvlink_bytes_per_step_max_rank": remote_rank,
+                             "floor_us": round(floor_us, 2),
+                             "frac_of_roofline": round(floor_us / exch_p50_us, 3),
+                             "basis": f"max(NVLink bytes / {NVLINK_GBS:.0f} GB/s measured peer copy, "
+                                      f"2 x halo bytes / {hbm_gbs:.0f} GB/s HBM copy ({hbm_src})) "
+                                      "against exchange_us_p50"},
                 "exchange_us_min": round(min(exch_max) * 1e3, 2),
                 "step_ms_p50": round(statistics.median(step_max), 4),
                 "jacobi_gcells_per_s_job": round(

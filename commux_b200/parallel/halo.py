@@ -109,6 +109,15 @@ class HaloExchange:
             total += math.prod(self.h if o else n for o, n in zip(d, self.n)) * elem_size
         return total
 
+    def remote_bytes(self, elem_size: int, rank: int) -> int:
+        """Bytes this rank receives from other ranks per exchange (with one
+        GPU per rank: the bytes that cross NVLink into this GPU)."""
+        total = 0
+        for d in self.directions:
+            if self.grid.neighbor(tuple(-o for o in d)) != rank:
+                total += math.prod(self.h if o else n for o, n in zip(d, self.n)) * elem_size
+        return total
+
     def ops(self, u: torch.Tensor) -> list:
         ops = []
         for d in self.directions:
