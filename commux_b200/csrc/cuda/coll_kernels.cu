@@ -118,14 +118,13 @@ __device__ __forceinline__ std::uint64_t* flag_at(std::uint64_t* base, int phase
 }
 
 // After all threads' stores, thread p stores the flag into rank p's area
-// (every rank when `only` < 0, else only rank `only`).
+// (every rank when `only` < 0, else only rank `only`). The barrier orders the
+// CTA's stores before thread p's flag store, whose release at system scope is
+// cumulative over them, so no separate fence precedes it.
 __device__ __forceinline__ void signal(const CollArgs& a, int phase, std::uint64_t seq, int only = -1) {
   __syncthreads();
   const int p = threadIdx.x;
-  if (p < a.P && (only < 0 || p == only)) {
-    fence_acq_rel_sys();
-    st_release_sys(flag_at(a.flags[p], phase, a.me, blockIdx.x), seq);
-  }
+  if (p < a.P && (only < 0 || p == only)) st_release_sys(flag_at(a.flags[p], phase, a.me, blockIdx.x), seq);
 }
 
 // Thread p waits for rank p's flag (every rank when `only` < 0). Returns false
@@ -302,6 +301,8 @@ __device__ __forceinline__ void gsignal(const CollArgs& a, const Grp& g, int pha
   g.sync();  // every store of the group precedes the flag
   const int p = g.tid();
   if (p < a.P) {
+    // a full fence, unlike signal(): the group's stores include multimem.st
+    // through the multicast object
     fence_acq_rel_sys();
     st_release_sys(flag_at(a.flags[p], phase, a.me, blockIdx.x), seq);
   }

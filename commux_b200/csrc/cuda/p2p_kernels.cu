@@ -213,11 +213,11 @@ struct InlineSrc {
       }
     }
   }
+  // The data these signals announce was written by earlier work on this
+  // stream; the release store at system scope orders it before the flag for
+  // a peer that acquires the flag, so no separate fence precedes it.
   __device__ void entry_signals(std::uint64_t epoch) const {
-    if (blockIdx.x == 0 && threadIdx.x < b.nsig) {
-      fence_acq_rel_sys();
-      st_release_sys(b.sig[threadIdx.x], epoch);
-    }
+    if (blockIdx.x == 0 && threadIdx.x < b.nsig) st_release_sys(b.sig[threadIdx.x], epoch);
   }
 };
 
@@ -283,7 +283,11 @@ __device__ __forceinline__ void pull_body(const S& s) {
         const bool any_failed = failed || (prev & kFailBit) != 0u;
         *counter = 0u;
         if (!any_failed) {
-          fence_acq_rel_sys();
+          // acquire the other warps' slices (their release fences and adds
+          // are GPU-local), then publish all of them to the peer: the store's
+          // release at system scope is cumulative over what this thread has
+          // acquired
+          fence_acq_rel_gpu();
           st_release_sys(done, epoch ? epoch : d.done_val);
         }
       }
