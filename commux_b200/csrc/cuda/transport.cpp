@@ -411,7 +411,7 @@ void CudaTransport::shutdown() {
   flights_.clear();
   std::lock_guard<std::mutex> lk(ipc_mu_);
   if (alive)
-    for (auto& kv : opened_) cudaIpcCloseMemHandle(kv.second);
+    for (auto& kv : opened_) cudaIpcCloseMemHandle(kv.second.ptr);
   opened_.clear();
   cudaGetLastError();
 }
@@ -466,20 +466,38 @@ void CudaTransport::ipc_export(const void* ptr, std::uint64_t* buffer_id, std::u
   st_ipc_exports_++;
 }
 
-void* CudaTransport::ipc_open(int src, std::uint64_t buffer_id, const cudaIpcMemHandle_t& h,
-                              DevCtx* c) {
+void* CudaTransport::ipc_open(int src, std::uint64_t buffer_id, std::uint64_t base, std::uint64_t size,
+                              const cudaIpcMemHandle_t& h, DevCtx* c) {
   std::lock_guard<std::mutex> lk(ipc_mu_);
   auto key = std::make_pair(src, buffer_id);
   auto it = opened_.find(key);
-  if (it != opened_.end()) return it->second;
+  if (it != opened_.end()) return it->second.ptr;
   c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(c->dev));
+  // The sender reuses an address range only after freeing the allocation that
+  // held it, and it frees a tensor only after every receive of it completed
+  // (the receiver's copy kernel stored its completion flag after its last
+  // load), and a persistent plan keeps its tensors alive. So no copy of this
+  // rank will read an overlapping older mapping again: close it, instead of
+  // keeping one mapping per allocation the sender ever had.
+  if (size != 0) {
+    for (auto o = opened_.lower_bound({src, 0}); o != opened_.end() && o->first.first == src;) {
+      const Opened& m = o->second;
+      if (m.size != 0 && m.base < base + size && base < m.base + m.size) {
+        cudaIpcCloseMemHandle(m.ptr);
+        cudaGetLastError();
+        st_ipc_closes_++;
+        o = opened_.erase(o);
+      } else {
+        ++o;
+      }
+    }
+  }
   void* p = nullptr;
   cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
   if (e != cudaSuccess)
     throw std::runtime_error(std::string("commux: cudaIpcOpenMemHandle for rank ") +
                              std::to_string(src) + " failed: " + cudaGetErrorString(e));
-  opened_[key] = p;
-  opened_lru_.push_back(key);
+  opened_[key] = Opened{p, base, size};
   st_ipc_opens_++;
   return p;
 }
@@ -642,7 +660,7 @@ void CudaTransport::build_descs(const ReqPtr& r, const char* blob, std::size_t l
   std::uint64_t* done = nullptr;
   std::uint64_t done_val = 0;
   if (!local) {
-    auto* mb = static_cast<std::uint64_t*>(ipc_open(pp.src, w->mbox_id, w->mbox_handle, c));
+    auto* mb = static_cast<std::uint64_t*>(ipc_open(pp.src, w->mbox_id, 0, 0, w->mbox_handle, c));
     done = mb + w->slot;
     done_val = w->value;
   }
@@ -656,7 +674,7 @@ void CudaTransport::build_descs(const ReqPtr& r, const char* blob, std::size_t l
   auto src_base = [&](const SegWire& sw) -> const char* {
     if (numel_wire(sw) == 0) return nullptr;
     if (local) return reinterpret_cast<const char*>(sw.base);
-    return static_cast<const char*>(ipc_open(pp.src, sw.buffer_id, sw.handle, c));
+    return static_cast<const char*>(ipc_open(pp.src, sw.buffer_id, sw.base, sw.alloc_size, sw.handle, c));
   };
   auto src_ptr = [&](const SegWire& sw) -> const char* {
     const char* b = src_base(sw);
@@ -1105,6 +1123,7 @@ std::vector<std::pair<std::string, std::int64_t>> CudaTransport::stats() {
       {"cuda_wait_kernels", st_wait_kernels_.load()},
       {"cuda_fins", st_fins_.load()},
       {"cuda_ipc_opens", st_ipc_opens_.load()},
+      {"cuda_ipc_closes", st_ipc_closes_.load()},
       {"cuda_ipc_exports", st_ipc_exports_.load()},
       {"cuda_staged_sends", st_staged_.load()},
   };
@@ -1649,7 +1668,7 @@ DevicePlanPtr CudaTransport::create_plan(const std::vector<at::Tensor>& recv_t, 
       plan->n_shared_++;
     } else {
       m.mode = PlanMode::Device;
-      auto* mb = static_cast<std::uint64_t*>(ipc_open(m.peer, rep.mbox_id, rep.mbox_handle, c));
+      auto* mb = static_cast<std::uint64_t*>(ipc_open(m.peer, rep.mbox_id, 0, 0, rep.mbox_handle, c));
       m.ready_remote = mb + rep.ready_slot;
     }
   }

@@ -179,7 +179,12 @@ class CudaTransport final : public DeviceTransport {
   // shared with the collectives
   Engine* engine() { return eng_; }
   DevCtx* ctx(int dev);
-  void* ipc_open(int src, std::uint64_t buffer_id, const cudaIpcMemHandle_t& h, DevCtx* c);
+  // Maps rank src's allocation `buffer_id` (cached per (src, buffer_id)).
+  // `base`/`size` give its address range in the sender (size 0: unknown, as
+  // for the mailboxes): an older mapping of the same sender whose range
+  // overlaps it belongs to an allocation the sender has freed, and is closed.
+  void* ipc_open(int src, std::uint64_t buffer_id, std::uint64_t base, std::uint64_t size,
+                 const cudaIpcMemHandle_t& h, DevCtx* c);
   void ipc_export(const void* ptr, std::uint64_t* buffer_id, std::uint64_t* base,
                   std::uint64_t* size, cudaIpcMemHandle_t* handle);
   std::uint64_t device_timeout_ns() const { return timeout_ns_; }
@@ -201,8 +206,11 @@ class CudaTransport final : public DeviceTransport {
 
   std::mutex ipc_mu_;
   std::unordered_map<std::uint64_t, cudaIpcMemHandle_t> exported_;  // by buffer id
-  std::map<std::pair<int, std::uint64_t>, void*> opened_;
-  std::deque<std::pair<int, std::uint64_t>> opened_lru_;
+  struct Opened {
+    void* ptr = nullptr;
+    std::uint64_t base = 0, size = 0;  // the sender's address range (size 0: unknown)
+  };
+  std::map<std::pair<int, std::uint64_t>, Opened> opened_;
 
   std::mutex local_mu_;
   std::unordered_map<std::uint64_t, ReqPtr> local_sends_;  // self-sends awaiting a match
@@ -228,7 +236,7 @@ class CudaTransport final : public DeviceTransport {
   std::unique_ptr<CollImpl> coll_;
 
   std::atomic<std::int64_t> st_pulls_{0}, st_pull_bytes_{0}, st_wait_kernels_{0}, st_fins_{0},
-      st_ipc_opens_{0}, st_ipc_exports_{0}, st_staged_{0};
+      st_ipc_opens_{0}, st_ipc_exports_{0}, st_staged_{0}, st_ipc_closes_{0};
 };
 
 }  // namespace cuda

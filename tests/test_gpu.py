@@ -108,6 +108,12 @@ def test_halo_cuda_batch_path(world):
     check(run("halo.py", world, env=dict(CUDA, COMMUX_HALO_PLAN="0", COMMUX_GROUP="1"), timeout=180))
 
 
+def test_ipc_mappings_bounded_under_allocator_churn():
+    # ranks share one GPU or have one each: either way the receiver maps the
+    # sender's segments through CUDA IPC
+    check(run("gpu_ipc_churn.py", 2, env=CUDA, timeout=240))
+
+
 def test_tcp_cuda_p2p_staged():
     # ranks "on other hosts" (forced TCP): CUDA tensors travel through host memory
     check(run("gpu_p2p.py", 2, env=dict(CUDA, COMMUX_TRANSPORT="tcp"), timeout=240))
