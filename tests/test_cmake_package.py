@@ -1,7 +1,10 @@
-"""C++ consumers: `cmake --install` of the in-tree build, then a separate
+"""C++ consumers. (1) `cmake --install` of the in-tree build, then a separate
 project that does find_package(commux) and links commux::commux and
-commux::commux_io (the reference documents the same consumer flow with its
-installed headers and libcommux.so)."""
+commux::commux_io. (2) A project that pulls the source tree in with
+FetchContent and links the same targets. The reference documents both flows
+(reference: README.md:85-114)."""
+
+import sys
 
 import os
 import shutil
@@ -58,3 +61,55 @@ def test_find_package_consumer():
         r = subprocess.run([os.path.join(b, "consumer")], capture_output=True, text=True)
         assert r.returncode == 0, r.stdout + r.stderr
         assert "tag 1000500000007" in r.stdout
+
+
+FETCH_CMAKE = """cmake_minimum_required(VERSION 3.26)
+project(fetch_consumer CXX)
+set(CMAKE_CXX_STANDARD 17)
+include(FetchContent)
+FetchContent_Declare(commux SOURCE_DIR "{root}")
+set(COMMUX_CUDA OFF CACHE BOOL "" FORCE)
+FetchContent_MakeAvailable(commux)
+add_executable(consumer main.cpp)
+target_link_libraries(consumer PRIVATE commux::commux commux::commux_io)
+"""
+
+
+def _tree_state(root):
+    """Modification times of the package's build outputs (must not change)."""
+    out = {}
+    for d in (os.path.join(root, "commux_b200", "lib"), os.path.join(root, "commux_b200")):
+        if os.path.isdir(d):
+            for f in os.listdir(d):
+                if f.endswith(".so") or f == "test_commux":
+                    out[os.path.join(d, f)] = os.stat(os.path.join(d, f)).st_mtime_ns
+    return out
+
+
+def test_fetchcontent_consumer():
+    if shutil.which("cmake") is None:
+        pytest.skip("no cmake")
+    before = _tree_state(ROOT)
+    with tempfile.TemporaryDirectory() as d:
+        src = os.path.join(d, "consumer")
+        os.makedirs(src)
+        with open(os.path.join(src, "CMakeLists.txt"), "w") as f:
+            f.write(FETCH_CMAKE.format(root=ROOT))
+        with open(os.path.join(src, "main.cpp"), "w") as f:
+            f.write(CONSUMER_MAIN)
+        env = dict(os.environ, CXX="/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++",
+                   CC="/usr/bin/gcc" if os.path.exists("/usr/bin/gcc") else "gcc")
+        b = os.path.join(d, "b")
+        gen = ["-G", "Ninja"] if shutil.which("ninja") else []
+        r = subprocess.run(["cmake", "-S", src, "-B", b, *gen, f"-DPython3_EXECUTABLE={sys.executable}"],
+                           env=env, capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]
+        r = subprocess.run(["cmake", "--build", b, "-j", str(os.cpu_count() or 4)], env=env,
+                           capture_output=True, text=True, timeout=1200)
+        assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]
+        # the commux libraries of this build live in the consumer's tree
+        assert os.path.exists(os.path.join(b, "_deps", "commux-build", "lib", "libcommux.so"))
+        r = subprocess.run([os.path.join(b, "consumer")], capture_output=True, text=True)
+        assert r.returncode == 0, r.stdout + r.stderr
+        assert "tag 1000500000007" in r.stdout
+    assert _tree_state(ROOT) == before, "a build inside another project wrote into the package"
