@@ -287,6 +287,46 @@ EventPool::~EventPool() {
   for (auto e : free) cudaEventDestroy(e);
 }
 
+ExportPool::~ExportPool() {
+  if (!select_device_quiet(dev)) return;  // context already gone at exit
+  for (auto& kv : free) cudaFree(kv.second);
+  cudaGetLastError();
+}
+
+at::Tensor DevCtx::exportable_empty(at::IntArrayRef sizes, at::ScalarType dtype) {
+  std::int64_t numel = 1;
+  for (auto v : sizes) numel *= v;
+  constexpr std::size_t kGrain = std::size_t{1} << 21;  // cudaMalloc's own granularity
+  const std::size_t need = std::max<std::size_t>(1, static_cast<std::size_t>(numel) * at::elementSize(dtype));
+  const std::size_t cap = (need + kGrain - 1) / kGrain * kGrain;
+  void* p = nullptr;
+  std::size_t got = 0;
+  {
+    std::lock_guard<std::mutex> lk(export_pool->mu);
+    auto it = export_pool->free.lower_bound(cap);
+    if (it != export_pool->free.end() && it->first <= 2 * cap) {  // reuse up to twice the size
+      p = it->second;
+      got = it->first;
+      export_pool->free.erase(it);
+    }
+  }
+  if (p == nullptr) {
+    c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev));
+    CMX_CUDA(cudaMalloc(&p, cap));
+    got = cap;
+    std::lock_guard<std::mutex> lk(export_pool->mu);
+    export_pool->bytes += static_cast<std::int64_t>(cap);
+  }
+  std::shared_ptr<ExportPool> pool = export_pool;
+  return at::from_blob(
+      p, sizes,
+      [pool, got](void* q) {
+        std::lock_guard<std::mutex> lk(pool->mu);
+        pool->free.emplace(got, q);
+      },
+      at::TensorOptions().dtype(dtype).device(at::kCUDA, dev));
+}
+
 EventRef::~EventRef() {
   if (pool && ev != nullptr) {
     std::lock_guard<std::mutex> lk(pool->mu);
@@ -294,7 +334,8 @@ EventRef::~EventRef() {
   }
 }
 
-DevCtx::DevCtx(int d) : dev(d), pool_(std::make_shared<EventPool>(d)) {
+DevCtx::DevCtx(int d)
+    : dev(d), export_pool(std::make_shared<ExportPool>(d)), pool_(std::make_shared<EventPool>(d)) {
   c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(d));
   cudaDeviceProp prop;
   CMX_CUDA(cudaGetDeviceProperties(&prop, d));
@@ -436,6 +477,26 @@ int CudaTransport::pull_ctas(DevCtx* c) const {
   return v > 0 ? static_cast<int>(v) : c->sm_count * 8;
 }
 
+bool CudaTransport::exportable(const void* ptr) {
+  std::uint64_t id = 0, base = 0, size = 0;
+  cudaIpcMemHandle_t h;
+  try {
+    ipc_export(ptr, &id, &base, &size, &h);
+    return true;
+  } catch (const std::runtime_error&) {
+    cudaGetLastError();
+    return false;
+  }
+}
+
+at::Tensor CudaTransport::export_or_stage(const at::Tensor& t, DevCtx* c) {
+  if (t.numel() == 0 || exportable(t.data_ptr())) return t;
+  at::Tensor s = c->exportable_empty(t.sizes(), t.scalar_type());
+  s.copy_(t);  // on the current stream, ahead of the send's ready event
+  st_export_staged_++;
+  return s;
+}
+
 void CudaTransport::ipc_export(const void* ptr, std::uint64_t* buffer_id, std::uint64_t* base,
                                std::uint64_t* size, cudaIpcMemHandle_t* handle) {
   CUpointer_attribute attrs[3] = {CU_POINTER_ATTRIBUTE_BUFFER_ID,
@@ -456,12 +517,16 @@ void CudaTransport::ipc_export(const void* ptr, std::uint64_t* buffer_id, std::u
     *handle = it->second;
     return;
   }
-  cudaError_t e = cudaIpcGetMemHandle(handle, reinterpret_cast<void*>(start));
-  if (e != cudaSuccess)
-    throw std::runtime_error(std::string("commux: this CUDA tensor cannot be exported through CUDA IPC (") +
-                             cudaGetErrorString(e) +
-                             "); allocations made with PYTORCH_CUDA_ALLOC_CONF=expandable_segments:True "
-                             "are not exportable");
+  cudaError_t e = unexportable_.count(id) != 0 ? cudaErrorInvalidValue
+                                               : cudaIpcGetMemHandle(handle, reinterpret_cast<void*>(start));
+  if (e != cudaSuccess) {
+    // e.g. the caching allocator's expandable segments (cuMemCreate
+    // mappings); callers stage such memory through the export pool
+    cudaGetLastError();
+    unexportable_.insert(id);  // allocation ids are never reused
+    throw std::runtime_error(std::string("commux: this CUDA allocation cannot be exported through CUDA IPC (") +
+                             cudaGetErrorString(e) + ")");
+  }
   exported_[id] = *handle;
   st_ipc_exports_++;
 }
@@ -557,9 +622,23 @@ void CudaTransport::prepare_send(const ReqPtr& s, int dst, std::vector<char>& bl
       st_staged_++;
     }
   }
+  // a receiver in another process maps the sender's memory: memory that CUDA
+  // IPC cannot export travels through an exportable pool buffer instead
+  if (!st->local) {
+    for (auto& t : wire_t) {
+      at::Tensor e = export_or_stage(t, c);
+      if (!e.is_same(t)) {
+        st->staged.push_back(e);
+        t = e;
+      }
+    }
+  }
   {
+    // A batch shares one ready event, recorded by its first message: it may
+    // precede the copies just staged for this one, so a send that staged
+    // anything records its own event behind them.
     std::lock_guard<std::mutex> lk(batch_mu_);
-    st->ready = ready_event_for(c, st->stream, batch_depth_, batch_event_);
+    st->ready = ready_event_for(c, st->stream, st->staged.empty() ? batch_depth_ : 0, batch_event_);
   }
 
   blob.assign(sizeof(DrtsWire) + wire_t.size() * sizeof(SegWire), 0);
@@ -1124,6 +1203,7 @@ std::vector<std::pair<std::string, std::int64_t>> CudaTransport::stats() {
       {"cuda_fins", st_fins_.load()},
       {"cuda_ipc_opens", st_ipc_opens_.load()},
       {"cuda_ipc_closes", st_ipc_closes_.load()},
+      {"cuda_export_staged", st_export_staged_.load()},
       {"cuda_ipc_exports", st_ipc_exports_.load()},
       {"cuda_staged_sends", st_staged_.load()},
   };
@@ -1578,8 +1658,12 @@ DevicePlanPtr CudaTransport::create_plan(const std::vector<at::Tensor>& recv_t, 
       // pack descriptors run in the plan's first launch; a receiver that
       // turns out to share this GPU reads the view itself)
       at::Tensor wire_src = m.t;
-      if (narrow_rows(m.t)) {
+      // also staged: memory that CUDA IPC cannot export; the stage then comes
+      // from the exportable pool
+      const bool unexportable = m.t.numel() > 0 && !exportable(m.t.data_ptr());
+      if (narrow_rows(m.t) || unexportable) {
         m.stage = at::empty(m.t.sizes(), m.t.options().memory_format(at::MemoryFormat::Contiguous));
+        if (!exportable(m.stage.data_ptr())) m.stage = c->exportable_empty(m.t.sizes(), m.t.scalar_type());
         auto self_blob = wire_of(m.t, true, 0);
         m.pack = plan_descs(self_blob.data(), self_blob.size(), me, true, m.stage, c);
         wire_src = m.stage;

@@ -36,6 +36,7 @@
 #include <mutex>
 #include <string>
 #include <unordered_map>
+#include <unordered_set>
 #include <vector>
 
 #include "../engine/engine.hpp"
@@ -77,6 +78,21 @@ struct EventRef {
 };
 using EventPtr = std::shared_ptr<EventRef>;
 
+// Device buffers from cudaMalloc, which CUDA IPC can always export, for
+// sends whose own memory cannot be exported (the caching allocator's
+// expandable segments are cuMemCreate mappings). Buffers are kept for reuse,
+// so a receiver maps each of them once. Shared with the tensors it lends out:
+// a buffer returns here when the last tensor over it dies, after the transport
+// may be gone.
+struct ExportPool {
+  explicit ExportPool(int d) : dev(d) {}
+  ~ExportPool();
+  int dev;
+  std::mutex mu;
+  std::multimap<std::size_t, void*> free;  // by capacity
+  std::int64_t bytes = 0;                  // allocated in total
+};
+
 class DevCtx {
  public:
   explicit DevCtx(int dev);
@@ -95,6 +111,9 @@ class DevCtx {
   unsigned long long* status_d = nullptr;
 
   EventPtr event();                          // from the pool
+  // An uninitialised contiguous tensor in an exportable pool buffer.
+  at::Tensor exportable_empty(at::IntArrayRef sizes, at::ScalarType dtype);
+  std::shared_ptr<ExportPool> export_pool;
   void release(cudaEvent_t e);
   std::uint32_t* scratch(cudaStream_t s);    // zeroed per-stream counters
   // first of `n` consecutive counter slots (mod kCounterSlots) on stream s
@@ -185,6 +204,11 @@ class CudaTransport final : public DeviceTransport {
   // overlaps it belongs to an allocation the sender has freed, and is closed.
   void* ipc_open(int src, std::uint64_t buffer_id, std::uint64_t base, std::uint64_t size,
                  const cudaIpcMemHandle_t& h, DevCtx* c);
+  // false when CUDA IPC cannot export the allocation holding `ptr`
+  bool exportable(const void* ptr);
+  // `t` itself when the receiver can map it, else a copy (enqueued on the
+  // current stream) in an exportable pool buffer
+  at::Tensor export_or_stage(const at::Tensor& t, DevCtx* c);
   void ipc_export(const void* ptr, std::uint64_t* buffer_id, std::uint64_t* base,
                   std::uint64_t* size, cudaIpcMemHandle_t* handle);
   std::uint64_t device_timeout_ns() const { return timeout_ns_; }
@@ -211,6 +235,7 @@ class CudaTransport final : public DeviceTransport {
     std::uint64_t base = 0, size = 0;  // the sender's address range (size 0: unknown)
   };
   std::map<std::pair<int, std::uint64_t>, Opened> opened_;
+  std::unordered_set<std::uint64_t> unexportable_;  // allocation ids IPC refused
 
   std::mutex local_mu_;
   std::unordered_map<std::uint64_t, ReqPtr> local_sends_;  // self-sends awaiting a match
@@ -236,7 +261,7 @@ class CudaTransport final : public DeviceTransport {
   std::unique_ptr<CollImpl> coll_;
 
   std::atomic<std::int64_t> st_pulls_{0}, st_pull_bytes_{0}, st_wait_kernels_{0}, st_fins_{0},
-      st_ipc_opens_{0}, st_ipc_exports_{0}, st_staged_{0}, st_ipc_closes_{0};
+      st_ipc_opens_{0}, st_ipc_exports_{0}, st_staged_{0}, st_ipc_closes_{0}, st_export_staged_{0};
 };
 
 }  // namespace cuda

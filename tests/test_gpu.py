@@ -114,6 +114,15 @@ def test_ipc_mappings_bounded_under_allocator_churn():
     check(run("gpu_ipc_churn.py", 2, env=CUDA, timeout=240))
 
 
+def test_unexportable_memory_staged():
+    # the caching allocator's expandable segments cannot be exported through
+    # CUDA IPC: sends to another process travel through the export pool
+    env = dict(CUDA, PYTORCH_CUDA_ALLOC_CONF="expandable_segments:True")
+    check(run("gpu_p2p.py", 2, env=dict(env, CMX_EXPECT_EXPORT_STAGING="1"), timeout=240))
+    check(run("gpu_plan.py", 2, env=env, timeout=240))
+    check(run("halo.py", 2, env=dict(env, COMMUX_GROUP="1"), timeout=240))
+
+
 def test_tcp_cuda_p2p_staged():
     # ranks "on other hosts" (forced TCP): CUDA tensors travel through host memory
     check(run("gpu_p2p.py", 2, env=dict(CUDA, COMMUX_TRANSPORT="tcp"), timeout=240))

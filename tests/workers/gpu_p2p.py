@@ -91,7 +91,12 @@ for w in dist.batch_isend_irecv(ops):
     w.wait()
 for k in range(26):
     c.equal(f"window {k}", outs[k].cpu(), torch.full((100 + k,), float(src * 10 + k)))
+import commux_b200  # noqa: E402
+
+st = commux_b200.stats(device=dev)
+if os.environ.get("CMX_EXPECT_EXPORT_STAGING") == "1" and world > 1:
+    # memory CUDA IPC cannot export (expandable segments) went through the pool
+    c.check("export staging used", st.get("cuda_export_staged", 0) > 0, str(st))
 if rank == 0:
-    import commux_b200
-    print({k: v for k, v in commux_b200.stats().items() if k.startswith("cuda")}, flush=True)
+    print({k: v for k, v in st.items() if k.startswith("cuda")}, flush=True)
 c.finish()
