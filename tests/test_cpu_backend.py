@@ -16,12 +16,12 @@ def test_torch_dist_2ranks():
     check(run("torch_dist.py", 2))
 
 
-@pytest.mark.parametrize("world", [1, 2, 3, 4])
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 7])
 def test_collectives(world):
     check(run("collectives.py", world, timeout=180))
 
 
-@pytest.mark.parametrize("world", [1, 3])
+@pytest.mark.parametrize("world", [1, 3, 4])
 def test_reduce_op_rejected_everywhere(world):
     check(run("reduce_op.py", world, timeout=120))
 
