@@ -10,12 +10,29 @@ importable at build time (install with ``--no-build-isolation``).
     pip install --no-build-isolation .
 """
 
+import os
 import subprocess
 import sys
 
 from setuptools import find_packages, setup
 from setuptools.command.build_py import build_py
 from setuptools.dist import Distribution
+
+
+def _version() -> str:
+    """COMMUX_VERSION, else the latest `vX.Y.Z` git tag, else 0.1.0."""
+    v = os.environ.get("COMMUX_VERSION")
+    if v:
+        return v.lstrip("v")
+    try:
+        tag = subprocess.run(["git", "describe", "--tags", "--abbrev=0", "--match", "v[0-9]*"],
+                             capture_output=True, text=True, cwd=os.path.dirname(os.path.abspath(__file__)),
+                             timeout=30)
+        if tag.returncode == 0 and tag.stdout.strip():
+            return tag.stdout.strip().lstrip("v")
+    except (OSError, subprocess.SubprocessError):
+        pass
+    return "0.1.0"
 
 
 class BuildNative(build_py):
@@ -31,7 +48,7 @@ class BinaryDistribution(Distribution):
 
 setup(
     name="commux-b200",
-    version="0.1.0",
+    version=_version(),
     description="MPI-style tagged p2p and collectives for torch.distributed on B200 (NVLink 5 / NVSwitch)",
     packages=find_packages(include=["commux_b200", "commux_b200.*", "commux"]),
     package_data={"commux_b200": ["_C*.so", "_ops*.so", "lib/*.so", "lib/test_commux",
