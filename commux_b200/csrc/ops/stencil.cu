@@ -103,6 +103,25 @@ unsigned* status_word(unsigned** dev) {
   return host;
 }
 
+// cuTensorMapEncodeTiled, resolved through the runtime at first use: the
+// extension does not link libcuda, so it imports on machines without a GPU
+// driver (a build host) and only needs the driver once a kernel launches.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static const EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    C10_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p != nullptr,
+                "jacobi7: the CUDA driver has no cuTensorMapEncodeTiled");
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
 template <typename T>
 void launch_tma(const at::Tensor& u, at::Tensor& v, int nz, int ny, int nx, int h, int iz, int iy, int ix,
                 double* res, cudaStream_t stream) {
@@ -113,7 +132,7 @@ void launch_tma(const at::Tensor& u, at::Tensor& v, int nz, int ny, int nx, int 
                            static_cast<cuuint64_t>(nx) * ny * sizeof(T)};
   cuuint32_t box[3] = {static_cast<cuuint32_t>(B::kW), static_cast<cuuint32_t>(B::kH), 1};
   cuuint32_t estride[3] = {1, 1, 1};
-  CUresult rc = cuTensorMapEncodeTiled(
+  CUresult rc = encode_tiled()(
       &map, sizeof(T) == 8 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT64 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
       const_cast<void*>(u.data_ptr()), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
       CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
