@@ -1,0 +1,24 @@
+"""The package and both extensions import on a machine without a GPU driver
+(the build host): libcommux.so loads the CUDA library only on first CUDA use,
+and the compute-kernel extension resolves its driver entry points at run time.
+`__graft_entry__.build()` relies on this when it imports what it built."""
+
+import os
+import subprocess
+import sys
+
+from mp import ROOT
+
+CODE = """
+import commux_b200 as c
+from commux_b200 import _C, _ops
+c.register()
+print("import ok", c.preferred_backend())
+"""
+
+
+def test_extensions_import_without_driver():
+    r = subprocess.run([sys.executable, "-c", CODE], cwd=ROOT, capture_output=True, text=True, timeout=300,
+                       env=dict(os.environ, PYTHONPATH=ROOT))
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "import ok ucx" in r.stdout
