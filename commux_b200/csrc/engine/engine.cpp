@@ -151,6 +151,7 @@ Engine::Engine(c10::intrusive_ptr<c10d::Store> store, int rank, int size,
   if (wait_poll_ms_ <= 0) wait_poll_ms_ = 1;
   fault_ = FaultSpec::from_env();
   cma_enabled_ = env_int("COMMUX_CMA", 1) != 0;
+  copy_threads_ = static_cast<int>(std::max<std::int64_t>(0, env_int("COMMUX_COPY_THREADS", 2)));
   cma_off_.reset(new std::atomic<bool>[static_cast<std::size_t>(size)]);
   for (int p = 0; p < size; ++p) cma_off_[p].store(false);
   bootstrap();
@@ -1176,12 +1177,19 @@ void Engine::on_fin(int src, const proto::FinRec* rec) {
 
 bool Engine::cma_read(int src, const ReqPtr& r, std::int32_t pid, const proto::CmaSeg* segs, std::uint32_t nseg,
                       std::uint64_t total) {
-  // walk the sender's segments and this request's host segments together
+  // Pair the sender's segments with this request's host segments: pieces of
+  // (local address, remote address, bytes).
+  struct Piece {
+    char* local;
+    std::uint64_t remote;
+    std::uint64_t bytes;
+  };
+  std::vector<Piece> pieces;
   std::uint32_t si = 0;
-  std::uint64_t soff = 0, done = 0;
+  std::uint64_t soff = 0, mapped = 0;
   std::size_t li = 0;
   std::uint64_t loff = 0;
-  while (done < total) {
+  while (mapped < total) {
     while (si < nseg && soff >= segs[si].bytes) {
       ++si;
       soff = 0;
@@ -1191,24 +1199,63 @@ bool Engine::cma_read(int src, const ReqPtr& r, std::int32_t pid, const proto::C
       loff = 0;
     }
     if (si >= nseg || li >= r->host.size()) break;
-    std::uint64_t n = std::min({segs[si].bytes - soff, r->host[li].bytes - loff, total - done});
-    iovec liov{r->host[li].ptr + loff, static_cast<std::size_t>(n)};
-    iovec riov{reinterpret_cast<void*>(segs[si].addr + soff), static_cast<std::size_t>(n)};
-    ssize_t got = ::process_vm_readv(static_cast<pid_t>(pid), &liov, 1, &riov, 1, 0);
-    if (got <= 0) {
-      // refused (ptrace policy, seccomp, another host): this peer uses the
-      // two-copy path from now on
-      cma_off_[src].store(true);
-      logf(LogLevel::Info, rank_, "single-copy reads from rank %d refused (%s); using the ring", src,
-           std::strerror(errno));
-      return false;
-    }
-    soff += static_cast<std::uint64_t>(got);
-    loff += static_cast<std::uint64_t>(got);
-    done += static_cast<std::uint64_t>(got);
+    std::uint64_t n = std::min({segs[si].bytes - soff, r->host[li].bytes - loff, total - mapped});
+    pieces.push_back({static_cast<char*>(r->host[li].ptr) + loff, segs[si].addr + soff, n});
+    soff += n;
+    loff += n;
+    mapped += n;
   }
-  if (done != total) {
+  if (mapped != total) {
     cma_off_[src].store(true);
+    return false;
+  }
+  // Large reads are split into equal byte ranges, one per thread: the caller
+  // and up to COMMUX_COPY_THREADS helpers, each range at least kMinShare.
+  constexpr std::uint64_t kMinShare = std::uint64_t{1} << 20;
+  std::uint64_t shares = 1;
+  if (copy_threads_ > 0 && total >= 2 * kMinShare)
+    shares = std::min<std::uint64_t>(static_cast<std::uint64_t>(copy_threads_) + 1, total / kMinShare);
+  std::atomic<int> failed_errno{0};
+  auto copy_range = [&, pid](std::uint64_t lo, std::uint64_t hi) {
+    std::uint64_t at = 0;  // byte offset of the current piece in the message
+    for (const Piece& pc : pieces) {
+      const std::uint64_t a = std::max(lo, at), b = std::min(hi, at + pc.bytes);
+      at += pc.bytes;
+      if (a >= b) continue;
+      std::uint64_t off = a - (at - pc.bytes);
+      std::uint64_t left = b - a;
+      while (left > 0) {
+        if (failed_errno.load(std::memory_order_relaxed) != 0) return;
+        iovec liov{pc.local + off, static_cast<std::size_t>(left)};
+        iovec riov{reinterpret_cast<void*>(pc.remote + off), static_cast<std::size_t>(left)};
+        ssize_t got = ::process_vm_readv(static_cast<pid_t>(pid), &liov, 1, &riov, 1, 0);
+        if (got <= 0) {
+          int e = errno != 0 ? errno : EIO;
+          int zero = 0;
+          failed_errno.compare_exchange_strong(zero, e);
+          return;
+        }
+        off += static_cast<std::uint64_t>(got);
+        left -= static_cast<std::uint64_t>(got);
+      }
+    }
+  };
+  if (shares <= 1) {
+    copy_range(0, total);
+  } else {
+    std::call_once(copy_pool_once_, [&] { copy_pool_ = std::make_unique<CopyPool>(copy_threads_); });
+    std::vector<std::function<void()>> tasks;
+    const std::uint64_t step = (total + shares - 1) / shares;
+    for (std::uint64_t lo = 0; lo < total; lo += step)
+      tasks.push_back([&copy_range, lo, hi = std::min(total, lo + step)] { copy_range(lo, hi); });
+    copy_pool_->run_all(tasks);
+  }
+  if (failed_errno.load() != 0) {
+    // refused (ptrace policy, seccomp, another host): this peer uses the
+    // two-copy path from now on
+    cma_off_[src].store(true);
+    logf(LogLevel::Info, rank_, "single-copy reads from rank %d refused (%s); using the ring", src,
+         std::strerror(failed_errno.load()));
     return false;
   }
   stats_.single_copy_msgs++;

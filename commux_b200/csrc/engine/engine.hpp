@@ -34,6 +34,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "copy_pool.hpp"
 #include "protocol.hpp"
 #include "shm.hpp"
 #include "tcp.hpp"
@@ -247,6 +248,9 @@ class Engine {
   std::vector<bool> remote_;                         // remote_[p]: TCP peer
   std::unique_ptr<std::atomic<bool>[]> cma_off_;     // single-copy refused for peer p
   bool cma_enabled_ = true;                          // COMMUX_CMA
+  int copy_threads_ = 2;                             // COMMUX_COPY_THREADS: helpers of large reads
+  std::unique_ptr<CopyPool> copy_pool_;              // created on the first large read
+  std::once_flag copy_pool_once_;
   bool any_remote_ = false;
   std::unique_ptr<tcp::Links> links_;                // TCP peers (null when none)
   std::vector<shm::RingReader> in_;                  // in_[src]

@@ -1,7 +1,7 @@
 // Multi-rank C++ test driver for commux::ProcessGroupUCX (same coverage as
 // reference tests/test_commux.cpp: tag matching, collectives, vector p2p,
 // group window, multi-threaded posting, parked-waiter wakeups, a V-tensor
-// ping-pong benchmark). Ranks bootstrap through a c10d::TCPStore (rank 0
+// ping-pong benchmark), plus large rendezvous messages (T8). Ranks bootstrap through a c10d::TCPStore (rank 0
 // hosts it).
 //
 //   test_commux <rank> <world> [host] [port]
@@ -47,6 +47,9 @@ int main(int argc, char** argv) {
   const int world = std::atoi(argv[2]);
   const std::string host = argc > 3 ? argv[3] : "127.0.0.1";
   const int port = argc > 4 ? std::atoi(argv[4]) : 29555;
+  // the driver checks the engine's threads: torch's own intra-op threads
+  // (OpenMP, whose synchronisation ThreadSanitizer cannot see) stay off
+  at::set_num_threads(1);
 
   c10d::TCPStoreOptions so;
   so.port = static_cast<std::uint16_t>(port);
@@ -139,6 +142,22 @@ int main(int argc, char** argv) {
     pg->send(mine, peer, rank == 0 ? 410 : 420);
     pg->endCoalescing()->wait();
     check(out[0].eq(peer + 1.0).all().item<bool>(), "group window: deferred recv/send completed");
+  }
+  pg->barrier()->wait();
+
+  // T8: large messages both ways at once (rendezvous; on one host the
+  // single-copy read, split across the copy helpers)
+  if (world >= 2 && rank <= 1) {
+    const int peer = 1 - rank;
+    const std::int64_t n = 3 << 20;  // 24 MiB of fp64 per message
+    std::vector<at::Tensor> mine{torch::arange(n, f64).add_(1e7 * rank)};
+    std::vector<at::Tensor> got{torch::zeros({n}, f64)};
+    auto r = pg->recv(got, peer, 800);
+    auto s = pg->send(mine, peer, 800);
+    r->wait();
+    s->wait();
+    check(got[0].equal(torch::arange(n, f64).add_(1e7 * peer)),
+          "large message: every byte of a 24 MiB rendezvous arrived");
   }
   pg->barrier()->wait();
 
