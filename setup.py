@@ -51,8 +51,11 @@ setup(
     version=_version(),
     description="MPI-style tagged p2p and collectives for torch.distributed on B200 (NVLink 5 / NVSwitch)",
     packages=find_packages(include=["commux_b200", "commux_b200.*", "commux"]),
+    # `commux` (the reference's package name) carries the libraries and
+    # headers too, where C++ consumers of the reference look for them
     package_data={"commux_b200": ["_C*.so", "_ops*.so", "lib/*.so", "lib/test_commux",
-                                  "include/commux/*.hpp", "include/commux/*.h"]},
+                                  "include/commux/*.hpp", "include/commux/*.h"],
+                  "commux": ["lib/*.so", "include/commux/*.hpp", "include/commux/*.h"]},
     python_requires=">=3.10",
     cmdclass={"build_py": BuildNative},
     distclass=BinaryDistribution,

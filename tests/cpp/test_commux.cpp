@@ -5,7 +5,8 @@
 // hosts it).
 //
 //   test_commux <rank> <world> [host] [port]
-//   COMMUX_TEST_DEVICE=cuda  runs the p2p/collective checks on CUDA tensors
+//   COMMUX_TEST_DEVICE=cuda (or UCXPG_DEVICE=cuda) runs the p2p/collective
+//                            checks on CUDA tensors
 //   COMMUX_BENCH=1 [COMMUX_BENCH_V=16]  adds the ping-pong benchmark
 //   COMMUX_MT=1 / COMMUX_DEADLOCK=1     add the thread tests
 
@@ -61,7 +62,9 @@ int main(int argc, char** argv) {
                                                         std::chrono::milliseconds(60000));
 
   torch::Device device(torch::kCPU);
+  // COMMUX_TEST_DEVICE, or UCXPG_DEVICE as in the reference's instructions
   const char* dv = std::getenv("COMMUX_TEST_DEVICE");
+  if (dv == nullptr) dv = std::getenv("UCXPG_DEVICE");
   if (dv != nullptr && std::string(dv) == "cuda") {
     if (!torch::cuda::is_available()) {
       std::fprintf(stderr, "CUDA requested but not available\n");

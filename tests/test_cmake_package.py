@@ -1,8 +1,10 @@
 """C++ consumers. (1) `cmake --install` of the in-tree build, then a separate
 project that does find_package(commux) and links commux::commux and
 commux::commux_io. (2) A project that pulls the source tree in with
-FetchContent and links the same targets. The reference documents both flows
-(reference: README.md:85-114)."""
+FetchContent and links the same targets. (3) A project that finds the library
+and headers inside the installed `commux` Python package, as the reference's
+README shows. The reference documents all three flows
+(reference: README.md:83-114)."""
 
 import sys
 
@@ -113,3 +115,52 @@ def test_fetchcontent_consumer():
         assert r.returncode == 0, r.stdout + r.stderr
         assert "tag 1000500000007" in r.stdout
     assert _tree_state(ROOT) == before, "a build inside another project wrote into the package"
+
+
+PROBE_CMAKE = """cmake_minimum_required(VERSION 3.22)
+project(probe_consumer CXX)
+set(CMAKE_CXX_STANDARD 17)
+find_package(Python3 REQUIRED COMPONENTS Interpreter)
+execute_process(
+  COMMAND ${{Python3_EXECUTABLE}} -c "import commux,os;print(os.path.dirname(commux.__file__))"
+  OUTPUT_VARIABLE COMMUX_DIR OUTPUT_STRIP_TRAILING_WHITESPACE)
+find_library(COMMUX_LIBRARY commux HINTS ${{COMMUX_DIR}}/lib REQUIRED NO_DEFAULT_PATH)
+add_executable(consumer main.cpp)
+target_include_directories(consumer PRIVATE ${{COMMUX_DIR}}/include {torch_inc})
+target_compile_definitions(consumer PRIVATE _GLIBCXX_USE_CXX11_ABI={abi})
+target_link_directories(consumer PRIVATE {torch_lib})
+target_link_libraries(consumer PRIVATE ${{COMMUX_LIBRARY}} torch torch_cpu c10)
+set_target_properties(consumer PROPERTIES BUILD_RPATH "${{COMMUX_DIR}}/lib;{torch_lib}")
+"""
+
+
+def test_python_package_probe_consumer():
+    """The reference README's route: locate lib/ and include/ from the
+    installed `commux` package (here the in-tree package, on PYTHONPATH)."""
+    if shutil.which("cmake") is None:
+        pytest.skip("no cmake")
+    if not os.path.exists(os.path.join(ROOT, "commux", "lib", "libcommux.so")):
+        pytest.skip("no in-tree build")
+    import torch
+    from torch.utils import cpp_extension
+
+    torch_lib = os.path.join(os.path.dirname(torch.__file__), "lib")
+    with tempfile.TemporaryDirectory() as d:
+        src = os.path.join(d, "consumer")
+        os.makedirs(src)
+        with open(os.path.join(src, "CMakeLists.txt"), "w") as f:
+            f.write(PROBE_CMAKE.format(torch_inc=" ".join(cpp_extension.include_paths()), torch_lib=torch_lib,
+                                       abi=int(torch._C._GLIBCXX_USE_CXX11_ABI)))
+        with open(os.path.join(src, "main.cpp"), "w") as f:
+            f.write(CONSUMER_MAIN)
+        env = dict(os.environ, PYTHONPATH=ROOT,
+                   CXX="/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++")
+        b = os.path.join(d, "b")
+        r = subprocess.run(["cmake", "-S", src, "-B", b, f"-DPython3_EXECUTABLE={sys.executable}"], env=env,
+                           capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]
+        r = subprocess.run(["cmake", "--build", b], env=env, capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]
+        r = subprocess.run([os.path.join(b, "consumer")], capture_output=True, text=True)
+        assert r.returncode == 0, r.stdout + r.stderr
+        assert "tag 1000500000007" in r.stdout
