@@ -14,261 +14,11 @@
 
 #include "coll.hpp"
 #include "commux/process_group_ucx.hpp"
+#include "wire.hpp"
 
 namespace commux {
 namespace cuda {
 
-namespace {
-
-constexpr std::uint32_t kWireMagic = 0x54524443u;
-constexpr int kWireDims = 8;
-constexpr std::uint64_t kSlots = 1ull << 16;  // consumed-flag slots per device
-constexpr std::uint64_t kMaxUnitsPerDesc = 1ull << 30;
-
-// One tensor of a device message, as the sender describes it.
-struct SegWire {
-  std::uint64_t buffer_id;  // allocation id in the sender process (0: local)
-  std::uint64_t base;       // allocation base address in the sender process
-  std::uint64_t alloc_size;
-  std::uint64_t offset;     // first element, bytes from base
-  cudaIpcMemHandle_t handle;
-  std::uint32_t elem;
-  std::int32_t ndim;
-  std::int64_t sizes[kWireDims];
-  std::int64_t strides[kWireDims];  // elements
-};
-
-struct DrtsWire {
-  std::uint32_t magic;
-  std::uint32_t nseg;
-  std::int32_t pid;
-  std::int32_t device;
-  unsigned char uuid[16];
-  std::uint32_t sender_waits_on_device;
-  std::uint32_t pad;
-  std::uint64_t mbox_id;
-  std::uint64_t mbox_base;
-  cudaIpcMemHandle_t mbox_handle;
-  std::uint64_t slot;
-  std::uint64_t value;
-};
-
-cudaStream_t current_stream(int dev) {
-  return c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(dev)).stream();
-}
-
-void cu_check(CUresult r, const char* what) {
-  if (r == CUDA_SUCCESS) return;
-  const char* s = nullptr;
-  cuGetErrorString(r, &s);
-  throw std::runtime_error(std::string("commux CUDA driver error in ") + what + ": " +
-                           (s ? s : "unknown"));
-}
-
-template <typename T>
-std::shared_ptr<T> state(const ReqPtr& r) {
-  return std::static_pointer_cast<T>(r->dev);
-}
-
-// A tensor dimension as (size, src stride, dst stride), strides in elements
-// or bytes depending on the stage.
-struct Dim {
-  std::int64_t size, ss, ds;
-};
-
-// Refine two shapes with equal element counts into one common shape (split
-// dims where they differ) so a single index walks both. Returns false when no
-// common refinement exists (e.g. sizes 6 and 4 facing each other).
-bool refine(const std::vector<std::pair<std::int64_t, std::int64_t>>& a,
-            const std::vector<std::pair<std::int64_t, std::int64_t>>& b, std::vector<Dim>& out) {
-  out.clear();
-  int i = static_cast<int>(a.size()) - 1, j = static_cast<int>(b.size()) - 1;
-  if (i < 0 || j < 0) return false;
-  std::int64_t ra = a[i].first, rb = b[j].first, sa = a[i].second, sb = b[j].second;
-  while (i >= 0 && j >= 0) {
-    std::int64_t m = std::min(ra, rb);
-    if (m <= 0 || ra % m || rb % m) return false;
-    out.push_back({m, sa, sb});
-    if (ra == m) {
-      if (--i >= 0) {
-        ra = a[i].first;
-        sa = a[i].second;
-      }
-    } else {
-      ra /= m;
-      sa *= m;
-    }
-    if (rb == m) {
-      if (--j >= 0) {
-        rb = b[j].first;
-        sb = b[j].second;
-      }
-    } else {
-      rb /= m;
-      sb *= m;
-    }
-  }
-  if (i >= 0 || j >= 0) return false;
-  std::reverse(out.begin(), out.end());
-  // merge dims that are contiguous in both
-  std::vector<Dim> m;
-  for (auto& d : out) {
-    if (!m.empty() && m.back().ss == d.size * d.ss && m.back().ds == d.size * d.ds) {
-      m.back().size *= d.size;
-      m.back().ss = d.ss;
-      m.back().ds = d.ds;
-    } else {
-      m.push_back(d);
-    }
-  }
-  out.swap(m);
-  return true;
-}
-
-std::vector<std::pair<std::int64_t, std::int64_t>> dims_of(const std::int64_t* sizes,
-                                                           const std::int64_t* strides, int nd) {
-  std::vector<std::pair<std::int64_t, std::int64_t>> v;
-  for (int k = 0; k < nd; ++k)
-    if (sizes[k] != 1) v.push_back({sizes[k], strides[k]});
-  if (v.empty()) v.push_back({1, 1});
-  return v;
-}
-
-// Turn common dims (element strides) into pull descriptors with the widest
-// vector unit the alignment allows; appends to `out`.
-void emit_descs(const char* sp, char* dp, std::vector<Dim> dims, std::int64_t elem,
-                std::vector<PullDesc>& out) {
-  // element strides -> byte strides
-  for (auto& d : dims) {
-    d.ss *= elem;
-    d.ds *= elem;
-  }
-  std::int64_t unit = elem;
-  Dim& in = dims.back();
-  if (in.ss == elem && in.ds == elem) {
-    std::int64_t inner_bytes = in.size * elem;
-    for (std::int64_t u : {16, 8, 4, 2, 1}) {
-      bool ok = inner_bytes % u == 0 && reinterpret_cast<std::uintptr_t>(sp) % u == 0 &&
-                reinterpret_cast<std::uintptr_t>(dp) % u == 0;
-      for (std::size_t k = 0; ok && k + 1 < dims.size(); ++k)
-        ok = dims[k].ss % u == 0 && dims[k].ds % u == 0;
-      if (ok) {
-        unit = u;
-        break;
-      }
-    }
-    in.size = inner_bytes / unit;
-    in.ss = unit;
-    in.ds = unit;
-    // a row of exactly one unit (e.g. a 16-byte x-face row): the row dim
-    // adds nothing but a division per unit
-    if (in.size == 1 && dims.size() > 1) dims.pop_back();
-  } else if (!(elem == 1 || elem == 2 || elem == 4 || elem == 8 || elem == 16)) {
-    throw std::runtime_error("commux: unsupported element size for a strided device copy");
-  }
-  if (dims.size() > static_cast<std::size_t>(kMaxPullDims))
-    throw std::runtime_error("layout");
-  // split along the outermost dim so every descriptor has < 2^30 units
-  std::int64_t per0 = 1;
-  for (std::size_t k = 1; k < dims.size(); ++k) per0 *= dims[k].size;
-  if (per0 > static_cast<std::int64_t>(kMaxUnitsPerDesc))
-    throw std::runtime_error("commux: device message row too large");
-  std::int64_t step0 = std::max<std::int64_t>(1, static_cast<std::int64_t>(kMaxUnitsPerDesc) / per0);
-  for (std::int64_t s0 = 0; s0 < dims[0].size; s0 += step0) {
-    std::int64_t n0 = std::min(step0, dims[0].size - s0);
-    PullDesc d{};
-    d.src = sp + s0 * dims[0].ss;
-    d.dst = dp + s0 * dims[0].ds;
-    d.ndim = static_cast<std::uint32_t>(dims.size());
-    d.unit = static_cast<std::uint32_t>(unit);
-    const int off = kMaxPullDims - static_cast<int>(dims.size());
-    for (int k = 0; k < kMaxPullDims; ++k) {
-      d.div[k] = FastDiv(1);
-      d.sst[k] = 0;
-      d.dstr[k] = 0;
-    }
-    std::int64_t units = 1;
-    for (std::size_t k = 0; k < dims.size(); ++k) {
-      std::int64_t sz = k == 0 ? n0 : dims[k].size;
-      d.div[off + k] = FastDiv(static_cast<std::uint32_t>(sz));
-      d.sst[off + k] = dims[k].ss;
-      d.dstr[off + k] = dims[k].ds;
-      units *= sz;
-    }
-    d.units = static_cast<std::uint32_t>(units);
-    d.nchunks = static_cast<std::uint32_t>(std::max<std::int64_t>(1, (units + kChunkUnits - 1) / kChunkUnits));
-    // the kernel's common walk holds strides in 32 bits
-    constexpr std::int64_t lim = std::int64_t{1} << 31;
-    for (int k = 0; k < kMaxPullDims; ++k)
-      if (d.sst[k] >= lim || d.sst[k] <= -lim || d.dstr[k] >= lim || d.dstr[k] <= -lim) d.wide = 1;
-    out.push_back(d);
-  }
-}
-
-// Host-side bounds check of every descriptor before launch: the bytes a
-// descriptor touches must lie inside the source allocation (the IPC mapping)
-// and the destination storage. A layout bug then raises here instead of
-// reaching the GPU as an out-of-bounds access. The bounds-check build also
-// hands the same limits to the kernel, which checks every unit it copies.
-void check_desc(PullDesc& d, std::uintptr_t src_lo, std::uintptr_t src_hi,
-                std::uintptr_t dst_lo, std::uintptr_t dst_hi) {
-  if (d.units == 0) return;
-  std::int64_t s_min = 0, s_max = 0, d_min = 0, d_max = 0;
-  for (int k = 0; k < kMaxPullDims; ++k) {
-    std::int64_t ext = static_cast<std::int64_t>(d.div[k].d) - 1;
-    std::int64_t a = ext * d.sst[k], b = ext * d.dstr[k];
-    (a < 0 ? s_min : s_max) += a;
-    (b < 0 ? d_min : d_max) += b;
-  }
-  auto sp = reinterpret_cast<std::intptr_t>(d.src), dp = reinterpret_cast<std::intptr_t>(d.dst);
-  bool ok = sp + s_min >= static_cast<std::intptr_t>(src_lo) &&
-            sp + s_max + static_cast<std::intptr_t>(d.unit) <= static_cast<std::intptr_t>(src_hi) &&
-            dp + d_min >= static_cast<std::intptr_t>(dst_lo) &&
-            dp + d_max + static_cast<std::intptr_t>(d.unit) <= static_cast<std::intptr_t>(dst_hi);
-  if (!ok)
-    throw std::runtime_error("commux: internal error, a copy descriptor leaves its buffers "
-                             "(layout bug caught before launch)");
-#if defined(COMMUX_DEVICE_CHECKS)
-  d.src_lo = static_cast<std::intptr_t>(src_lo) - sp;
-  d.src_hi = static_cast<std::intptr_t>(src_hi) - sp;
-  d.dst_lo = static_cast<std::intptr_t>(dst_lo) - dp;
-  d.dst_hi = static_cast<std::intptr_t>(dst_hi) - dp;
-#endif
-}
-
-bool contiguous_wire(const SegWire& s) {
-  std::int64_t expect = 1;
-  for (int k = s.ndim - 1; k >= 0; --k) {
-    if (s.sizes[k] != 1 && s.strides[k] != expect) return false;
-    expect *= s.sizes[k];
-  }
-  return true;
-}
-
-std::int64_t numel_wire(const SegWire& s) {
-  std::int64_t n = 1;
-  for (int k = 0; k < s.ndim; ++k) n *= s.sizes[k];
-  return n;
-}
-
-// Narrow rows (a halo x-face: 16-byte runs at a row pitch) cross NVLink far
-// below its bandwidth when a peer reads them one by one; such a send is
-// packed into a contiguous staging buffer on its own GPU first, and the
-// receiver reads that buffer.
-constexpr std::int64_t kPackRunBytes = 512;
-
-bool narrow_rows(const at::Tensor& t) {
-  if (t.numel() == 0 || t.dim() > kWireDims) return false;
-  std::vector<std::int64_t> sz(t.sizes().begin(), t.sizes().end()), sd(t.strides().begin(), t.strides().end());
-  auto d = dims_of(sz.data(), sd.data(), t.dim());
-  std::vector<Dim> m;
-  if (!refine(d, d, m) || m.empty()) return false;
-  const Dim& in = m.back();
-  const std::int64_t run = (in.ss == 1 ? in.size : 1) * static_cast<std::int64_t>(t.element_size());
-  return run < kPackRunBytes;
-}
-
-}  // namespace
 
 // ---------------------------------------------------------------------------
 // device context
@@ -1210,555 +960,6 @@ std::vector<std::pair<std::string, std::int64_t>> CudaTransport::stats() {
   if (coll_)
     for (auto& kv : coll_->stats()) v.push_back(kv);
   return v;
-}
-
-// ---------------------------------------------------------------------------
-// persistent plans
-// ---------------------------------------------------------------------------
-
-namespace {
-
-constexpr std::uint32_t kPlanSub = 0x7FF0;       // sub-index of setup descriptors
-constexpr std::uint32_t kPlanReplySub = 0x7FF1;  // sub-index of setup replies
-constexpr std::uint32_t kPlanMagic = 0x4E414C50u;
-
-// receiver -> sender at setup: where the sender stores "ready"
-struct PlanReply {
-  std::uint32_t magic;
-  std::int32_t pid;
-  unsigned char uuid[16];
-  std::uint64_t mbox_id;
-  cudaIpcMemHandle_t mbox_handle;
-  std::uint64_t ready_slot;
-};
-
-enum class PlanMode { Local, Device, Shared };
-
-}  // namespace
-
-class CudaPlan final : public DevicePlan {
- public:
-  struct Msg {
-    at::Tensor t;
-    int peer = -1;
-    int tag = 0;
-    PlanMode mode = PlanMode::Local;
-    std::uint64_t* ready_remote = nullptr;    // send: where "ready" is stored
-    std::uint64_t* consumed_local = nullptr;  // send: set by the receiver's pull
-    const std::uint64_t* ready_local = nullptr;  // recv: set by the sender
-    std::vector<PullDesc> descs;              // recv (local/device)
-    bool matched = false;                     // self recv paired with a send
-    at::Tensor stage;                         // send: packed copy the receiver reads
-    std::vector<PullDesc> pack;               // send: view -> stage
-  };
-
-  CudaPlan(CudaTransport* tr, Engine* eng, DevCtx* c) : tr_(tr), eng_(eng), c_(c) {}
-  ~CudaPlan() override {
-    if (!select_device_quiet(c_->dev)) return;  // context gone at process exit
-    // the last start may still run: its buffers (state_, staging) must not be
-    // handed to other work before it is done
-    if (last_stream_ != nullptr) cudaStreamSynchronize(last_stream_);
-    if (exec_) cudaGraphExecDestroy(exec_);
-    if (graph_) cudaGraphDestroy(graph_);
-    if (trace_h_) cudaFreeHost(trace_h_);
-    cudaGetLastError();
-  }
-  std::vector<Msg> sends, recvs;
-
-  // Builds the launches every start() replays: (1) pack + "ready" signals of
-  // the sends to other GPUs (without packing, the signals are stored by the
-  // first pull launch at entry instead), (2) the pulls of every receive, (3)
-  // the wait for the receivers' "consumed" flags, ending with the epoch bump.
-  // Every flag value is
-  // the plan's epoch, read from device memory, so the launches never change:
-  // they are captured once into a CUDA graph and a start is one graph launch.
-  void finalize() {
-    // Sends to another GPU: packed ones (their "ready" is stored by the last
-    // warp of the pack), the rest signal "ready" at the entry of the plan's
-    // first launch.
-    std::vector<std::vector<PullDesc>> packs, pull;
-    std::vector<std::uint64_t*> ready_only;
-    for (auto& m : sends) {
-      if (m.mode != PlanMode::Device) continue;
-      if (m.pack.empty()) {
-        ready_only.push_back(m.ready_remote);
-        continue;
-      }
-      std::vector<PullDesc> d = m.pack;
-      for (auto& x : d) x.done = m.ready_remote;
-      packs.push_back(std::move(d));
-    }
-    for (auto& m : recvs)
-      if (m.mode != PlanMode::Shared && !m.descs.empty()) pull.push_back(m.descs);
-    // The packs ride in the pull launch, ahead of every pull chunk, when all
-    // of them share the pull launch's unit class: each CTA (all resident,
-    // the grid is capped at residency) finishes its pack chunks before it
-    // waits on any peer's "ready". Otherwise they get a launch of their own
-    // before the pulls.
-    bool merge = !packs.empty() && !pull.empty();
-    // one launch only: a pack split into a later launch of the peer, behind
-    // pulls that wait, could leave two ranks waiting on each other
-    std::size_t ndesc = 0;
-    for (auto* v : {&packs, &pull})
-      for (auto& m : *v) ndesc += m.size();
-    merge = merge && ndesc <= static_cast<std::size_t>(kMaxBatch);
-    if (merge) {
-      const int cls = pull_unit_class(pull[0][0]);
-      for (auto& m : pull) merge = merge && pull_unit_class(m[0]) == cls;
-      for (auto& m : packs) merge = merge && pull_unit_class(m[0]) == cls;
-    }
-    std::vector<std::vector<PullDesc>> pre;
-    if (merge) {
-      pull.insert(pull.begin(), packs.begin(), packs.end());
-    } else {
-      pre = packs;
-    }
-    // no launch at all would carry the entry signals: a pure-signal launch
-    if (pre.empty() && pull.empty() && !ready_only.empty()) {
-      PullDesc x{};
-      x.ndim = 1;
-      x.unit = 16;
-      x.units = 0;
-      x.nchunks = 1;
-      pre.push_back({x});
-    }
-    // device state: [epoch u64, starts at 1][counters u32 x kCounterSlots]
-    const std::size_t state_bytes = 64 + kCounterSlots * sizeof(std::uint32_t);
-    state_ = at::empty({static_cast<std::int64_t>(state_bytes)},
-                       at::TensorOptions().dtype(at::kByte).device(at::kCUDA, c_->dev));
-    epoch_d_ = reinterpret_cast<std::uint64_t*>(state_.data_ptr());
-    counters_d_ = reinterpret_cast<std::uint32_t*>(static_cast<char*>(state_.data_ptr()) + 64);
-    std::vector<char> init(state_bytes, 0);
-    const std::uint64_t one = 1;
-    std::memcpy(init.data(), &one, sizeof(one));
-    CMX_CUDA(cudaMemcpy(state_.data_ptr(), init.data(), state_bytes, cudaMemcpyHostToDevice));
-    pre_ = batches(pre);
-    pulls_ = batches(pull);
-    if (!ready_only.empty()) {
-      TORCH_CHECK(ready_only.size() <= static_cast<std::size_t>(kMaxEntrySignals), "commux plan: more than ",
-                  kMaxEntrySignals, " unpacked sends to other GPUs");
-      PullBatch& first = pre_.empty() ? *pulls_[0] : *pre_[0];
-      first.nsig = static_cast<std::uint32_t>(ready_only.size());
-      for (std::size_t k = 0; k < ready_only.size(); ++k) first.sig[k] = ready_only[k];
-    }
-    std::memset(&wait_, 0, sizeof(wait_));
-    wait_.timeout_ns = tr_->device_timeout_ns();
-    wait_.status = c_->status_d;
-    wait_.epoch = epoch_d_;
-    wait_.bump = epoch_d_;  // the wait launch also advances the epoch
-    for (auto& m : sends)
-      if (m.mode == PlanMode::Device) {
-        TORCH_CHECK(wait_.n < static_cast<std::uint32_t>(kMaxWaitFlags), "commux plan: more than ",
-                    kMaxWaitFlags, " sends to other GPUs");
-        wait_.flag[wait_.n++] = m.consumed_local;
-      }
-    // COMMUX_PLAN_TRACE: span of every launch of a start (earliest CTA start,
-    // latest CTA end), printed after each start (which then synchronises)
-    if (env_int("COMMUX_PLAN_TRACE", 0) != 0) {
-      const std::size_t n = pre_.size() + pulls_.size() + 1;
-      CMX_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&trace_h_), n * 2 * sizeof(unsigned long long),
-                             cudaHostAllocMapped));
-      unsigned long long* d = nullptr;
-      CMX_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&d), trace_h_, 0));
-      std::size_t k = 0;
-      // the last message-counter slot is the launches' CTA counter (reset
-      // by the last CTA of each launch)
-      std::uint32_t* count = counters_d_ + (kCounterSlots - 1);
-      for (auto* ls : {&pre_, &pulls_})
-        for (auto& b : *ls) {
-          b->trace = d + 2 * k++;
-          b->trace_count = count;
-        }
-      wait_.trace = d + 2 * k;
-      trace_n_ = n;
-    }
-  }
-
-  void start() override {
-    ++starts_;
-    c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(c_->dev));
-    cudaStream_t cur = c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(c_->dev)).stream();
-    // messages to/from a rank on this same GPU go through the host-gated path
-    std::vector<ReqPtr> shared;
-    if (n_shared_) {
-      tr_->begin_batch();
-      try {
-        for (auto& m : recvs)
-          if (m.mode == PlanMode::Shared)
-            shared.push_back(eng_->post_recv({m.t}, m.peer, make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), 0, false)));
-        for (auto& m : sends)
-          if (m.mode == PlanMode::Shared)
-            shared.push_back(eng_->post_send({m.t}, m.peer, make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), 0, false)));
-      } catch (...) {
-        tr_->end_batch();
-        throw;
-      }
-      tr_->end_batch();
-    }
-    if (!exec_) capture();
-    last_stream_ = cur;
-    if (trace_h_ != nullptr)
-      for (std::size_t k = 0; k < trace_n_; ++k) {
-        trace_h_[2 * k] = ~0ull;
-        trace_h_[2 * k + 1] = 0;
-      }
-    CMX_CUDA(cudaGraphLaunch(exec_, cur));
-    tr_->kernel_launches += nodes_;
-    if (trace_h_ != nullptr) report_trace(cur);
-    if (!shared.empty()) {
-      for (auto& r : shared) eng_->wait(r, std::chrono::milliseconds(0));
-      tr_->stream_wait_all(shared);
-    }
-    std::string e = tr_->device_error();
-    if (!e.empty()) C10_THROW_ERROR(DistBackendError, e);
-  }
-
-  std::vector<std::pair<std::string, std::int64_t>> info() override {
-    std::int64_t loc = 0, dev = 0, packed = 0;
-    for (auto* v : {&sends, &recvs})
-      for (auto& m : *v) (m.mode == PlanMode::Local ? loc : dev) += m.mode != PlanMode::Shared;
-    for (auto& m : sends) packed += (m.mode == PlanMode::Device && !m.pack.empty()) ? 1 : 0;
-    return {{"local", loc},      {"device", dev},       {"shared", n_shared_}, {"packed_sends", packed},
-            {"graph_nodes", nodes_}, {"starts", static_cast<std::int64_t>(starts_)}};
-  }
-
-  std::int64_t n_shared_ = 0;
-
- private:
-  void report_trace(cudaStream_t cur) {
-    CMX_CUDA(cudaStreamSynchronize(cur));
-    unsigned long long t0 = ~0ull;
-    for (std::size_t k = 0; k < trace_n_; ++k) t0 = std::min(t0, trace_h_[2 * k]);
-    std::string line;
-    char buf[96];
-    std::size_t k = 0;
-    auto span = [&](const char* what) {
-      const unsigned long long a = trace_h_[2 * k], b = trace_h_[2 * k + 1];
-      ++k;
-      if (a == ~0ull || b == 0) return;  // launch left out of this plan's graph
-      std::snprintf(buf, sizeof(buf), " %s %.1f-%.1f", what, (a - t0) / 1e3, (b - t0) / 1e3);
-      line += buf;
-    };
-    for (std::size_t i = 0; i < pre_.size(); ++i) span("pack");
-    for (std::size_t i = 0; i < pulls_.size(); ++i) span("pull");
-    span("wait");
-    std::fprintf(stderr, "[commux plan trace rank %d] start %llu, us from the first CTA:%s\n", eng_->rank(),
-                 static_cast<unsigned long long>(starts_), line.c_str());
-  }
-
-  // Messages -> parameter blocks of at most kMaxBatch descriptors, one unit
-  // class each; every message counts into its own counter slot (the plan's
-  // launches run one after another and each message returns its counter to
-  // zero, so the slots are reused by the next start).
-  std::vector<std::unique_ptr<PullBatch>> batches(const std::vector<std::vector<PullDesc>>& msgs) {
-    std::map<int, std::vector<PullDesc>> by_cls;
-    std::uint32_t slot = 0;
-    for (auto& m : msgs) {
-      if (m.empty()) continue;
-      const int cls = pull_unit_class(m[0]);
-      std::uint32_t chunks = 0;
-      for (auto& d : m) {
-        TORCH_CHECK(pull_unit_class(d) == cls, "commux plan: a message mixes unit classes");
-        chunks += d.nchunks;
-      }
-      TORCH_CHECK(slot < kCounterSlots - 1, "commux plan: too many messages");
-      auto& v = by_cls[cls];
-      for (auto d : m) {
-        d.counter_idx = slot;
-        d.msg_chunks = chunks;
-        v.push_back(d);
-      }
-      ++slot;
-    }
-    std::vector<std::unique_ptr<PullBatch>> out;
-    for (auto& kv : by_cls) {
-      std::size_t i = 0;
-      while (i < kv.second.size()) {
-        auto b = std::make_unique<PullBatch>();
-        b->n = 0;
-        b->total_chunks = 0;
-        b->counters = counters_d_;
-        b->status = c_->status_d;
-        b->timeout_ns = tr_->device_timeout_ns();
-        b->epoch = epoch_d_;
-        b->nsig = 0;
-        while (i < kv.second.size() && b->n < static_cast<std::uint32_t>(kMaxBatch)) {
-          PullDesc d = kv.second[i++];
-          d.chunk0 = b->total_chunks;
-          b->total_chunks += d.nchunks;
-          b->d[b->n++] = d;
-        }
-        out.push_back(std::move(b));
-      }
-    }
-    return out;
-  }
-
-  void capture() {
-    cudaStream_t cs = nullptr;
-    CMX_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
-    // a launch whose CTAs wait on peers keeps every CTA resident at once, so
-    // a CTA never waits while another CTA of the launch that still has pack
-    // work waits for an SM; launches without waits keep the wider grid
-    bool waits = false;
-    for (auto& m : recvs) waits |= m.mode == PlanMode::Device;
-    const int ctas = waits ? std::min(tr_->pull_ctas(c_), 4 * c_->sm_count) : tr_->pull_ctas(c_);
-    nodes_ = 0;
-    CMX_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
-    cudaError_t e = cudaSuccess;
-    for (auto* ls : {&pre_, &pulls_})
-      for (auto& b : *ls) {
-        int launched = 0;
-        if (e == cudaSuccess) e = launch_pull(*b, ctas, 256, cs, &launched);
-        nodes_ += launched;
-      }
-    // waits (if any), then the epoch bump; a plan whose every message stays
-    // on this GPU has no flags, so no epoch to advance and no launch here
-    bool flags = wait_.n > 0;
-    for (auto& m : recvs) flags |= m.mode == PlanMode::Device;
-    if (e == cudaSuccess && flags) {
-      e = launch_wait(wait_, cs);
-      ++nodes_;
-    }
-    cudaGraph_t g = nullptr;
-    cudaError_t e2 = cudaStreamEndCapture(cs, &g);
-    cudaStreamDestroy(cs);  // holds no tensors: safe to destroy
-    CMX_CUDA(e);
-    CMX_CUDA(e2);
-    graph_ = g;
-    CMX_CUDA(cudaGraphInstantiate(&exec_, graph_, 0));
-  }
-
-  CudaTransport* tr_;
-  Engine* eng_;
-  DevCtx* c_;
-  std::uint64_t starts_ = 0;
-  at::Tensor state_;
-  std::uint64_t* epoch_d_ = nullptr;
-  std::uint32_t* counters_d_ = nullptr;
-  std::vector<std::unique_ptr<PullBatch>> pre_, pulls_;
-  WaitBatch wait_{};
-  cudaGraph_t graph_ = nullptr;
-  cudaGraphExec_t exec_ = nullptr;
-  std::int64_t nodes_ = 0;
-  unsigned long long* trace_h_ = nullptr;  // COMMUX_PLAN_TRACE (host-mapped)
-  std::size_t trace_n_ = 0;
-  cudaStream_t last_stream_ = nullptr;      // stream of the last start
-};
-
-std::vector<PullDesc> CudaTransport::plan_descs(const char* wire, std::size_t len, int src, bool local,
-                                                const at::Tensor& dst, DevCtx* c) {
-  auto r = std::make_shared<Request>();
-  r->kind = ReqKind::Recv;
-  r->device = true;
-  r->tensors = {dst};
-  r->total = static_cast<std::uint64_t>(dst.numel()) * dst.element_size();
-  auto rs = std::make_shared<RecvState>();
-  rs->device = c->dev;
-  r->dev = rs;
-  PendingPull pp;
-  pp.r = r;
-  pp.src = src;
-  pp.ctx = c;
-  build_descs(r, wire, len, local, pp);
-  TORCH_CHECK(rs->unpack.empty(), "commux plan: this receive layout needs a staged copy; persistent plans "
-              "take views whose strides merge to at most 4 dims on both sides");
-  return pp.descs;
-}
-
-DevicePlanPtr CudaTransport::create_plan(const std::vector<at::Tensor>& recv_t, const std::vector<int>& recv_peer,
-                                         const std::vector<int>& recv_tag, const std::vector<at::Tensor>& send_t,
-                                         const std::vector<int>& send_peer, const std::vector<int>& send_tag) {
-  TORCH_CHECK(!recv_t.empty() || !send_t.empty(), "commux plan: no messages");
-  const at::Tensor& any = recv_t.empty() ? send_t[0] : recv_t[0];
-  const int dev = any.device().index();
-  for (auto* v : {&recv_t, &send_t})
-    for (auto& t : *v)
-      TORCH_CHECK(t.is_cuda() && t.device().index() == dev, "commux plan: all tensors must be on one CUDA device");
-  DevCtx* c = ctx(dev);
-  publish_uuid(c);
-  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev));
-  const int me = eng_->rank();
-  auto plan = std::make_shared<CudaPlan>(this, eng_, c);
-
-  // wire description of one tensor (DrtsWire + one SegWire), as a send would
-  auto wire_of = [&](const at::Tensor& t, bool local, std::uint64_t consumed_slot) {
-    std::vector<std::int64_t> sz(t.sizes().begin(), t.sizes().end()), sd(t.strides().begin(), t.strides().end());
-    auto d = dims_of(sz.data(), sd.data(), t.dim());
-    std::vector<Dim> merged;
-    TORCH_CHECK(t.dim() <= kWireDims && refine(d, d, merged) && merged.size() <= static_cast<std::size_t>(kMaxPullDims),
-                "commux plan: send views must merge to at most 4 dims (send a contiguous tensor)");
-    std::vector<char> blob(sizeof(DrtsWire) + sizeof(SegWire), 0);
-    auto* w = reinterpret_cast<DrtsWire*>(blob.data());
-    w->magic = kWireMagic;
-    w->nseg = 1;
-    w->pid = static_cast<std::int32_t>(::getpid());
-    w->device = dev;
-    std::memcpy(w->uuid, c->uuid, 16);
-    w->mbox_id = c->mbox_id;
-    w->mbox_base = c->mbox_base;
-    w->mbox_handle = c->mbox_handle;
-    w->slot = consumed_slot;
-    auto* sw = reinterpret_cast<SegWire*>(blob.data() + sizeof(DrtsWire));
-    sw->elem = static_cast<std::uint32_t>(t.element_size());
-    sw->ndim = static_cast<std::int32_t>(t.dim());
-    for (int k = 0; k < t.dim(); ++k) {
-      sw->sizes[k] = t.size(k);
-      sw->strides[k] = t.stride(k);
-    }
-    if (t.numel() > 0) {
-      const char* p = static_cast<const char*>(t.data_ptr());
-      if (local) {
-        CUpointer_attribute attrs[2] = {CU_POINTER_ATTRIBUTE_RANGE_START_ADDR, CU_POINTER_ATTRIBUTE_RANGE_SIZE};
-        CUdeviceptr start = 0;
-        std::size_t asz = 0;
-        void* data[2] = {&start, &asz};
-        cu_check(cuPointerGetAttributes(2, attrs, data, reinterpret_cast<CUdeviceptr>(p)), "cuPointerGetAttributes");
-        sw->base = static_cast<std::uint64_t>(start);
-        sw->alloc_size = asz;
-      } else {
-        ipc_export(p, &sw->buffer_id, &sw->base, &sw->alloc_size, &sw->handle);
-      }
-      sw->offset = reinterpret_cast<std::uint64_t>(p) - sw->base;
-    }
-    return blob;
-  };
-  auto plan_slot = [&]() {
-    std::uint64_t s = kSlots + c->next_plan_slot.fetch_add(1);
-    TORCH_CHECK(s < 2 * kSlots, "commux plan: out of persistent flag slots");
-    return s;
-  };
-  auto bytes_tensor = [](const void* p, std::size_t n) {
-    at::Tensor t = at::empty({static_cast<std::int64_t>(n)}, at::TensorOptions().dtype(at::kByte));
-    std::memcpy(t.data_ptr(), p, n);
-    return t;
-  };
-  const std::size_t wire_len = sizeof(DrtsWire) + sizeof(SegWire);
-
-  std::vector<ReqPtr> pending_sends;
-  struct RecvSetup {
-    std::size_t idx;
-    ReqPtr req;
-    at::Tensor buf;
-  };
-  std::vector<RecvSetup> desc_recvs, reply_recvs;
-  // sends: descriptor to the receiver, then expect its reply
-  for (std::size_t i = 0; i < send_t.size(); ++i) {
-    CudaPlan::Msg m;
-    m.t = send_t[i];
-    m.peer = send_peer[i];
-    m.tag = send_tag[i];
-    TORCH_CHECK(m.peer >= 0 && m.peer < eng_->size(), "commux plan: invalid send peer ", m.peer);
-    if (m.peer == me) {
-      m.mode = PlanMode::Local;
-    } else {
-      std::uint64_t slot = plan_slot();
-      m.consumed_local = c->mbox + slot;
-      // narrow rows: the receiver reads a contiguous copy packed here (the
-      // pack descriptors run in the plan's first launch; a receiver that
-      // turns out to share this GPU reads the view itself)
-      at::Tensor wire_src = m.t;
-      // also staged: memory that CUDA IPC cannot export; the stage then comes
-      // from the exportable pool
-      const bool unexportable = m.t.numel() > 0 && !exportable(m.t.data_ptr());
-      if (narrow_rows(m.t) || unexportable) {
-        m.stage = at::empty(m.t.sizes(), m.t.options().memory_format(at::MemoryFormat::Contiguous));
-        if (!exportable(m.stage.data_ptr())) m.stage = c->exportable_empty(m.t.sizes(), m.t.scalar_type());
-        auto self_blob = wire_of(m.t, true, 0);
-        m.pack = plan_descs(self_blob.data(), self_blob.size(), me, true, m.stage, c);
-        wire_src = m.stage;
-      }
-      auto blob = wire_of(wire_src, false, slot);
-      pending_sends.push_back(eng_->post_send({bytes_tensor(blob.data(), blob.size())}, m.peer,
-                                              make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), kPlanSub, true)));
-      at::Tensor rb = at::empty({static_cast<std::int64_t>(sizeof(PlanReply))}, at::TensorOptions().dtype(at::kByte));
-      reply_recvs.push_back({plan->sends.size(),
-                             eng_->post_recv({rb}, m.peer, make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), kPlanReplySub, true)),
-                             rb});
-    }
-    plan->sends.push_back(std::move(m));
-  }
-  // receives: expect the sender's descriptor
-  for (std::size_t j = 0; j < recv_t.size(); ++j) {
-    CudaPlan::Msg m;
-    m.t = recv_t[j];
-    m.peer = recv_peer[j];
-    m.tag = recv_tag[j];
-    TORCH_CHECK(m.peer >= 0 && m.peer < eng_->size(), "commux plan: invalid recv peer ", m.peer);
-    if (m.peer == me) {
-      m.mode = PlanMode::Local;
-    } else {
-      at::Tensor db = at::empty({static_cast<std::int64_t>(wire_len)}, at::TensorOptions().dtype(at::kByte));
-      desc_recvs.push_back({plan->recvs.size(),
-                            eng_->post_recv({db}, m.peer, make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), kPlanSub, true)),
-                            db});
-    }
-    plan->recvs.push_back(std::move(m));
-  }
-  // self messages pair up locally, FIFO per tag
-  for (auto& s : plan->sends) {
-    if (s.peer != me) continue;
-    CudaPlan::Msg* r = nullptr;
-    for (auto& x : plan->recvs)
-      if (x.peer == me && !x.matched && x.tag == s.tag) {
-        r = &x;
-        break;
-      }
-    TORCH_CHECK(r != nullptr, "commux plan: self-send with tag ", s.tag, " has no matching self-receive");
-    r->matched = true;
-    auto blob = wire_of(s.t, true, 0);
-    r->descs = plan_descs(blob.data(), blob.size(), me, true, r->t, c);
-  }
-  for (auto& x : plan->recvs)
-    TORCH_CHECK(x.peer != me || x.matched, "commux plan: self-receive with tag ", x.tag, " has no matching self-send");
-  // remote receives: build the pull, allocate "ready", reply to the sender
-  for (auto& rs : desc_recvs) {
-    eng_->wait(rs.req, std::chrono::milliseconds(0));
-    CudaPlan::Msg& m = plan->recvs[rs.idx];
-    const char* blob = static_cast<const char*>(rs.buf.data_ptr());
-    auto* w = reinterpret_cast<const DrtsWire*>(blob);
-    TORCH_CHECK(w->magic == kWireMagic, "commux plan: malformed setup descriptor from rank ", m.peer);
-    const bool same_gpu = std::memcmp(w->uuid, c->uuid, 16) == 0;
-    PlanReply rep;
-    std::memset(&rep, 0, sizeof(rep));
-    rep.magic = kPlanMagic;
-    rep.pid = static_cast<std::int32_t>(::getpid());
-    std::memcpy(rep.uuid, c->uuid, 16);
-    rep.mbox_id = c->mbox_id;
-    rep.mbox_handle = c->mbox_handle;
-    if (same_gpu) {
-      m.mode = PlanMode::Shared;
-      plan->n_shared_++;
-    } else {
-      m.mode = PlanMode::Device;
-      std::uint64_t slot = plan_slot();
-      m.ready_local = c->mbox + slot;
-      rep.ready_slot = slot;
-      m.descs = plan_descs(blob, wire_len, m.peer, false, m.t, c);
-      for (auto& d : m.descs) d.ready = m.ready_local;
-    }
-    pending_sends.push_back(eng_->post_send({bytes_tensor(&rep, sizeof(rep))}, m.peer,
-                                            make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), kPlanReplySub, true)));
-  }
-  // remote sends: learn where to store "ready"
-  for (auto& rr : reply_recvs) {
-    eng_->wait(rr.req, std::chrono::milliseconds(0));
-    CudaPlan::Msg& m = plan->sends[rr.idx];
-    PlanReply rep;
-    std::memcpy(&rep, rr.buf.data_ptr(), sizeof(rep));
-    TORCH_CHECK(rep.magic == kPlanMagic, "commux plan: malformed setup reply from rank ", m.peer);
-    if (std::memcmp(rep.uuid, c->uuid, 16) == 0) {
-      m.mode = PlanMode::Shared;
-      plan->n_shared_++;
-    } else {
-      m.mode = PlanMode::Device;
-      auto* mb = static_cast<std::uint64_t*>(ipc_open(m.peer, rep.mbox_id, 0, 0, rep.mbox_handle, c));
-      m.ready_remote = mb + rep.ready_slot;
-    }
-  }
-  for (auto& s : pending_sends) eng_->wait(s, std::chrono::milliseconds(0));
-  plan->finalize();
-  return plan;
 }
 
 }  // namespace cuda
