@@ -58,4 +58,15 @@ if world >= 2:
         c.check("anysource sources", sorted(seen) == list(range(1, world)), str(seen))
     else:
         dist.send(torch.full((2,), float(rank), device=dev), 0, tag=600)
+    # the same through torch.distributed: recv without src returns the sender
+    if rank == 0:
+        seen = []
+        for _ in range(world - 1):
+            buf = torch.zeros(3, device=dev)
+            src = dist.recv(buf, tag=601)
+            seen.append(src)
+            c.equal(f"dist.recv any source from {src}", buf, torch.full((3,), float(10 * src)))
+        c.check("dist.recv any source senders", sorted(seen) == list(range(1, world)), str(seen))
+    else:
+        dist.send(torch.full((3,), float(10 * rank), device=dev), 0, tag=601)
 c.finish()
