@@ -9,6 +9,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -98,6 +99,22 @@ class CudaPlan final : public DevicePlan {
     }
     for (auto& m : recvs)
       if (m.mode != PlanMode::Shared && !m.descs.empty()) pull.push_back(m.descs);
+    // COMMUX_PLAN_ORDER: chunk order of the pull launch (CTAs take chunks in
+    // order). "plan" (default): the order the receives were given; "local":
+    // copies within this GPU first, hiding the peers' signal latency; "remote":
+    // receives from other GPUs first, starting the long NVLink reads early.
+    {
+      static const std::string order = [] {
+        const char* e = std::getenv("COMMUX_PLAN_ORDER");
+        return std::string(e != nullptr ? e : "plan");
+      }();
+      if (order == "local" || order == "remote") {
+        const bool local_first = order == "local";
+        std::stable_partition(pull.begin(), pull.end(), [&](const std::vector<PullDesc>& v) {
+          return (v[0].ready == nullptr) == local_first;  // a receive from another GPU waits on "ready"
+        });
+      }
+    }
     // The packs ride in the pull launch, ahead of every pull chunk, when all
     // of them share the pull launch's unit class: each CTA (all resident,
     // the grid is capped at residency) finishes its pack chunks before it
