@@ -223,13 +223,14 @@ CollImpl::~CollImpl() {
 
 int CollImpl::choose_ctas(int mode, int algo, std::int64_t bytes) const {
   static const std::int64_t forced = env_int("COMMUX_COLL_CTAS", 0);
-  if (forced > 0) return static_cast<int>(std::min<std::int64_t>(forced, kMaxCollCtas));
   // Every CTA of a launch must be resident at once (CTA b waits for CTA b of
   // the peers): the copy kernels fit two 512-thread CTAs per SM (<= 64
   // registers), the NVLS kernel one. Two per SM measured 8-10 % faster than
   // one on large two-shot allreduces (1 GiB at 2 GPUs: 2.06 vs 2.23 ms).
   const int one = std::min(ctx_->sm_count, kMaxCollCtas);
   const int two = std::min(2 * ctx_->sm_count, kMaxCollCtas);
+  // COMMUX_COLL_CTAS overrides the choice, within residency
+  if (forced > 0) return static_cast<int>(std::min<std::int64_t>(forced, algo == kAlgoNvls ? one : two));
   if (algo == kAlgoNvls) return one;
   if (mode == kModeAllreduce || mode == kModeReduce || mode == kModeReduceScatter) {
     if (algo == kAlgoOneShot)
