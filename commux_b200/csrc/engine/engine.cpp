@@ -412,11 +412,12 @@ ReqPtr Engine::post_send(std::vector<at::Tensor> tensors, int dst, tag_t tag) {
     rec->pad = 0;
     std::memcpy(job->head.data() + sizeof(proto::DrtsRec), blob.data(), blob.size());
     job->req = r;
-    enqueue(dst, std::move(job));
-    if (gate)
+    if (gate) {
+      enqueue(dst, std::move(job));
       wake_progress();  // the progress thread sends it once the data is ready
-    else
-      flush_out(dst, false);
+    } else {
+      post_job(dst, std::move(job));
+    }
     return r;
   }
 
@@ -454,8 +455,7 @@ ReqPtr Engine::post_send(std::vector<at::Tensor> tensors, int dst, tag_t tag) {
     for (std::uint32_t i = 0; i < nseg; ++i)
       segs[i] = {reinterpret_cast<std::uint64_t>(r->host[i].ptr), r->host[i].bytes};
   }
-  enqueue(dst, std::move(job));
-  flush_out(dst, false);
+  post_job(dst, std::move(job));
   return r;
 }
 
@@ -744,6 +744,14 @@ void Engine::enqueue(int dst, std::unique_ptr<OutJob> job) {
                        job->type == proto::kAbort;
   (control ? po.ctrl : po.jobs).push_back(std::move(job));
   po.pending.fetch_add(1);
+}
+
+void Engine::post_job(int dst, std::unique_ptr<OutJob> job) {
+  auto& po = *out_[dst];
+  po.posters.fetch_add(1, std::memory_order_acq_rel);
+  enqueue(dst, std::move(job));
+  flush_out(dst, false);
+  po.posters.fetch_sub(1, std::memory_order_acq_rel);
 }
 
 void Engine::send_fin(int dst, std::uint64_t send_id, std::int64_t status) {
@@ -1399,11 +1407,18 @@ void Engine::progress_loop() {
         abort_group(std::string("progress error: ") + e.what());
       }
     }
+    // Jobs the posting threads left behind (ring full, or their flush lost
+    // the lock race). The progress thread keeps off a peer's queue while a
+    // posting thread is between its enqueue and its own flush, and takes the
+    // lock without blocking: competing for it would turn every post into a
+    // contended mutex hand-off (two futex calls). The loop comes back while
+    // anything is pending.
     bool out_pending = false;
     for (int p = 0; p < size_; ++p) {
-      if (out_[p]->pending.load(std::memory_order_acquire) > 0) {
-        busy |= flush_out(p, true);
-        out_pending |= out_[p]->pending.load() > 0;
+      auto& po = *out_[p];
+      if (po.pending.load(std::memory_order_acquire) > 0) {
+        if (po.posters.load(std::memory_order_acquire) == 0) busy |= flush_out(p, false);
+        out_pending |= po.pending.load() > 0;
       }
     }
     int dev_inflight = 0;

@@ -120,6 +120,7 @@ struct PeerOut {
   std::deque<std::unique_ptr<OutJob>> ctrl;  // FIN/CTS/ABORT: never wait
   std::deque<std::unique_ptr<OutJob>> jobs;  // matched messages, FIFO
   std::atomic<int> pending{0};
+  std::atomic<int> posters{0};    // posting threads between enqueue and their flush
 };
 
 // Fault injection (host side only): COMMUX_FAULT
@@ -205,6 +206,8 @@ class Engine {
   bool flush_out(int dst, bool blocking_lock);
   bool write_job(int dst, PeerOut& po, OutJob& job);
   void enqueue(int dst, std::unique_ptr<OutJob> job);
+  // enqueue + flush from a posting thread (see progress_loop)
+  void post_job(int dst, std::unique_ptr<OutJob> job);
   void check_liveness();
   void fail_peer(int p, const std::string& why);
   void fail_all(const std::string& why);
