@@ -187,7 +187,7 @@ void Engine::release_for_exit() {
       dev_.reset();
     }
   }
-  std::lock_guard<std::mutex> lk(mu_);
+  std::lock_guard<SpinMutex> lk(mu_);
   posted_.clear();
   unexpected_.clear();
   sends_waiting_.clear();
@@ -368,7 +368,7 @@ ReqPtr Engine::post_send(std::vector<at::Tensor> tensors, int dst, tag_t tag) {
       d->prepare_send(r, dst, blob, &gate, &complete_on_post);
       ReqPtr rr;
       {
-        std::lock_guard<std::mutex> lk(mu_);
+        std::lock_guard<SpinMutex> lk(mu_);
         rr = match_posted(rank_, r->key);
         if (rr) {
           rr->source = rank_;
@@ -396,7 +396,7 @@ ReqPtr Engine::post_send(std::vector<at::Tensor> tensors, int dst, tag_t tag) {
       return r;
     }
     {
-      std::lock_guard<std::mutex> lk(mu_);
+      std::lock_guard<SpinMutex> lk(mu_);
       sends_waiting_[r->id] = r;
     }
     d->prepare_send(r, dst, blob, &gate, &complete_on_post);
@@ -437,7 +437,7 @@ ReqPtr Engine::post_send(std::vector<at::Tensor> tensors, int dst, tag_t tag) {
   } else {
     stats_.rndv_msgs++;
     {
-      std::lock_guard<std::mutex> lk(mu_);
+      std::lock_guard<SpinMutex> lk(mu_);
       sends_waiting_[r->id] = r;
     }
     job->type = proto::kRts;
@@ -495,7 +495,7 @@ ReqPtr Engine::post_recv(std::vector<at::Tensor> tensors, int src, tag_t tag) {
   bool flush_to = false;
   bool cma = false;
   {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::lock_guard<SpinMutex> lk(mu_);
     u = match_unexpected(src, r->key);
     if (!u) {
       posted_[r->key].push_back(r);
@@ -529,7 +529,7 @@ ReqPtr Engine::post_recv(std::vector<at::Tensor> tensors, int src, tag_t tag) {
       return r;
     }
     {
-      std::lock_guard<std::mutex> lk(mu_);
+      std::lock_guard<SpinMutex> lk(mu_);
       start_rndv_recv(r, u->src, u->msg_id, u->total);
     }
     flush_out(u->src, false);
@@ -722,7 +722,7 @@ void Engine::wait(const ReqPtr& r, std::chrono::milliseconds timeout) {
 }
 
 std::string Engine::failure_reason() const {
-  std::lock_guard<std::mutex> lk(mu_);
+  std::lock_guard<SpinMutex> lk(mu_);
   return abort_reason_;
 }
 
@@ -739,7 +739,7 @@ void Engine::wake_progress() {
 
 void Engine::enqueue(int dst, std::unique_ptr<OutJob> job) {
   auto& po = *out_[dst];
-  std::lock_guard<std::mutex> lk(po.mu);
+  std::lock_guard<SpinMutex> lk(po.mu);
   const bool control = job->type == proto::kFin || job->type == proto::kCts ||
                        job->type == proto::kAbort;
   (control ? po.ctrl : po.jobs).push_back(std::move(job));
@@ -832,7 +832,7 @@ bool Engine::write_job(int dst, PeerOut& po, OutJob& job) {
 bool Engine::flush_out(int dst, bool blocking_lock) {
   auto& po = *out_[dst];
   if (po.pending.load(std::memory_order_acquire) == 0) return false;
-  std::unique_lock<std::mutex> lk(po.mu, std::defer_lock);
+  std::unique_lock<SpinMutex> lk(po.mu, std::defer_lock);
   if (blocking_lock)
     lk.lock();
   else if (!lk.try_lock())
@@ -940,7 +940,7 @@ void Engine::on_eager(int src, const proto::EagerRec* rec) {
   UnexpPtr u;
   bool reject_device = false;
   {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::lock_guard<SpinMutex> lk(mu_);
     r = match_posted(src, rec->key);
     if (r) {
       r->source = src;
@@ -981,7 +981,7 @@ void Engine::on_eager(int src, const proto::EagerRec* rec) {
     std::memcpy(inf.unexp->data.data(), payload, rec->nbytes);
   inf.got = rec->nbytes;
   if (inf.got < inf.total) {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::lock_guard<SpinMutex> lk(mu_);
     inflight_[src][rec->msg_id] = inf;
     return;
   }
@@ -993,7 +993,7 @@ void Engine::on_eager(int src, const proto::EagerRec* rec) {
   } else if (inf.unexp) {
     ReqPtr b;
     {
-      std::lock_guard<std::mutex> lk(mu_);
+      std::lock_guard<SpinMutex> lk(mu_);
       inf.unexp->arrived = inf.total;
       inf.unexp->complete = true;
       b = inf.unexp->bound;
@@ -1006,7 +1006,7 @@ void Engine::on_frag(int src, const proto::FragRec* rec) {
   const char* payload = reinterpret_cast<const char*>(rec + 1);
   Inflight* inf = nullptr;
   {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::lock_guard<SpinMutex> lk(mu_);
     auto it = inflight_[src].find(rec->msg_id);
     if (it != inflight_[src].end()) inf = &it->second;
   }
@@ -1020,7 +1020,7 @@ void Engine::on_frag(int src, const proto::FragRec* rec) {
   if (inf->got < inf->total) return;
   Inflight done = *inf;
   {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::lock_guard<SpinMutex> lk(mu_);
     inflight_[src].erase(rec->msg_id);
   }
   if (done.recv) {
@@ -1030,7 +1030,7 @@ void Engine::on_frag(int src, const proto::FragRec* rec) {
   } else if (done.unexp) {
     ReqPtr b;
     {
-      std::lock_guard<std::mutex> lk(mu_);
+      std::lock_guard<SpinMutex> lk(mu_);
       done.unexp->arrived = done.total;
       done.unexp->complete = true;
       b = done.unexp->bound;
@@ -1046,7 +1046,7 @@ void Engine::on_rts(int src, const proto::RtsRec* rec) {
   const bool has_segs = rec->nseg > 0 && rec->nseg <= proto::kCmaSegs &&
                         rec->h.len >= sizeof(proto::RtsRec) + rec->nseg * sizeof(proto::CmaSeg);
   {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::lock_guard<SpinMutex> lk(mu_);
     r = match_posted(src, rec->key);
     if (!r) {
       auto u = std::make_shared<Unexpected>();
@@ -1082,7 +1082,7 @@ void Engine::on_rts(int src, const proto::RtsRec* rec) {
       return;
     }
     {
-      std::lock_guard<std::mutex> lk(mu_);
+      std::lock_guard<SpinMutex> lk(mu_);
       start_rndv_recv(r, src, rec->send_id, rec->total);
     }
     started = true;
@@ -1110,7 +1110,7 @@ void Engine::on_rts(int src, const proto::RtsRec* rec) {
 void Engine::on_cts(int src, const proto::CtsRec* rec) {
   ReqPtr s;
   {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::lock_guard<SpinMutex> lk(mu_);
     auto it = sends_waiting_.find(rec->send_id);
     if (it == sends_waiting_.end()) return;
     s = it->second;
@@ -1136,7 +1136,7 @@ void Engine::on_drts(int src, const proto::DrtsRec* rec) {
   const char* blob = reinterpret_cast<const char*>(rec + 1);
   ReqPtr r;
   {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::lock_guard<SpinMutex> lk(mu_);
     r = match_posted(src, rec->key);
     if (!r) {
       auto u = std::make_shared<Unexpected>();
@@ -1165,7 +1165,7 @@ void Engine::on_drts(int src, const proto::DrtsRec* rec) {
 void Engine::on_fin(int src, const proto::FinRec* rec) {
   ReqPtr s;
   {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::lock_guard<SpinMutex> lk(mu_);
     auto it = sends_waiting_.find(rec->send_id);
     if (it == sends_waiting_.end()) return;
     s = it->second;
@@ -1274,7 +1274,7 @@ bool Engine::cma_read(int src, const ReqPtr& r, std::int32_t pid, const proto::C
 void Engine::on_abort(int src, const proto::AbortRec* rec) {
   std::string why(rec->reason, strnlen(rec->reason, sizeof(rec->reason)));
   {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::lock_guard<SpinMutex> lk(mu_);
     if (abort_reason_.empty())
       abort_reason_ = "rank " + std::to_string(src) + " aborted: " + why;
   }
@@ -1288,7 +1288,7 @@ void Engine::on_abort(int src, const proto::AbortRec* rec) {
 
 void Engine::abort_group(const std::string& why) {
   {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::lock_guard<SpinMutex> lk(mu_);
     if (abort_reason_.empty()) abort_reason_ = "rank " + std::to_string(rank_) + ": " + why;
   }
   bool was = aborted_.exchange(true);
@@ -1320,7 +1320,7 @@ void Engine::abort_group(const std::string& why) {
 void Engine::fail_all(const std::string& why) {
   std::vector<ReqPtr> victims;
   {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::lock_guard<SpinMutex> lk(mu_);
     for (auto& kv : posted_)
       for (auto& r : kv.second) victims.push_back(r);
     posted_.clear();
@@ -1339,7 +1339,7 @@ void Engine::fail_peer(int p, const std::string& why) {
   if (dead_[p].exchange(true)) return;
   std::vector<ReqPtr> victims;
   {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::lock_guard<SpinMutex> lk(mu_);
     for (auto it = posted_.begin(); it != posted_.end();) {
       auto& dq = it->second;
       for (auto q = dq.begin(); q != dq.end();) {
@@ -1374,7 +1374,7 @@ void Engine::check_liveness() {
   if (mine->abort_code.load() != 0 && !aborted_.load()) {
     int who = mine->abort_rank.load();
     {
-      std::lock_guard<std::mutex> lk(mu_);
+      std::lock_guard<SpinMutex> lk(mu_);
       if (abort_reason_.empty()) abort_reason_ = "rank " + std::to_string(who) + " aborted the group";
     }
     aborted_.store(true);

@@ -114,8 +114,32 @@ struct OutJob {
   std::function<void()> on_done;  // optional callback after the last record
 };
 
+// A mutex for short critical sections shared by a posting thread and the
+// progress thread: a contended lock spins briefly (the holder is usually
+// about to release it) before it parks in the kernel, which saves the futex
+// wait/wake pair of a plain std::mutex hand-off.
+class SpinMutex {
+ public:
+  void lock() {
+    for (int i = 0; i < 256; ++i) {
+      if (m_.try_lock()) return;
+#if defined(__x86_64__) || defined(__i386__)
+      __builtin_ia32_pause();
+#else
+      std::this_thread::yield();
+#endif
+    }
+    m_.lock();
+  }
+  bool try_lock() { return m_.try_lock(); }
+  void unlock() { m_.unlock(); }
+
+ private:
+  std::mutex m_;
+};
+
 struct PeerOut {
-  std::mutex mu;                  // serialises writers of this ring
+  SpinMutex mu;                   // serialises writers of this ring
   shm::RingWriter ring;
   std::deque<std::unique_ptr<OutJob>> ctrl;  // FIN/CTS/ABORT: never wait
   std::deque<std::unique_ptr<OutJob>> jobs;  // matched messages, FIFO
@@ -260,7 +284,7 @@ class Engine {
   std::vector<std::unique_ptr<PeerOut>> out_;        // out_[dst]
 
   // matching state
-  mutable std::mutex mu_;
+  mutable SpinMutex mu_;
   std::unordered_map<tag_t, std::deque<ReqPtr>> posted_;
   std::unordered_map<tag_t, std::deque<UnexpPtr>> unexpected_;
   std::int64_t unexpected_count_ = 0;
