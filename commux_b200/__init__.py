@@ -50,7 +50,7 @@ except ImportError as _e:  # the build module itself imports this package
 __all__ = [
     "register", "create_backend", "preferred_backend", "stats", "reset_stats",
     "make_ucp_tag", "TAG_MASK_ANY_SOURCE", "IOContext", "make_tcp_io_context",
-    "library_paths",
+    "library_paths", "batch_p2p", "p2p_plan", "transports", "is_commux",
 ]
 
 _REGISTERED = False

@@ -22,3 +22,14 @@ def test_extensions_import_without_driver():
                        env=dict(os.environ, PYTHONPATH=ROOT))
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "import ok ucx" in r.stdout
+
+
+def test_commux_alias_exports_the_api():
+    code = ("import commux, commux_b200\n"
+            "missing = [n for n in commux_b200.__all__ if not hasattr(commux, n)]\n"
+            "assert not missing, missing\n"
+            "assert commux.register is commux_b200.register and commux.p2p_plan is commux_b200.p2p_plan\n"
+            "print('alias ok')\n")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300,
+                       env=dict(os.environ, PYTHONPATH=ROOT))
+    assert r.returncode == 0 and "alias ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
