@@ -12,6 +12,15 @@ import pytest
 from mp import check, run
 
 
+@pytest.mark.parametrize("world", [2, 3])
+def test_p2p_fuzz(world):
+    check(run("fuzz_p2p.py", world, timeout=240))
+
+
+def test_p2p_fuzz_tcp():
+    check(run("fuzz_p2p.py", 2, env={"COMMUX_TRANSPORT": "tcp"}, timeout=240))
+
+
 def test_torch_dist_2ranks():
     check(run("torch_dist.py", 2))
 
