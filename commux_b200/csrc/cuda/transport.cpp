@@ -733,6 +733,11 @@ void CudaTransport::launch_batch(DevCtx* c, std::vector<PendingPull>& pulls, cud
 }
 
 bool CudaTransport::poll() {
+  // inflight_ counts the pulls waiting in pending_ plus those in flights_:
+  // when it is zero there is nothing to do, and the progress thread, which
+  // calls this on every turn of its loop, stays off pend_mu_ (posting threads
+  // take it for every device message and every device_error() check)
+  if (inflight_.load(std::memory_order_acquire) == 0) return false;
   bool busy = false;
   std::vector<PendingPull> ready;
   {
