@@ -81,4 +81,16 @@ if dev.type == "cpu":
     o = torch.empty(2)
     dist.scatter(o, [torch.full((2,), float(r * 7)) for r in range(world)] if rank == 0 else None, src=0)
     c.equal("scatter", o, torch.full((2,), float(rank * 7)))
+# integer and fp64 payloads (exact): SUM / MIN / MAX / PRODUCT
+for dtype in (torch.int64, torch.int32, torch.uint8, torch.float64):
+    for op, fold in ((dist.ReduceOp.SUM, lambda a, b: a + b), (dist.ReduceOp.MIN, torch.minimum),
+                     (dist.ReduceOp.MAX, torch.maximum), (dist.ReduceOp.PRODUCT, lambda a, b: a * b)):
+        def mk(r):
+            return ((torch.arange(9) * (r + 1)) % 5 + (1 if op == dist.ReduceOp.PRODUCT else 0)).to(dtype)
+        want = mk(0)
+        for r in range(1, world):
+            want = fold(want, mk(r))
+        t = mk(rank).to(dev)
+        dist.all_reduce(t, op=op)
+        c.equal(f"all_reduce {dtype} {op}", t, want.to(dtype))
 c.finish()
