@@ -251,6 +251,7 @@ def main() -> None:
                 "l2": "fields 1.1 GB each > 126 MB L2; no flush needed",
                 "backend": "ucx (commux_b200)",
                 "group_window": os.environ.get("COMMUX_GROUP"),
+                "plan_order": os.environ.get("COMMUX_PLAN_ORDER", "plan"),
             },
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": forcing_h.numel() * forcing_h.element_size() * world,
