@@ -1,8 +1,7 @@
 #!/usr/bin/env python
 """Flagship benchmark: tagged 26-direction halo exchange of a 3-D stencil.
 
-Workload (the halo config of the reference's headline metric): a global
-periodic 1024^3 fp64 field ~U(-1,1) (seeded), split over a near-cubic grid of
+Workload: a global periodic 1024^3 fp64 field ~U(-1,1) (seeded), split over a near-cubic grid of
 ranks (2x2x2 at 8 GPUs -> 512^3 per rank; 512^3 per GPU at every N, i.e.
 weak scaling), halo width 2. One step = the 26-neighbour halo exchange
 (tag = 1000 + direction, posted out of order as one isend/irecv batch through

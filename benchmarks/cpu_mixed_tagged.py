@@ -1,13 +1,13 @@
 #!/usr/bin/env python
-"""Timing of the CPU workload of the headline benchmark's first config, on
-this backend or on Gloo (the comparator; the reference UCX backend cannot be
+"""Timing of the mixed tagged workload on CPU tensors, on this backend or on
+Gloo (the comparator; the reference UCX backend cannot be
 built offline). One iteration: every rank posts 64 non-blocking irecv, then
 64 isend of fp32 tensors (1..1M elements, log-spaced, tags 100..163 in
 shuffled order, seed 0), then all_reduce SUM and MAX of a 1M-element fp32
 tensor and a broadcast from rank 0. Reports the max over ranks of the mean
 iteration time after warm-up (host wall clock: CPU tensors).
 
-    torchrun --nproc-per-node 2 benchmarks/cpu_config1.py --backend ucx
+    torchrun --nproc-per-node 2 benchmarks/cpu_mixed_tagged.py --backend ucx
 """
 
 from __future__ import annotations
@@ -75,7 +75,7 @@ def main():
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     if rank == 0:
         moved = sum(sizes) * 4 + 3 * (1 << 22)
-        print(json.dumps({"config": "cpu config 1", "backend": args.backend, "world": world,
+        print(json.dumps({"workload": "cpu mixed tagged p2p + allreduce + broadcast", "backend": args.backend, "world": world,
                           "ms_per_iter": round(float(t) * 1e3, 3),
                           "payload_MB_per_rank": round(moved / 1e6, 2)}), flush=True)
     dist.barrier()

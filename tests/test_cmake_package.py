@@ -109,7 +109,7 @@ def test_fetchcontent_consumer():
         r = subprocess.run(["cmake", "--build", b, "-j", str(os.cpu_count() or 4)], env=env,
                            capture_output=True, text=True, timeout=1200)
         assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]
-        # the commux libraries of this build live in the consumer's tree
+        # the commux libraries built for the consumer live in its own tree
         assert os.path.exists(os.path.join(b, "_deps", "commux-build", "lib", "libcommux.so"))
         r = subprocess.run([os.path.join(b, "consumer")], capture_output=True, text=True)
         assert r.returncode == 0, r.stdout + r.stderr

@@ -1,7 +1,8 @@
 """Multi-rank CPU tests of the commux backend (gloo-free: every rank talks
 through commux's shared-memory engine). Mirrors the reference's Python tests
 (tests/test_torch_dist.py, test_collectives.py, test_reduce_op.py) and adds
-the BASELINE CPU config, coalescing/grouping, halo, DDP, IOContext and
+the mixed tagged p2p + collectives workload, coalescing/grouping, halo, DDP,
+IOContext and
 host-side failure detection."""
 
 import os
@@ -35,18 +36,18 @@ def test_reduce_op_rejected_everywhere(world):
     check(run("reduce_op.py", world, timeout=120))
 
 
-def test_config1_bit_exact():
-    out = check(run("config1.py", 2, timeout=180))
+def test_mixed_tagged_bit_exact():
+    out = check(run("mixed_tagged.py", 2, timeout=180))
     assert "PASSED" in out[0][1]
 
 
-def test_config1_bit_exact_4ranks():
-    check(run("config1.py", 4, timeout=240))
+def test_mixed_tagged_bit_exact_4ranks():
+    check(run("mixed_tagged.py", 4, timeout=240))
 
 
-def test_config1_two_copy_rendezvous():
+def test_mixed_tagged_two_copy_rendezvous():
     # same workload with the single-copy read switched off (ring + CTS path)
-    out = check(run("config1.py", 2, env={"COMMUX_CMA": "0"}, timeout=180))
+    out = check(run("mixed_tagged.py", 2, env={"COMMUX_CMA": "0"}, timeout=180))
     assert "PASSED" in out[0][1]
 
 
@@ -97,8 +98,8 @@ def test_tcp_collectives(world):
     check(run("collectives.py", world, env=TCP, timeout=180))
 
 
-def test_tcp_config1_bit_exact():
-    out = check(run("config1.py", 2, env=TCP, timeout=180))
+def test_tcp_mixed_tagged_bit_exact():
+    out = check(run("mixed_tagged.py", 2, env=TCP, timeout=180))
     assert "PASSED" in out[0][1]
 
 

@@ -1,4 +1,4 @@
-"""CPU config of the headline benchmark: each rank posts 64 non-blocking irecv
+"""Mixed tagged workload on CPU tensors: each rank posts 64 non-blocking irecv
 then 64 isend of fp32 tensors (1..1M elements, log-spaced) with tags 100..163
 in shuffled order (seed 0); all_reduce SUM and MAX of a 1M-element fp32 tensor
 ~N(0,1) seeded by rank; broadcast from rank 0. Results are checked bit-exact
