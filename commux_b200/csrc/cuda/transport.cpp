@@ -186,7 +186,7 @@ CudaTransport::~CudaTransport() { shutdown(); }
 void CudaTransport::shutdown() {
   coll_.reset();
   {
-    std::lock_guard<std::mutex> lk(pend_mu_);
+    std::lock_guard<SpinMutex> lk(pend_mu_);
     pending_.clear();
   }
   bool alive = true;
@@ -200,7 +200,7 @@ void CudaTransport::shutdown() {
     }
   }
   flights_.clear();
-  std::lock_guard<std::mutex> lk(ipc_mu_);
+  std::lock_guard<SpinMutex> lk(ipc_mu_);
   if (alive)
     for (auto& kv : opened_) cudaIpcCloseMemHandle(kv.second.ptr);
   opened_.clear();
@@ -261,7 +261,7 @@ void CudaTransport::ipc_export(const void* ptr, std::uint64_t* buffer_id, std::u
   *buffer_id = id;
   *base = static_cast<std::uint64_t>(start);
   *size = sz;
-  std::lock_guard<std::mutex> lk(ipc_mu_);
+  std::lock_guard<SpinMutex> lk(ipc_mu_);
   auto it = exported_.find(id);
   if (it != exported_.end()) {
     *handle = it->second;
@@ -283,7 +283,7 @@ void CudaTransport::ipc_export(const void* ptr, std::uint64_t* buffer_id, std::u
 
 void* CudaTransport::ipc_open(int src, std::uint64_t buffer_id, std::uint64_t base, std::uint64_t size,
                               const cudaIpcMemHandle_t& h, DevCtx* c) {
-  std::lock_guard<std::mutex> lk(ipc_mu_);
+  std::lock_guard<SpinMutex> lk(ipc_mu_);
   auto key = std::make_pair(src, buffer_id);
   auto it = opened_.find(key);
   if (it != opened_.end()) return it->second.ptr;
@@ -387,7 +387,7 @@ void CudaTransport::prepare_send(const ReqPtr& s, int dst, std::vector<char>& bl
     // A batch shares one ready event, recorded by its first message: it may
     // precede the copies just staged for this one, so a send that staged
     // anything records its own event behind them.
-    std::lock_guard<std::mutex> lk(batch_mu_);
+    std::lock_guard<SpinMutex> lk(batch_mu_);
     st->ready = ready_event_for(c, st->stream, st->staged.empty() ? batch_depth_ : 0, batch_event_);
   }
 
@@ -455,7 +455,7 @@ bool CudaTransport::send_gate_open(const ReqPtr& s) {
   if (e == cudaSuccess) return true;
   if (e == cudaErrorNotReady) return false;
   cudaGetLastError();
-  std::lock_guard<std::mutex> lk(pend_mu_);
+  std::lock_guard<SpinMutex> lk(pend_mu_);
   dev_error_ = std::string("commux: CUDA error while waiting for send data: ") + cudaGetErrorString(e);
   return true;
 }
@@ -471,7 +471,7 @@ void CudaTransport::prepare_recv(const ReqPtr& r) {
   st->device = dev;
   st->stream = current_stream(dev);
   {
-    std::lock_guard<std::mutex> lk(batch_mu_);
+    std::lock_guard<SpinMutex> lk(batch_mu_);
     st->ready = ready_event_for(c, st->stream, batch_depth_, batch_event_);
   }
   r->dev = st;
@@ -653,7 +653,7 @@ void CudaTransport::on_match(const ReqPtr& r, int src, std::uint64_t send_id, co
   st_pulls_++;
   if (!local) {
     {
-      std::lock_guard<std::mutex> lk(pend_mu_);
+      std::lock_guard<SpinMutex> lk(pend_mu_);
       pending_.push_back(std::move(pp));
       inflight_.fetch_add(1);
     }
@@ -668,7 +668,7 @@ void CudaTransport::on_match(const ReqPtr& r, int src, std::uint64_t send_id, co
   if (rs->stream != cur) CMX_CUDA(cudaStreamWaitEvent(cur, rs->ready->ev, 0));
   pp.descs.shrink_to_fit();
   {
-    std::lock_guard<std::mutex> lk(batch_mu_);
+    std::lock_guard<SpinMutex> lk(batch_mu_);
     if (batch_depth_ > 0) {
       // launched together with the rest of the window at end_batch
       batch_local_.push_back({std::move(pp), cur});
@@ -741,7 +741,7 @@ bool CudaTransport::poll() {
   bool busy = false;
   std::vector<PendingPull> ready;
   {
-    std::lock_guard<std::mutex> lk(pend_mu_);
+    std::lock_guard<SpinMutex> lk(pend_mu_);
     for (auto it = pending_.begin(); it != pending_.end();) {
       auto rs = state<RecvState>(it->r);
       cudaError_t e = cudaEventQuery(rs->ready->ev);
@@ -778,7 +778,7 @@ bool CudaTransport::poll() {
     if (e == cudaErrorNotReady) break;
     if (e != cudaSuccess) {
       cudaGetLastError();
-      std::lock_guard<std::mutex> lk(pend_mu_);
+      std::lock_guard<SpinMutex> lk(pend_mu_);
       dev_error_ = std::string("commux: CUDA error in a pull: ") + cudaGetErrorString(e);
     }
     for (auto& fin : f.fins) {
@@ -887,7 +887,7 @@ bool CudaTransport::query(const ReqPtr& r) {
 
 std::string CudaTransport::device_error() {
   {
-    std::lock_guard<std::mutex> lk(pend_mu_);
+    std::lock_guard<SpinMutex> lk(pend_mu_);
     if (!dev_error_.empty()) return dev_error_;
   }
   std::lock_guard<std::mutex> lk(ctx_mu_);
@@ -917,7 +917,7 @@ std::string CudaTransport::device_error() {
 int CudaTransport::inflight() { return inflight_.load(); }
 
 void CudaTransport::begin_batch() {
-  std::lock_guard<std::mutex> lk(batch_mu_);
+  std::lock_guard<SpinMutex> lk(batch_mu_);
   ++batch_depth_;
 }
 
@@ -925,7 +925,7 @@ void CudaTransport::end_batch() {
   std::vector<std::pair<PendingPull, cudaStream_t>> todo;
   std::vector<ReqPtr> sends;
   {
-    std::lock_guard<std::mutex> lk(batch_mu_);
+    std::lock_guard<SpinMutex> lk(batch_mu_);
     if (batch_depth_ == 0 || --batch_depth_ > 0) return;
     todo.swap(batch_local_);
     sends.swap(batch_local_sends_);

@@ -228,7 +228,7 @@ class CudaTransport final : public DeviceTransport {
   std::map<int, std::unique_ptr<DevCtx>> ctx_;
   bool uuid_published_ = false;
 
-  std::mutex ipc_mu_;
+  SpinMutex ipc_mu_;  // shared by posting threads and the progress thread
   std::unordered_map<std::uint64_t, cudaIpcMemHandle_t> exported_;  // by buffer id
   struct Opened {
     void* ptr = nullptr;
@@ -240,7 +240,7 @@ class CudaTransport final : public DeviceTransport {
   std::mutex local_mu_;
   std::unordered_map<std::uint64_t, ReqPtr> local_sends_;  // self-sends awaiting a match
 
-  std::mutex pend_mu_;
+  SpinMutex pend_mu_;  // shared by posting threads and the progress thread
   std::vector<PendingPull> pending_;
   struct Flight {
     EventPtr done;
@@ -251,7 +251,7 @@ class CudaTransport final : public DeviceTransport {
   std::atomic<int> inflight_{0};
 
   // group window batching (self-sends launch at end_batch)
-  std::mutex batch_mu_;
+  SpinMutex batch_mu_;  // shared by posting threads and the progress thread
   int batch_depth_ = 0;
   std::map<int, EventPtr> batch_event_;  // one ready event per device per window
   std::vector<std::pair<PendingPull, cudaStream_t>> batch_local_;
