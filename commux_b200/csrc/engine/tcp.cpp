@@ -147,7 +147,16 @@ struct Links::Peer {
   std::uint64_t sleft = 0;
   std::vector<char> rbuf;  // bytes received, not yet published
   std::size_t rlen = 0;
+  // a large record received straight into its reserved in-ring slot
+  char* direct = nullptr;
+  std::uint64_t dlen = 0, dgot = 0;
 };
+
+namespace {
+// Records at least this long that arrive in pieces are received straight
+// into the in-ring rather than through rbuf (one copy fewer per byte).
+constexpr std::uint64_t kDirectRecvBytes = 64 << 10;
+}  // namespace
 
 Links::Links(int rank, int size, std::uint64_t ring_bytes, std::vector<bool> remote, shm::Segment* own)
     : rank_(rank), size_(size), ring_bytes_(ring_bytes), remote_(std::move(remote)), own_(own) {
@@ -317,6 +326,31 @@ bool Links::pump_peer(Peer& P, bool* want_out, bool* blocked_in) {
   // inbound: bytes -> whole records -> this rank's in-ring for the peer
   const std::uint64_t max_rec = ring_bytes_ / 2;
   for (;;) {
+    if (P.direct != nullptr) {
+      // the rest of a large record, straight into its reserved slot; the
+      // slot is published only once the record is complete
+      while (P.dgot < P.dlen) {
+        ssize_t n = ::recv(P.fd, P.direct + P.dgot, P.dlen - P.dgot, MSG_DONTWAIT);
+        if (n > 0) {
+          P.dgot += static_cast<std::uint64_t>(n);
+          received_ += n;
+          work = true;
+          continue;
+        }
+        if (n == 0) {
+          P.eof = true;  // closed inside a record: the partial record is dropped
+          return work;
+        }
+        if (errno == EINTR) continue;
+        if (errno == EAGAIN || errno == EWOULDBLOCK) return work;
+        fail(std::string("recv: ") + std::strerror(errno));
+        return work;
+      }
+      P.direct = nullptr;
+      P.in.publish();
+      if (wake_) wake_();
+      work = true;
+    }
     std::size_t off = 0;
     bool published = false;
     while (P.rlen - off >= sizeof(shm::WireHdr)) {
@@ -325,7 +359,29 @@ bool Links::pump_peer(Peer& P, bool* want_out, bool* blocked_in) {
         fail("corrupt record stream");
         return work;
       }
-      if (P.rlen - off < h->len) break;
+      if (P.rlen - off < h->len) {
+        if (h->len < kDirectRecvBytes) break;
+        // a large record in pieces: publish the complete records first
+        // (publish() covers every reservation), then reserve its slot
+        if (published) {
+          P.in.publish();
+          if (wake_) wake_();
+          published = false;
+          work = true;
+        }
+        char* dst = P.in.reserve(h->len);
+        if (dst == nullptr) {
+          *blocked_in = true;
+          break;
+        }
+        const std::uint64_t have = P.rlen - off;
+        std::memcpy(dst, h, have);
+        P.direct = dst;
+        P.dlen = h->len;
+        P.dgot = have;
+        off = P.rlen;
+        break;
+      }
       char* dst = P.in.reserve(h->len);
       if (dst == nullptr) {
         *blocked_in = true;
@@ -344,6 +400,7 @@ bool Links::pump_peer(Peer& P, bool* want_out, bool* blocked_in) {
       std::memmove(P.rbuf.data(), P.rbuf.data() + off, P.rlen - off);
       P.rlen -= off;
     }
+    if (P.direct != nullptr) continue;  // receive the rest of the large record
     if (*blocked_in || P.rlen == P.rbuf.size()) break;
     ssize_t n = ::recv(P.fd, P.rbuf.data() + P.rlen, P.rbuf.size() - P.rlen, MSG_DONTWAIT);
     if (n > 0) {
