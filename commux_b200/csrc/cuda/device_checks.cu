@@ -33,10 +33,12 @@
 
 namespace {
 
-constexpr int kOk = 0;
 constexpr int kDisabled = 1;  // production build
-constexpr int kCuda = 2;      // a CUDA call failed
-constexpr int kWrong = 3;     // the check did not behave as specified
+#if defined(COMMUX_DEVICE_CHECKS)
+constexpr int kOk = 0;
+constexpr int kCuda = 2;   // a CUDA call failed
+constexpr int kWrong = 3;  // the check did not behave as specified
+#endif
 
 int fail(char* err, std::size_t len, int code, const char* fmt, ...) {
   if (err != nullptr && len > 0) {
