@@ -33,7 +33,7 @@
 
 namespace {
 
-constexpr int kDisabled = 1;  // production build
+[[maybe_unused]] constexpr int kDisabled = 1;  // production build
 #if defined(COMMUX_DEVICE_CHECKS)
 constexpr int kOk = 0;
 constexpr int kCuda = 2;   // a CUDA call failed
