@@ -147,6 +147,7 @@ Engine::Engine(c10::intrusive_ptr<c10d::Store> store, int rank, int size,
   for (auto& d : dead_) d.store(false);
   eager_limit_ = static_cast<std::uint64_t>(env_int("COMMUX_EAGER_BYTES", 64 << 10));
   spin_us_ = static_cast<int>(env_int("COMMUX_PROGRESS_SPIN_US", 200));
+  spin_wait_us_ = static_cast<int>(std::max<std::int64_t>(0, env_int("COMMUX_WAIT_SPIN_US", 100)));
   wait_poll_ms_ = static_cast<int>(env_int("COMMUX_WAIT_POLL_MS", 1));
   if (wait_poll_ms_ <= 0) wait_poll_ms_ = 1;
   fault_ = FaultSpec::from_env();
@@ -679,9 +680,16 @@ void Engine::wait(const ReqPtr& r, std::chrono::milliseconds timeout) {
   auto limit = timeout.count() > 0 ? timeout : timeout_;
   auto t0 = std::chrono::steady_clock::now();
   auto deadline = t0 + limit;
-  // brief spin: most waits in a latency-bound exchange end within microseconds
-  for (int i = 0; i < 2000 && r->state.load(std::memory_order_acquire) == kPending; ++i)
-    COMMUX_PAUSE();
+  // brief spin: most waits in a latency-bound exchange end within
+  // microseconds. Bounded by time, not by a count: the latency of one pause
+  // differs by an order of magnitude between CPU generations.
+  if (r->state.load(std::memory_order_acquire) == kPending) {
+    const auto spin_end = t0 + std::chrono::microseconds(spin_wait_us_);
+    for (int i = 0; r->state.load(std::memory_order_acquire) == kPending; ++i) {
+      COMMUX_PAUSE();
+      if ((i & 63) == 63 && std::chrono::steady_clock::now() >= spin_end) break;
+    }
+  }
   if (r->state.load(std::memory_order_acquire) == kPending) {
     waiters_.fetch_add(1);
     std::unique_lock<std::mutex> lk(done_mu_);

@@ -267,6 +267,7 @@ class Engine {
   std::uint64_t eager_limit_;
   std::uint64_t frag_bytes_;
   int spin_us_;
+  int spin_wait_us_ = 100;  // COMMUX_WAIT_SPIN_US: spin of a waiting thread before it sleeps
   int wait_poll_ms_;
   FaultSpec fault_;
   std::atomic<std::int64_t> op_count_{0};
