@@ -756,10 +756,15 @@ void Engine::enqueue(int dst, std::unique_ptr<OutJob> job) {
 
 void Engine::post_job(int dst, std::unique_ptr<OutJob> job) {
   auto& po = *out_[dst];
-  po.posters.fetch_add(1, std::memory_order_acq_rel);
+  // released on every exit (a failed write throws): a count left behind
+  // would keep the progress thread off this peer's queue for good
+  struct Poster {
+    std::atomic<int>& n;
+    explicit Poster(std::atomic<int>& c) : n(c) { n.fetch_add(1, std::memory_order_acq_rel); }
+    ~Poster() { n.fetch_sub(1, std::memory_order_acq_rel); }
+  } poster(po.posters);
   enqueue(dst, std::move(job));
   flush_out(dst, false);
-  po.posters.fetch_sub(1, std::memory_order_acq_rel);
 }
 
 void Engine::send_fin(int dst, std::uint64_t send_id, std::int64_t status) {
