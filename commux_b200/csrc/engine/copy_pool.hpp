@@ -18,16 +18,14 @@ namespace commux {
 class CopyPool {
  public:
   explicit CopyPool(int threads) {
-    for (int i = 0; i < threads; ++i) threads_.emplace_back([this] { run(); });
-  }
-  ~CopyPool() {
-    {
-      std::lock_guard<std::mutex> lk(mu_);
-      stop_ = true;
+    try {
+      for (int i = 0; i < threads; ++i) threads_.emplace_back([this] { run(); });
+    } catch (...) {
+      stop_and_join();  // a thread that failed to start leaves the others joinable
+      throw;
     }
-    cv_.notify_all();
-    for (auto& t : threads_) t.join();
   }
+  ~CopyPool() { stop_and_join(); }
   CopyPool(const CopyPool&) = delete;
   CopyPool& operator=(const CopyPool&) = delete;
 
@@ -60,6 +58,16 @@ class CopyPool {
   }
 
  private:
+  void stop_and_join() {
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      stop_ = true;
+    }
+    cv_.notify_all();
+    for (auto& t : threads_)
+      if (t.joinable()) t.join();
+  }
+
   void run() {
     for (;;) {
       std::function<void()> f;

@@ -1261,10 +1261,19 @@ bool Engine::cma_read(int src, const ReqPtr& r, std::int32_t pid, const proto::C
       }
     }
   };
+  if (shares > 1) {
+    std::call_once(copy_pool_once_, [&] {
+      try {
+        copy_pool_ = std::make_unique<CopyPool>(copy_threads_);
+      } catch (const std::exception& e) {  // no threads to spare: copy alone
+        logf(LogLevel::Info, rank_, "single-copy helper threads unavailable (%s)", e.what());
+      }
+    });
+    if (!copy_pool_) shares = 1;
+  }
   if (shares <= 1) {
     copy_range(0, total);
   } else {
-    std::call_once(copy_pool_once_, [&] { copy_pool_ = std::make_unique<CopyPool>(copy_threads_); });
     std::vector<std::function<void()>> tasks;
     const std::uint64_t step = (total + shares - 1) / shares;
     for (std::uint64_t lo = 0; lo < total; lo += step)
