@@ -79,7 +79,7 @@ def main() -> None:
     ap.add_argument("--build-dir")
     ap.add_argument("-j", "--jobs", type=int)
     ap.add_argument("-v", "--verbose", action="store_true")
-    ap.add_argument("--sanitize", default="", help="thread or address (host code)")
+    ap.add_argument("--sanitize", default="", help="thread, address or undefined (host code)")
     ap.add_argument("--device-checks", action="store_true",
                     help="kernels bounds-check descriptors and report instead of faulting")
     ap.add_argument("--no-cuda", action="store_true")
