@@ -33,3 +33,14 @@ def test_commux_alias_exports_the_api():
     r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300,
                        env=dict(os.environ, PYTHONPATH=ROOT))
     assert r.returncode == 0 and "alias ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+def test_halo_helper_under_both_names():
+    code = ("import commux.halo as a, commux_b200.halo as b, commux_b200.parallel.halo as c\n"
+            "assert a.HaloExchange is b.HaloExchange is c.HaloExchange\n"
+            "g = a.CartGrid((2, 2, 2), 5)\n"
+            "assert len(a.DIRECTIONS) == 26 and a.TAG_BASE == 1000 and g.neighbor((1, 0, 0)) != 5\n"
+            "print('halo ok')\n")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300,
+                       env=dict(os.environ, PYTHONPATH=ROOT))
+    assert r.returncode == 0 and "halo ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
