@@ -296,7 +296,8 @@ void Engine::bootstrap() {
   if (links_) {
     links_->connect(*store_, pfx, timeout_);
     links_->start([this] { wake_progress(); },
-                  [this](int p, const std::string& why) { fail_peer(p, why); });
+                  [this](int p, const std::string& why) { fail_peer(p, why); },
+                  [this](std::uint64_t id) { on_pump_sent(id); });
   }
   // Everyone has mapped everyone: drop the names so a crash leaks nothing.
   store_barrier(pfx + "mapped");
@@ -767,6 +768,18 @@ void Engine::post_job(int dst, std::unique_ptr<OutJob> job) {
   flush_out(dst, false);
 }
 
+void Engine::on_pump_sent(std::uint64_t id) {
+  ReqPtr r;
+  {
+    std::lock_guard<std::mutex> lk(pump_mu_);
+    auto it = pump_waiting_.find(id);
+    if (it == pump_waiting_.end()) return;
+    r = std::move(it->second);
+    pump_waiting_.erase(it);
+  }
+  complete(r);
+}
+
 void Engine::send_fin(int dst, std::uint64_t send_id, std::int64_t status) {
   auto job = std::make_unique<OutJob>();
   job->type = proto::kFin;
@@ -795,7 +808,56 @@ bool Engine::write_job(int dst, PeerOut& po, OutJob& job) {
     stats_.records_out++;
     return true;
   }
-  // payload stream: EAGER head + FRAG continuation, or DATA (FRAG only)
+  // payload stream: EAGER head + FRAG continuation, or DATA (FRAG only).
+  // To a TCP peer, a large payload in one host segment travels as indirect
+  // records: the pump sends it straight from the request's memory, and the
+  // request completes once the pump has sent its last record.
+  constexpr std::uint64_t kIndirectMin = 64 << 10;
+  const bool indirect = remote_[dst] && job.req && job.req->host.size() == 1 && job.total >= kIndirectMin &&
+                        job.req->host[0].bytes >= job.total;
+  while (indirect && (!job.head_sent || job.off < job.total)) {
+    const std::uint64_t chunk = std::min<std::uint64_t>(job.total - job.off, frag_bytes_);
+    const std::uint64_t hdr = job.head_sent ? sizeof(proto::FragRec) : sizeof(proto::EagerRec);
+    const std::uint64_t n = shm::align8(sizeof(proto::IndirectRec));
+    char* p = ring.reserve(n);
+    if (p == nullptr) return false;
+    auto* ir = reinterpret_cast<proto::IndirectRec*>(p);
+    std::memset(ir, 0, sizeof(*ir));
+    ir->h.len = static_cast<std::uint32_t>(n);
+    ir->h.type = proto::kIndirect;
+    ir->wire_len = static_cast<std::uint32_t>(shm::align8(hdr + chunk));
+    ir->head_bytes = static_cast<std::uint32_t>(hdr);
+    ir->payload = reinterpret_cast<std::uint64_t>(job.req->host[0].ptr + job.off);
+    ir->payload_bytes = chunk;
+    auto* wh = reinterpret_cast<shm::WireHdr*>(ir->head);
+    wh->len = ir->wire_len;
+    wh->flags = 0;
+    if (!job.head_sent) {
+      auto* rec = reinterpret_cast<proto::EagerRec*>(ir->head);
+      wh->type = proto::kEager;
+      rec->key = job.req->key;
+      rec->total = job.total;
+      rec->msg_id = job.msg_id;
+      rec->nbytes = chunk;
+      job.head_sent = true;
+    } else {
+      auto* rec = reinterpret_cast<proto::FragRec*>(ir->head);
+      wh->type = proto::kFrag;
+      rec->msg_id = job.msg_id;
+      rec->offset = job.off;
+      rec->nbytes = chunk;
+    }
+    job.off += chunk;
+    if (job.off >= job.total && job.complete_req_when_done) {
+      // registered before the ring is published, so the pump finds it
+      std::lock_guard<std::mutex> lk(pump_mu_);
+      pump_waiting_[job.req->id] = job.req;
+      ir->h.flags = proto::kIndirectComplete;
+      ir->done_id = job.req->id;
+      job.completes_when_sent = true;
+    }
+    stats_.records_out++;
+  }
   while (!job.head_sent || job.off < job.total) {
     std::uint64_t chunk = std::min<std::uint64_t>(job.total - job.off, frag_bytes_);
     std::uint64_t hdr = job.head_sent ? sizeof(proto::FragRec) : sizeof(proto::EagerRec);
@@ -891,7 +953,7 @@ bool Engine::flush_out(int dst, bool blocking_lock) {
   }
   lk.unlock();
   for (auto& j : finished) {
-    if (j->complete_req_when_done && j->req) complete(j->req);
+    if (j->complete_req_when_done && j->req && !j->completes_when_sent) complete(j->req);
     if (j->on_done) j->on_done();
   }
   return wrote;

@@ -111,6 +111,7 @@ struct OutJob {
   std::uint64_t total = 0;        // payload bytes
   bool head_sent = false;
   bool complete_req_when_done = false;
+  bool completes_when_sent = false;  // TCP pump completes req (indirect records)
   std::function<void()> on_done;  // optional callback after the last record
 };
 
@@ -232,6 +233,8 @@ class Engine {
   void enqueue(int dst, std::unique_ptr<OutJob> job);
   // enqueue + flush from a posting thread (see progress_loop)
   void post_job(int dst, std::unique_ptr<OutJob> job);
+  // the TCP pump has sent the last record of request `id` (indirect records)
+  void on_pump_sent(std::uint64_t id);
   void check_liveness();
   void fail_peer(int p, const std::string& why);
   void fail_all(const std::string& why);
@@ -268,6 +271,8 @@ class Engine {
   std::uint64_t frag_bytes_;
   int spin_us_;
   int spin_wait_us_ = 100;  // COMMUX_WAIT_SPIN_US: spin of a waiting thread before it sleeps
+  std::mutex pump_mu_;                                      // guards pump_waiting_
+  std::unordered_map<std::uint64_t, ReqPtr> pump_waiting_;  // sends the TCP pump completes
   int wait_poll_ms_;
   FaultSpec fault_;
   std::atomic<std::int64_t> op_count_{0};

@@ -32,6 +32,7 @@ enum : std::uint16_t {
   kDrts = 5,
   kFin = 6,
   kAbort = 7,
+  kIndirect = 8,  // sender-local, TCP peers only: never crosses the wire
 };
 
 constexpr std::uint64_t kDataBit = 1ull << 63;
@@ -52,6 +53,26 @@ struct FragRec {
   std::uint64_t nbytes;
   // payload follows
 };
+
+// Written into the out-ring of a TCP peer instead of an EAGER or FRAG record
+// with a large payload: it names the payload in this process's memory, and
+// the TCP pump sends the record header it carries followed by the payload
+// straight from there (zero padding up to wire_len), so the payload is not
+// copied into the ring first. With h.flags == kIndirectComplete, the request
+// `done_id` completes once the pump has sent the record: the payload memory
+// must stay valid until then.
+constexpr std::uint16_t kIndirectComplete = 1;
+struct IndirectRec {
+  shm::WireHdr h;
+  std::uint32_t wire_len;    // bytes of the record on the wire (header + payload + pad)
+  std::uint32_t head_bytes;  // bytes of the header below (EagerRec or FragRec)
+  std::uint64_t payload;     // address of the payload in this process
+  std::uint64_t payload_bytes;
+  std::uint64_t done_id;
+  std::uint64_t head[5];     // the on-wire record header
+};
+static_assert(sizeof(EagerRec) <= sizeof(IndirectRec::head) && sizeof(FragRec) <= sizeof(IndirectRec::head),
+              "an indirect record carries the whole record header");
 
 // Host rendezvous. When the sender's bytes are in at most kCmaSegs host
 // segments, the record also lists them (address, length) with the sender's

@@ -1,5 +1,7 @@
 #include "tcp.hpp"
 
+#include "protocol.hpp"
+
 #include <arpa/inet.h>
 #include <fcntl.h>
 #include <netdb.h>
@@ -145,6 +147,8 @@ struct Links::Peer {
   const shm::WireHdr* cur = nullptr;  // record being sent
   const char* sptr = nullptr;
   std::uint64_t sleft = 0;
+  const proto::IndirectRec* ind = nullptr;  // cur, when it is an indirect record
+  std::uint64_t ioff = 0;                   // wire bytes of it already sent
   std::vector<char> rbuf;  // bytes received, not yet published
   std::size_t rlen = 0;
   // a large record received straight into its reserved in-ring slot
@@ -268,9 +272,11 @@ void Links::connect(c10d::Store& store, const std::string& pfx, std::chrono::mil
   listen_fd_ = -1;
 }
 
-void Links::start(std::function<void()> wake, std::function<void(int, const std::string&)> dead) {
+void Links::start(std::function<void()> wake, std::function<void(int, const std::string&)> dead,
+                  std::function<void(std::uint64_t)> sent) {
   wake_ = std::move(wake);
   dead_ = std::move(dead);
+  sent_cb_ = std::move(sent);
   thread_ = std::thread([this] { pump(); });
 }
 
@@ -293,23 +299,60 @@ bool Links::pump_peer(Peer& P, bool* want_out, bool* blocked_in) {
     if (dead_) dead_(P.p, "commux: peer rank " + std::to_string(P.p) + " failed: its TCP connection was lost (" + why + ")");
   };
   // outbound: whole records from the out-ring, in order
+  static const char kZeros[8] = {};
   for (;;) {
-    if (P.sleft == 0) {
+    if (P.cur == nullptr) {
       const shm::WireHdr* h = P.out.peek();
       if (h == nullptr) break;
       P.cur = h;
-      P.sptr = reinterpret_cast<const char*>(h);
-      P.sleft = h->len;
+      if (h->type == proto::kIndirect) {
+        // header carried in the record, payload from the sender's memory,
+        // zero padding up to wire_len
+        P.ind = reinterpret_cast<const proto::IndirectRec*>(h);
+        P.ioff = 0;
+        P.sleft = P.ind->wire_len;
+      } else {
+        P.ind = nullptr;
+        P.sptr = reinterpret_cast<const char*>(h);
+        P.sleft = h->len;
+      }
     }
-    ssize_t n = ::send(P.fd, P.sptr, P.sleft, MSG_NOSIGNAL | MSG_DONTWAIT);
+    ssize_t n;
+    if (P.ind != nullptr) {
+      const proto::IndirectRec& ir = *P.ind;
+      const std::uint64_t hb = ir.head_bytes, pb = ir.payload_bytes;
+      iovec iov[3];
+      int k = 0;
+      std::uint64_t off = P.ioff;
+      if (off < hb) {
+        iov[k++] = {const_cast<char*>(reinterpret_cast<const char*>(ir.head)) + off, static_cast<std::size_t>(hb - off)};
+        off = hb;
+      }
+      if (off < hb + pb) {
+        iov[k++] = {reinterpret_cast<char*>(ir.payload) + (off - hb), static_cast<std::size_t>(hb + pb - off)};
+        off = hb + pb;
+      }
+      if (off < ir.wire_len) iov[k++] = {const_cast<char*>(kZeros), static_cast<std::size_t>(ir.wire_len - off)};
+      msghdr m{};
+      m.msg_iov = iov;
+      m.msg_iovlen = static_cast<std::size_t>(k);
+      n = ::sendmsg(P.fd, &m, MSG_NOSIGNAL | MSG_DONTWAIT);
+      if (n > 0) P.ioff += static_cast<std::uint64_t>(n);
+    } else {
+      n = ::send(P.fd, P.sptr, P.sleft, MSG_NOSIGNAL | MSG_DONTWAIT);
+      if (n > 0) P.sptr += n;
+    }
     if (n > 0) {
-      P.sptr += n;
       P.sleft -= static_cast<std::uint64_t>(n);
       sent_ += n;
       work = true;
       if (P.sleft == 0) {
+        const bool report = P.ind != nullptr && (P.ind->h.flags & proto::kIndirectComplete) != 0;
+        const std::uint64_t id = report ? P.ind->done_id : 0;
         P.out.pop(P.cur);
         P.cur = nullptr;
+        P.ind = nullptr;
+        if (report && sent_cb_) sent_cb_(id);
       }
       continue;
     }

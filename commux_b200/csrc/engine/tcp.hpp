@@ -52,8 +52,10 @@ class Links {
   char* out_data(int p) const;
 
   // Start the pump thread. `wake` rings this rank's doorbell; `dead(p, why)`
-  // reports a lost peer.
-  void start(std::function<void()> wake, std::function<void(int, const std::string&)> dead);
+  // reports a lost peer; `sent(id)` reports that the last indirect record of
+  // request `id` has left (its payload memory is no longer read).
+  void start(std::function<void()> wake, std::function<void(int, const std::string&)> dead,
+             std::function<void(std::uint64_t)> sent);
   void notify();  // new bytes in some out-ring
   void stop();
 
@@ -77,6 +79,7 @@ class Links {
   std::atomic<bool> stop_{false};
   std::function<void()> wake_;
   std::function<void(int, const std::string&)> dead_;
+  std::function<void(std::uint64_t)> sent_cb_;
   std::atomic<std::int64_t> sent_{0}, received_{0};
 };
 
