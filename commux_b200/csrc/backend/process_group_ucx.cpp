@@ -1170,4 +1170,64 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::alltoall_base(at::Tensor& output
   return completed_work(engine_.get(), c10d::OpType::ALLTOALL_BASE, {outputBuffer});
 }
 
+c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::alltoall(std::vector<at::Tensor>& outputTensors,
+                                                         std::vector<at::Tensor>& inputTensors,
+                                                         const c10d::AllToAllOptions& /*opts*/) {
+  TraceRange trace_("commux.alltoall_list");
+  const int P = getSize();
+  TORCH_CHECK(static_cast<int>(outputTensors.size()) == P && static_cast<int>(inputTensors.size()) == P,
+              "commux alltoall: needs world_size input and output tensors");
+  check_same_device_kind(outputTensors, "alltoall");
+  check_same_device_kind(inputTensors, "alltoall");
+  TORCH_CHECK(outputTensors[0].is_cuda() == inputTensors[0].is_cuda(),
+              "commux alltoall: inputs and outputs must live on the same kind of device");
+  if (outputTensors[0].is_cuda() && engine_->any_remote()) {
+    // a group spanning hosts: stage through host memory
+    std::vector<at::Tensor> hout, hin;
+    for (int p = 0; p < P; ++p) {
+      hout.push_back(at::empty(outputTensors[p].sizes(), outputTensors[p].options().device(at::kCPU)));
+      hin.push_back(inputTensors[p].cpu());
+    }
+    alltoall(hout, hin, c10d::AllToAllOptions())->wait();
+    for (int p = 0; p < P; ++p) outputTensors[p].copy_(hout[p]);
+    return completed_work(engine_.get(), c10d::OpType::ALLTOALL, outputTensors);
+  }
+  const tag_t tg = make_ucp_tag(0, CollEngine::kAllToAll * 16 + 1, 0, true);
+  if (outputTensors[0].is_cuda()) {
+    // tagged device p2p, one batch (strided views are gathered and scattered
+    // inside the copy)
+    auto* dev = engine_->device();
+    dev->begin_batch();
+    std::vector<ReqPtr> reqs;
+    try {
+      for (int p = 0; p < P; ++p) {
+        reqs.push_back(engine_->post_recv({outputTensors[p]}, p, tg));
+        reqs.push_back(engine_->post_send({inputTensors[p]}, p, tg));
+      }
+    } catch (...) {
+      dev->end_batch();
+      throw;
+    }
+    dev->end_batch();
+    return c10::make_intrusive<CommuxWork>(engine_.get(), c10d::OpType::ALLTOALL, reqs, outputTensors);
+  }
+  // host: contiguous sends, contiguous temps for strided outputs
+  std::vector<at::Tensor> outs(P), ins(P);
+  for (int p = 0; p < P; ++p) {
+    ins[p] = inputTensors[p].contiguous();
+    outs[p] = outputTensors[p].is_contiguous() ? outputTensors[p] : at::empty(outputTensors[p].sizes(),
+                                                                               outputTensors[p].options());
+  }
+  std::vector<ReqPtr> reqs;
+  for (int p = 0; p < P; ++p)
+    if (p != getRank()) reqs.push_back(engine_->post_recv({outs[p]}, p, tg));
+  for (int p = 0; p < P; ++p)
+    if (p != getRank()) reqs.push_back(engine_->post_send({ins[p]}, p, tg));
+  outs[getRank()].copy_(ins[getRank()]);
+  for (auto& r : reqs) engine_->wait(r, std::chrono::milliseconds(0));
+  for (int p = 0; p < P; ++p)
+    if (!outs[p].is_same(outputTensors[p])) outputTensors[p].copy_(outs[p]);
+  return completed_work(engine_.get(), c10d::OpType::ALLTOALL, outputTensors);
+}
+
 }  // namespace commux

@@ -118,6 +118,10 @@ class ProcessGroupUCX : public c10d::Backend {
       std::vector<int64_t>& outputSplitSizes,
       std::vector<int64_t>& inputSplitSizes,
       const c10d::AllToAllOptions& opts = c10d::AllToAllOptions()) override;
+  // list form: outputTensors[p] receives rank p's inputTensors[me]
+  c10::intrusive_ptr<c10d::Work> alltoall(
+      std::vector<at::Tensor>& outputTensors, std::vector<at::Tensor>& inputTensors,
+      const c10d::AllToAllOptions& opts = c10d::AllToAllOptions()) override;
 
   // --- coalescing (group) window: the c10d analog of ncclGroupStart/End ----
   // With COMMUX_GROUP=1, send()/recv() between startCoalescing() and

@@ -72,6 +72,16 @@ if dev.type == "cpu" or os.environ.get("CMX_A2A", "1") == "1":
     dist.all_to_all_single(out, inp)
     want = torch.cat([torch.arange(2 * rank, 2 * rank + 2, dtype=torch.float32) + 1000 * r for r in range(world)])
     c.equal("all_to_all_single", out, want)
+    # list form: outs[p] receives rank p's ins[me]
+    ins = [torch.full((3,), float(100 * rank + p), device=dev) for p in range(world)]
+    if dev.type == "cpu":  # a strided output view too
+        base = torch.zeros(world, 6)
+        outs = [base[p, ::2] for p in range(world)]
+    else:
+        outs = [torch.empty(3, device=dev) for _ in range(world)]
+    dist.all_to_all(outs, ins)
+    for p in range(world):
+        c.equal(f"all_to_all list from {p}", outs[p], torch.full((3,), float(100 * p + rank)))
 if dev.type == "cpu":
     g = [torch.empty(3) for _ in range(world)] if rank == 0 else None
     dist.gather(torch.full((3,), float(rank)), g, dst=0)
