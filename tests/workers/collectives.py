@@ -83,6 +83,17 @@ if dev.type == "cpu" or os.environ.get("CMX_A2A", "1") == "1":
     for p in range(world):
         c.equal(f"all_to_all list from {p}", outs[p], torch.full((3,), float(100 * p + rank)))
 if dev.type == "cpu":
+    # object collectives (torch pickles into byte tensors over this backend)
+    o = [{"rank": rank, "v": [rank] * 3}] if rank == 0 else [None]
+    dist.broadcast_object_list(o, src=0)
+    c.check("broadcast_object_list", o[0] == {"rank": 0, "v": [0, 0, 0]}, str(o))
+    allo = [None] * world
+    dist.all_gather_object(allo, ("r", rank))
+    c.check("all_gather_object", allo == [("r", r) for r in range(world)], str(allo))
+    got = [None]
+    dist.scatter_object_list(got, [f"x{r}" for r in range(world)] if rank == 0 else None, src=0)
+    c.check("scatter_object_list", got[0] == f"x{rank}", str(got))
+if dev.type == "cpu":
     g = [torch.empty(3) for _ in range(world)] if rank == 0 else None
     dist.gather(torch.full((3,), float(rank)), g, dst=0)
     if rank == 0:
