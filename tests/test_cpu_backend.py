@@ -13,6 +13,11 @@ import pytest
 from mp import check, run
 
 
+@pytest.mark.parametrize("world", [3, 4])
+def test_subgroups(world):
+    check(run("subgroups.py", world, timeout=180))
+
+
 @pytest.mark.parametrize("world", [2, 3])
 def test_p2p_fuzz(world):
     check(run("fuzz_p2p.py", world, timeout=240))
