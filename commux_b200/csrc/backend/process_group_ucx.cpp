@@ -297,6 +297,19 @@ class CollEngine {
 
   static std::int64_t lo(std::int64_t n, int P, int j) { return n * j / P; }
 
+  // fold_ranks over disjoint element ranges on the engine's copy helpers for
+  // large tensors: every element still folds in rank order, so the result is
+  // the same bit for bit
+  void pfold(at::ScalarType dt, RedOp op, void* out, const void* const* bufs, int nb, std::int64_t n,
+             int nranks) {
+    const std::int64_t es = static_cast<std::int64_t>(c10::elementSize(dt));
+    e_->parallel_ranges(n, std::max<std::int64_t>(1, (512 << 10) / es), [&](std::int64_t a, std::int64_t b) {
+      std::vector<const void*> part(static_cast<std::size_t>(nb));
+      for (int k = 0; k < nb; ++k) part[k] = static_cast<const char*>(bufs[k]) + a * es;
+      fold_ranks(dt, op, static_cast<char*>(out) + a * es, part.data(), nb, b - a, nranks);
+    });
+  }
+
   // In-place allreduce of a contiguous 1-D view.
   void allreduce(at::Tensor& t, RedOp op, std::size_t sub) {
     const std::int64_t n = t.numel();
@@ -317,7 +330,7 @@ class CollEngine {
         if (p != me_) reqs.push_back(send(mine, p, tag(kAllreduce, 0, sub)));
       wait_all(reqs);
       for (int p = 0; p < P_; ++p) bufs[p] = p == me_ ? mine.data_ptr() : tmp[p].data_ptr();
-      fold_ranks(dt, op, t.data_ptr(), bufs.data(), P_, n, P_);
+      pfold(dt, op, t.data_ptr(), bufs.data(), P_, n, P_);
       return;
     }
     // reduce-scatter (rank j folds chunk j in rank order) + allgather
@@ -335,7 +348,7 @@ class CollEngine {
     at::Tensor own = t.narrow(0, mlo, mhi - mlo);
     std::vector<const void*> bufs(P_);
     for (int p = 0; p < P_; ++p) bufs[p] = p == me_ ? own.data_ptr() : tmp[p].data_ptr();
-    fold_ranks(dt, op, own.data_ptr(), bufs.data(), P_, mhi - mlo, P_);
+    pfold(dt, op, own.data_ptr(), bufs.data(), P_, mhi - mlo, P_);
     for (int p = 0; p < P_; ++p)
       if (p != me_)
         reqs.push_back(recv(t.narrow(0, lo(n, P_, p), lo(n, P_, p + 1) - lo(n, P_, p)), p,
@@ -363,7 +376,7 @@ class CollEngine {
     }
     wait_all(reqs);
     for (int p = 0; p < P_; ++p) bufs[p] = p == me_ ? t.data_ptr() : tmp[p].data_ptr();
-    fold_ranks(dt, op, t.data_ptr(), bufs.data(), P_, n, P_);
+    pfold(dt, op, t.data_ptr(), bufs.data(), P_, n, P_);
   }
 
   void broadcast(at::Tensor& t, int root, std::size_t sub) {
@@ -441,7 +454,7 @@ class CollEngine {
     std::vector<const void*> bufs(P_);
     at::Tensor own = ins[me_].contiguous();
     for (int p = 0; p < P_; ++p) bufs[p] = p == me_ ? own.data_ptr() : tmp[p].data_ptr();
-    fold_ranks(out.scalar_type(), op, out.data_ptr(), bufs.data(), P_, out.numel(), P_);
+    pfold(out.scalar_type(), op, out.data_ptr(), bufs.data(), P_, out.numel(), P_);
   }
 
   void alltoall(const std::vector<at::Tensor>& outs, const std::vector<at::Tensor>& ins) {

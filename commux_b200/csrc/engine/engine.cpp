@@ -768,6 +768,35 @@ void Engine::post_job(int dst, std::unique_ptr<OutJob> job) {
   flush_out(dst, false);
 }
 
+CopyPool* Engine::copy_pool() {
+  if (copy_threads_ <= 0) return nullptr;
+  std::call_once(copy_pool_once_, [&] {
+    try {
+      copy_pool_ = std::make_unique<CopyPool>(copy_threads_);
+    } catch (const std::exception& e) {  // no threads to spare: work alone
+      logf(LogLevel::Info, rank_, "copy helper threads unavailable (%s)", e.what());
+    }
+  });
+  return copy_pool_.get();
+}
+
+void Engine::parallel_ranges(std::int64_t n, std::int64_t grain,
+                             const std::function<void(std::int64_t, std::int64_t)>& fn) {
+  std::int64_t parts = 1;
+  if (n >= 2 * grain && copy_threads_ > 0)
+    parts = std::min<std::int64_t>(copy_threads_ + 1, n / std::max<std::int64_t>(1, grain));
+  CopyPool* pool = parts > 1 ? copy_pool() : nullptr;
+  if (pool == nullptr) {
+    if (n > 0) fn(0, n);
+    return;
+  }
+  std::vector<std::function<void()>> tasks;
+  const std::int64_t step = (n + parts - 1) / parts;
+  for (std::int64_t lo = 0; lo < n; lo += step)
+    tasks.push_back([&fn, lo, hi = std::min(n, lo + step)] { fn(lo, hi); });
+  pool->run_all(tasks);
+}
+
 void Engine::on_pump_sent(std::uint64_t id) {
   ReqPtr r;
   {
@@ -1323,16 +1352,7 @@ bool Engine::cma_read(int src, const ReqPtr& r, std::int32_t pid, const proto::C
       }
     }
   };
-  if (shares > 1) {
-    std::call_once(copy_pool_once_, [&] {
-      try {
-        copy_pool_ = std::make_unique<CopyPool>(copy_threads_);
-      } catch (const std::exception& e) {  // no threads to spare: copy alone
-        logf(LogLevel::Info, rank_, "single-copy helper threads unavailable (%s)", e.what());
-      }
-    });
-    if (!copy_pool_) shares = 1;
-  }
+  if (shares > 1 && copy_pool() == nullptr) shares = 1;
   if (shares <= 1) {
     copy_range(0, total);
   } else {

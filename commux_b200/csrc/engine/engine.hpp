@@ -235,6 +235,15 @@ class Engine {
   void post_job(int dst, std::unique_ptr<OutJob> job);
   // the TCP pump has sent the last record of request `id` (indirect records)
   void on_pump_sent(std::uint64_t id);
+
+ public:
+  // fn(lo, hi) over [0, n) in at most 1 + COMMUX_COPY_THREADS ranges of at
+  // least `grain`, on this thread and the copy helpers; returns when all are
+  // done. Serial when the helpers are off or unavailable.
+  void parallel_ranges(std::int64_t n, std::int64_t grain, const std::function<void(std::int64_t, std::int64_t)>& fn);
+
+ private:
+  CopyPool* copy_pool();  // created on first use; nullptr when unavailable
   void check_liveness();
   void fail_peer(int p, const std::string& why);
   void fail_all(const std::string& why);
