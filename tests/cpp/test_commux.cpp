@@ -1,7 +1,8 @@
 // Multi-rank C++ test driver for commux::ProcessGroupUCX (same coverage as
 // reference tests/test_commux.cpp: tag matching, collectives, vector p2p,
 // group window, multi-threaded posting, parked-waiter wakeups, a V-tensor
-// ping-pong benchmark), plus large rendezvous messages (T8). Ranks bootstrap through a c10d::TCPStore (rank 0
+// ping-pong benchmark), plus large rendezvous messages (T8) and a large
+// allreduce (T9). Ranks bootstrap through a c10d::TCPStore (rank 0
 // hosts it).
 //
 //   test_commux <rank> <world> [host] [port]
@@ -161,6 +162,18 @@ int main(int argc, char** argv) {
     s->wait();
     check(got[0].equal(torch::arange(n, f64).add_(1e7 * peer)),
           "large message: every byte of a 24 MiB rendezvous arrived");
+  }
+  pg->barrier()->wait();
+
+  // T9: a 4 MiB allreduce (its fold runs on the copy helpers), exact values
+  {
+    const std::int64_t n = 1 << 19;  // fp64
+    std::vector<at::Tensor> t{torch::arange(n, f64).remainder(97).add_(rank)};
+    pg->allreduce(t)->wait();
+    double ranks = 0;
+    for (int r = 0; r < world; ++r) ranks += r;
+    auto want = torch::arange(n, f64).remainder(97).mul_(static_cast<double>(world)).add_(ranks);
+    check(t[0].equal(want), "large allreduce (parallel fold) exact");
   }
   pg->barrier()->wait();
 
