@@ -571,6 +571,7 @@ std::vector<std::pair<std::string, std::int64_t>> ProcessGroupUCX::stats() const
       {"single_copy_msgs", s.single_copy_msgs.load()},
       {"faults_injected", s.faults_injected.load()},
   };
+  for (auto& kv : engine_->gauges()) v.push_back(kv);
   if (auto* d = engine_->device(false))
     for (auto& kv : d->stats()) v.push_back(kv);
   return v;

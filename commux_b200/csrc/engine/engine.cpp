@@ -768,6 +768,26 @@ void Engine::post_job(int dst, std::unique_ptr<OutJob> job) {
   flush_out(dst, false);
 }
 
+std::vector<std::pair<std::string, std::int64_t>> Engine::gauges() {
+  std::int64_t posted = 0, unexpected = 0, partial = 0, waiting = 0, pump = 0;
+  {
+    std::lock_guard<SpinMutex> lk(mu_);
+    for (auto& kv : posted_) posted += static_cast<std::int64_t>(kv.second.size());
+    for (auto& kv : unexpected_) unexpected += static_cast<std::int64_t>(kv.second.size());
+    for (auto& m : inflight_) partial += static_cast<std::int64_t>(m.size());
+    waiting = static_cast<std::int64_t>(sends_waiting_.size());
+  }
+  {
+    std::lock_guard<std::mutex> lk(pump_mu_);
+    pump = static_cast<std::int64_t>(pump_waiting_.size());
+  }
+  return {{"posted_now", posted},
+          {"unexpected_now", unexpected},
+          {"partial_now", partial},
+          {"sends_waiting_now", waiting},
+          {"pump_waiting_now", pump}};
+}
+
 CopyPool* Engine::copy_pool() {
   if (copy_threads_ <= 0) return nullptr;
   std::call_once(copy_pool_once_, [&] {

@@ -212,6 +212,11 @@ class Engine {
   void release_for_exit();
   static void release_all();
   const Stats& stats() const { return stats_; }
+  // current sizes of the engine's queues and tables (all zero when no
+  // message is in flight): posted receives, unexpected messages, messages
+  // partly received, sends waiting for their FIN, sends the TCP pump has
+  // still to send
+  std::vector<std::pair<std::string, std::int64_t>> gauges();
 
   // Internal fault injection hook (counts operations for kill:<rank>:<n>).
   void count_op();

@@ -23,6 +23,11 @@ def test_p2p_fuzz(world):
     check(run("fuzz_p2p.py", world, timeout=240))
 
 
+@pytest.mark.parametrize("world,transport", [(3, "shm"), (2, "tcp")])
+def test_no_engine_state_left_behind(world, transport):
+    check(run("resource_stability.py", world, env={"COMMUX_TRANSPORT": transport}, timeout=180))
+
+
 @pytest.mark.parametrize("transport", ["shm", "tcp"])
 def test_buffer_reuse_after_wait(transport):
     check(run("reuse_after_wait.py", 2, env={"COMMUX_TRANSPORT": transport}, timeout=180))
