@@ -1,7 +1,7 @@
 // IOContext: collective file primitives over a private commux group
 // (behaviour of reference: src/io.cpp:43-192). Error agreement is one
-// allreduce-MAX of the local errno, so every rank raises with the same first
-// failing errno; sizes and payloads travel on the collective tag namespace.
+// allreduce-MAX of the local errno, so every rank raises, all with the same
+// errno (the largest of those that failed); sizes and payloads travel on the collective tag namespace.
 
 #include "commux/io.hpp"
 
