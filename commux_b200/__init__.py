@@ -135,10 +135,12 @@ def batch_p2p(sends=(), recvs=(), group=None):
     messages to self) one copy launch on CUDA.
     """
     group = group if group is not None else dist.distributed_c10d._get_default_group()
-    first = (list(recvs) + list(sends))[0][0]
-    backend = group._get_backend(first.device)
     r = list(recvs)
     s = list(sends)
+    if not r and not s:
+        raise ValueError("commux.batch_p2p: no sends and no receives")
+    first = (r + s)[0][0]
+    backend = group._get_backend(first.device)
     return _C.batch_p2p(backend, [t for t, _, _ in r], [int(p) for _, p, _ in r], [int(g) for _, _, g in r],
                         [t for t, _, _ in s], [int(p) for _, p, _ in s], [int(g) for _, _, g in s])
 
@@ -148,17 +150,21 @@ def p2p_plan(sends=(), recvs=(), group=None):
 
     ``sends``/``recvs`` are ``(tensor, peer, tag)`` like :func:`batch_p2p`.
     ``plan.start()`` enqueues one exchange of the same buffers on the current
-    stream: a signal launch (data ready), one pull launch (copies, waiting on
-    the peers' ready flags on the device) and one wait launch (this rank's
-    data was consumed) -- no host matching and no host round trip per step.
+    stream as one CUDA graph: a pull launch that stores this rank's "ready"
+    signals, packs narrow rows for peers on other GPUs, and copies every
+    receive (waiting on the peers' ready flags on the device), then -- when
+    peers on other GPUs read this rank's data -- a wait launch for their
+    "consumed" flags. No host matching and no host round trip per step.
     Every rank the plan talks to creates its side in the same order and calls
     start() the same number of times (the analogue of MPI_Startall).
     """
     group = group if group is not None else dist.distributed_c10d._get_default_group()
-    first = (list(recvs) + list(sends))[0][0]
-    backend = group._get_backend(first.device)
     r = list(recvs)
     s = list(sends)
+    if not r and not s:
+        raise ValueError("commux.p2p_plan: no sends and no receives")
+    first = (r + s)[0][0]
+    backend = group._get_backend(first.device)
     return _C.p2p_plan(backend, [t for t, _, _ in r], [int(p) for _, p, _ in r], [int(g) for _, _, g in r],
                        [t for t, _, _ in s], [int(p) for _, p, _ in s], [int(g) for _, _, g in s])
 

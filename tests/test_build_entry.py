@@ -44,3 +44,20 @@ def test_halo_helper_under_both_names():
     r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300,
                        env=dict(os.environ, PYTHONPATH=ROOT))
     assert r.returncode == 0 and "halo ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+def test_empty_batches_are_rejected_clearly():
+    code = ("import commux_b200 as c, torch.distributed as dist, os\n"
+            "from commux_b200.utils import free_port\n"
+            "os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(free_port()))\n"
+            "c.register(); dist.init_process_group('ucx', rank=0, world_size=1)\n"
+            "for f in (c.batch_p2p, c.p2p_plan):\n"
+            "    try:\n"
+            "        f()\n"
+            "        raise SystemExit('accepted')\n"
+            "    except ValueError as e:\n"
+            "        assert 'no sends and no receives' in str(e)\n"
+            "dist.destroy_process_group(); print('empty ok')\n")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300,
+                       env=dict(os.environ, PYTHONPATH=ROOT))
+    assert r.returncode == 0 and "empty ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
