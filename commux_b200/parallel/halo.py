@@ -155,8 +155,8 @@ class HaloExchange:
                 self._plans.clear()
             persistent = None
             if u.is_cuda and self.use_plans and "tcp" not in commux_b200.transports(self.group):
-                # matched once; every later exchange of this field is three
-                # stream launches (collective: all ranks reach this together)
+                # matched once; every later exchange of this field replays
+                # one CUDA graph (collective: all ranks reach this together)
                 persistent = commux_b200.p2p_plan(sends=sends, recvs=recvs, group=self.group)
             plan = self._plans[key] = (sends, recvs, persistent)
         if plan[2] is not None:
