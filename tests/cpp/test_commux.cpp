@@ -1,8 +1,8 @@
 // Multi-rank C++ test driver for commux::ProcessGroupUCX (same coverage as
 // reference tests/test_commux.cpp: tag matching, collectives, vector p2p,
 // group window, multi-threaded posting, parked-waiter wakeups, a V-tensor
-// ping-pong benchmark), plus large rendezvous messages (T8) and a large
-// allreduce (T9). Ranks bootstrap through a c10d::TCPStore (rank 0
+// ping-pong benchmark), plus large rendezvous messages (T8), a large
+// allreduce (T9) and a seeded random exchange (T10). Ranks bootstrap through a c10d::TCPStore (rank 0
 // hosts it).
 //
 //   test_commux <rank> <world> [host] [port]
@@ -17,6 +17,7 @@
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
+#include <random>
 #include <string>
 #include <thread>
 #include <torch/csrc/distributed/c10d/TCPStore.hpp>
@@ -174,6 +175,40 @@ int main(int argc, char** argv) {
     for (int r = 0; r < world; ++r) ranks += r;
     auto want = torch::arange(n, f64).remainder(97).mul_(static_cast<double>(world)).add_(ranks);
     check(t[0].equal(want), "large allreduce (parallel fold) exact");
+  }
+  pg->barrier()->wait();
+
+  // T10: a seeded random exchange between ranks 0 and 1: 48 messages each
+  // way, from empty through eager to rendezvous sizes, on 4 tags (so many
+  // messages share a (source, tag) pair and must match in posting order),
+  // all posted before any wait
+  if (world >= 2 && rank <= 1) {
+    const int peer = 1 - rank;
+    const std::int64_t sizes[] = {0, 1, 7, 1000, 8192, 8193, 70000, 131072};  // fp64 elements
+    std::mt19937 rng(20261202);
+    struct Msg {
+      std::int64_t n;
+      int tag;
+    };
+    std::vector<Msg> msgs;
+    for (int i = 0; i < 48; ++i) msgs.push_back({sizes[rng() % 8], static_cast<int>(rng() % 4)});
+    auto payload = [&](int from, int i) {
+      return torch::arange(msgs[i].n, f64).remainder(1009).add_(1e4 * from + i);
+    };
+    std::vector<c10::intrusive_ptr<c10d::Work>> works;
+    std::vector<std::vector<at::Tensor>> got(msgs.size()), mine(msgs.size());
+    for (std::size_t i = 0; i < msgs.size(); ++i) {
+      got[i] = {torch::full({msgs[i].n}, -1.0, f64)};
+      works.push_back(pg->recv(got[i], peer, 700 + msgs[i].tag));
+    }
+    for (std::size_t i = 0; i < msgs.size(); ++i) {
+      mine[i] = {payload(rank, static_cast<int>(i))};
+      works.push_back(pg->send(mine[i], peer, 700 + msgs[i].tag));
+    }
+    for (auto& w : works) w->wait();
+    bool ok = true;
+    for (std::size_t i = 0; i < msgs.size(); ++i) ok = ok && got[i][0].equal(payload(peer, static_cast<int>(i)));
+    check(ok, "random exchange: 48 messages each way intact and in order");
   }
   pg->barrier()->wait();
 
