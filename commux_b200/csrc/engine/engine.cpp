@@ -1003,7 +1003,6 @@ bool Engine::flush_out(int dst, bool blocking_lock) {
   lk.unlock();
   for (auto& j : finished) {
     if (j->complete_req_when_done && j->req && !j->completes_when_sent) complete(j->req);
-    if (j->on_done) j->on_done();
   }
   return wrote;
 }

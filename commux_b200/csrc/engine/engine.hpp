@@ -112,7 +112,6 @@ struct OutJob {
   bool head_sent = false;
   bool complete_req_when_done = false;
   bool completes_when_sent = false;  // TCP pump completes req (indirect records)
-  std::function<void()> on_done;  // optional callback after the last record
 };
 
 // A mutex for short critical sections shared by a posting thread and the
