@@ -1,7 +1,6 @@
 """Vector p2p (COMMUX_COALESCE on/off), the group window (COMMUX_GROUP), the
 batch_isend_irecv aggregate Work, any-source receive with sourceRank, and
 strided receive views (reference: tests/test_commux.cpp:151-200)."""
-import os
 
 from common import Checker, init, torch, dist
 

@@ -3,7 +3,7 @@ single-process gradient of the concatenated batch (the reference backend
 cannot run DDP: no allgather, no Work::getFuture)."""
 import torch.nn as nn
 
-from common import Checker, init, torch, dist
+from common import Checker, init, torch
 
 rank, world, dev = init()
 c = Checker(rank)

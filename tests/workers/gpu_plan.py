@@ -3,7 +3,7 @@
 Every rank sends three tensors (contiguous, strided view, transposed) to
 (rank+1) % world and receives from (rank-1) % world; after each start() the
 receive buffers must hold the sender's data of that step."""
-from common import Checker, init, torch, dist
+from common import Checker, init, torch
 import commux_b200 as commux
 
 rank, world, dev = init(timeout_s=90)

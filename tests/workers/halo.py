@@ -4,7 +4,7 @@ fp32 with halo 2 (8-byte rows: the narrow rows and the wide ones fall in
 different copy classes), int16 with halo 3 (6-byte rows). Each field is
 exchanged twice (a persistent plan is matched once, then started again)."""
 
-from common import Checker, init, torch, dist
+from common import Checker, init, torch
 from commux_b200.parallel.halo import CartGrid, HaloExchange, factor3, reference_exchange
 
 rank, world, dev = init()
