@@ -21,6 +21,6 @@ if rc != 0:
     print(f"FAIL ({rc}): {msg}", flush=True)
     sys.exit(1)
 # the process can still run CUDA work
-x = torch.arange(1 << 20, device="cuda", dtype=torch.float32)
-assert float(x.sum()) == float((1 << 20) * ((1 << 20) - 1) / 2)
+x = torch.ones(1 << 20, device="cuda", dtype=torch.float32)  # every partial sum exact in fp32
+assert float(x.sum()) == float(1 << 20)
 print("PASS device waits give up, report and leave the context usable", flush=True)
