@@ -25,12 +25,12 @@
 // Kernels:
 //   oneshot  (small allreduce/reduce): push my data into slot[me] of every
 //            rank's A, one flag round, fold the P slots locally.
-//   twoshot  (large allreduce/reduce/reduce_scatter), pipelined over chunks
-//            by two warp groups: push segment s of the chunk into slot[me]
-//            of rank s's A (reduce-scatter by writes), flag round, rank s
-//            folds its segment (its own part read from its input) and pushes
-//            it into slot[s] of B on every rank that needs it, flag round,
-//            copy out; chunk c+1 crosses NVLink while chunk c is folded.
+//   twoshot  (large allreduce/reduce/reduce_scatter), chunk by chunk, the
+//            phases of a chunk in sequence within each CTA: push segment s of
+//            the chunk into slot[me] of rank s's A (reduce-scatter by
+//            writes), flag round, rank s folds its segment (its own part read
+//            from its input) and pushes it into slot[s] of B on every rank
+//            that needs it, flag round, copy out.
 //   gather   (allgather/broadcast), chunked: push my block into slot[me] of
 //            every rank's B (broadcast: the root's block into slot 0), flag
 //            round, copy out, flag round.

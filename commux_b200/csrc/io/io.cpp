@@ -10,6 +10,7 @@
 #include <sys/types.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <cerrno>
 #include <cstring>
 #include <stdexcept>
@@ -22,7 +23,6 @@ namespace commux {
 
 namespace {
 
-constexpr int kSizeTag = 0x10;
 constexpr int kDataTag = 0x11;
 
 at::Tensor bytes_view(void* data, std::size_t n) {
@@ -82,18 +82,35 @@ void IOContext::close_file(int fd) {
   agree(err, "close_file");
 }
 
+// Positional write of the whole buffer, local to this rank. Linux moves at
+// most 0x7ffff000 bytes per write call, so the buffer goes out in pieces of
+// at most kWritePiece bytes; a piece that was cut short resumes where the
+// kernel stopped. A failure reports how far the write got, so a caller can
+// tell a full disk (partial progress) from a bad descriptor (none).
 void IOContext::write_at(int fd, const void* data, std::size_t nbytes, std::int64_t offset) {
-  if (offset < 0) throw std::invalid_argument("commux::IOContext write_at: negative offset");
-  const char* p = static_cast<const char*>(data);
-  std::size_t done = 0;
-  while (done < nbytes) {
-    ssize_t n = ::pwrite(fd, p + done, nbytes - done, static_cast<off_t>(offset + static_cast<std::int64_t>(done)));
-    if (n < 0) {
-      if (errno == EINTR) continue;
-      throw std::runtime_error(std::string("commux::IOContext write_at failed: ") + std::strerror(errno));
+  constexpr std::size_t kWritePiece = std::size_t(1) << 30;
+  if (offset < 0)
+    throw std::invalid_argument("commux::IOContext::write_at: offset " + std::to_string(offset) +
+                                " is negative");
+  const auto* base = static_cast<const unsigned char*>(data);
+  std::size_t written = 0;
+  int stalls = 0;  // consecutive zero-byte writes
+  while (written < nbytes) {
+    const std::size_t piece = std::min(nbytes - written, kWritePiece);
+    const off_t at = static_cast<off_t>(offset) + static_cast<off_t>(written);
+    const ssize_t got = ::pwrite(fd, base + written, piece, at);
+    if (got > 0) {
+      written += static_cast<std::size_t>(got);
+      stalls = 0;
+      continue;
     }
-    if (n == 0) throw std::runtime_error("commux::IOContext write_at made no progress");
-    done += static_cast<std::size_t>(n);
+    const int err = got < 0 ? errno : 0;
+    if (err == EINTR || err == EAGAIN) continue;
+    if (got == 0 && ++stalls < 3) continue;
+    throw std::runtime_error("commux::IOContext::write_at(fd " + std::to_string(fd) + ", offset " +
+                             std::to_string(offset) + "): " + std::to_string(written) + " of " +
+                             std::to_string(nbytes) + " bytes written; " +
+                             (err != 0 ? std::strerror(err) : "the file accepts no more bytes"));
   }
 }
 
@@ -119,30 +136,39 @@ void IOContext::broadcast_bytes(std::vector<std::uint8_t>& bytes, int root) {
   }
 }
 
+// Every rank learns every payload size from one allgather; the root then
+// sizes the result once and receives each peer's payload straight into its
+// place (offset = sum of the sizes of the lower ranks), all receives in
+// flight together. No size messages, no per-peer temporaries, no padding.
 std::vector<std::uint8_t> IOContext::gather_bytes(const std::vector<std::uint8_t>& bytes, int root) {
   if (root < 0 || root >= size_) throw std::invalid_argument("commux::IOContext gather: root out of range");
+  at::Tensor mine = at::full({1}, static_cast<std::int64_t>(bytes.size()), at::TensorOptions().dtype(at::kLong));
+  at::Tensor all = at::empty({size_}, at::TensorOptions().dtype(at::kLong));
+  pg_->_allgather_base(all, mine)->wait();
+  const std::int64_t* sizes = all.data_ptr<std::int64_t>();
+  std::vector<std::size_t> offset(static_cast<std::size_t>(size_) + 1, 0);
+  for (int r = 0; r < size_; ++r) {
+    if (sizes[r] < 0) throw std::runtime_error("commux::IOContext gather: rank " + std::to_string(r) +
+                                               " reported a negative size");
+    offset[r + 1] = offset[r] + static_cast<std::size_t>(sizes[r]);
+  }
   std::vector<std::uint8_t> out;
   if (rank_ == root) {
-    std::vector<std::vector<std::uint8_t>> parts(size_);
-    parts[root] = bytes;
+    out.resize(offset[size_]);
+    if (!bytes.empty()) std::memcpy(out.data() + offset[root], bytes.data(), bytes.size());
+    std::vector<c10::intrusive_ptr<c10d::Work>> pending;
     for (int r = 0; r < size_; ++r) {
-      if (r == root) continue;
-      std::int64_t n = 0;
-      recv_bytes(&n, sizeof(n), r, kSizeTag);
-      if (n < 0) throw std::runtime_error("commux::IOContext gather: negative size");
-      parts[r].resize(static_cast<std::size_t>(n));
-      recv_bytes(parts[r].data(), parts[r].size(), r, kDataTag);
+      if (r == root || sizes[r] == 0) continue;
+      std::vector<at::Tensor> v{bytes_view(out.data() + offset[r], static_cast<std::size_t>(sizes[r]))};
+      pending.push_back(pg_->recv(v, r, kDataTag));
     }
-    std::size_t total = 0;
-    for (auto& p : parts) total += p.size();
-    out.reserve(total);
-    for (auto& p : parts) out.insert(out.end(), p.begin(), p.end());
-  } else {
-    std::int64_t n = static_cast<std::int64_t>(bytes.size());
-    send_bytes(&n, sizeof(n), root, kSizeTag);
-    send_bytes(bytes.data(), bytes.size(), root, kDataTag);
+    for (auto& w : pending) w->wait();
+  } else if (!bytes.empty()) {
+    // the send completes once the root holds the bytes, so `bytes` is
+    // borrowed in place, not copied
+    std::vector<at::Tensor> v{bytes_view(const_cast<std::uint8_t*>(bytes.data()), bytes.size())};
+    pg_->send(v, root, kDataTag)->wait();
   }
-  barrier();
   return out;
 }
 

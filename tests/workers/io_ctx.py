@@ -24,6 +24,25 @@ if got != b"hello":
 g = io.gather_bytes(bytes([rank]) * (rank + 1), 0)
 if rank == 0 and g != b"".join(bytes([r]) * (r + 1) for r in range(world)):
     fail.append(f"gather_bytes {g!r}")
+# an empty payload, a large one, and a root other than 0
+g2 = io.gather_bytes(b"" if rank == 0 else bytes([rank]) * (70000 * rank), world - 1)
+want2 = b"".join(b"" if r == 0 else bytes([r]) * (70000 * r) for r in range(world))
+if rank == world - 1 and g2 != want2:
+    fail.append(f"gather_bytes (root {world - 1}) {len(g2)} bytes, want {len(want2)}")
+if rank != world - 1 and g2 != b"":
+    fail.append("gather_bytes returned data on a non-root rank")
+try:
+    fd2 = os.open(path, os.O_RDONLY)
+    try:
+        io.write_at(fd2, b"x", 0)  # read-only descriptor: the write must fail with progress
+        fail.append("write_at on a read-only descriptor did not raise")
+    except RuntimeError as e:
+        if "0 of 1 bytes written" not in str(e):
+            fail.append(f"write_at error text: {e}")
+    finally:
+        os.close(fd2)
+except OSError as e:
+    fail.append(f"reopen: {e}")
 try:
     io.open_file("/nonexistent/dir/x" if rank == world - 1 else path, os.O_RDONLY, 0)
     fail.append("open_file error was not agreed")
