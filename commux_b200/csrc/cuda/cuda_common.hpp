@@ -126,6 +126,8 @@ cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStrea
 // 2, 1 byte units; 0 = wide strides).
 inline int pull_unit_class(const PullDesc& d) { return d.wide ? 0 : static_cast<int>(d.unit); }
 cudaError_t launch_wait(const WaitBatch& b, cudaStream_t s);
+// Loads every pull-kernel build into the current context (see p2p_kernels.cu).
+cudaError_t preload_pull_kernels();
 
 }  // namespace cuda
 }  // namespace commux

@@ -425,6 +425,18 @@ cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStrea
   return cudaSuccess;
 }
 
+// Loads every build of the pull kernel into the current context now, instead
+// of at its first launch (CUDA's default lazy loading; a load may allocate
+// device memory).
+cudaError_t preload_pull_kernels() {
+  cudaFuncAttributes a;
+  for (cudaError_t e : {cudaFuncGetAttributes(&a, pull_kernel<16>), cudaFuncGetAttributes(&a, pull_kernel<8>),
+                        cudaFuncGetAttributes(&a, pull_kernel<4>), cudaFuncGetAttributes(&a, pull_kernel<2>),
+                        cudaFuncGetAttributes(&a, pull_kernel<1>), cudaFuncGetAttributes(&a, pull_kernel<0>)})
+    if (e != cudaSuccess) return e;
+  return cudaSuccess;
+}
+
 cudaError_t launch_wait(const WaitBatch& b, cudaStream_t s) {
   if (b.bump != nullptr) {
     wait_bump_kernel<<<1, kMaxWaitFlags, 0, s>>>(b);

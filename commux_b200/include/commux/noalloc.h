@@ -33,8 +33,8 @@
  *     device, and must not overlap; the call checks the first, not the second;
  *   - asynchronous on `stream` (a cudaStream_t, NULL = the legacy default
  *     stream), which must belong to the current device;
- *   - before its kernel, each call clears the counters and flags on `stream`
- *     with a cudaMemsetAsync (they must start at zero).
+ *   - before its copy kernel, each call clears the counters and flags on
+ *     `stream` with a small kernel of its own (they must start at zero).
  *
  * Limits (oversize inputs are rejected with CMX_NOALLOC_ETOOBIG and a message,
  * before any memory is touched):
@@ -52,8 +52,19 @@
  * issue them on one stream or order them with events.
  *
  * Set-up: the first call on each device looks up the scratch array's device
- * address (cudaGetSymbolAddress, which may load the library's device code)
- * and caches it. Make that first call before any stream capture begins.
+ * address (cudaGetSymbolAddress) and loads every kernel a later call can
+ * launch (by default CUDA loads a kernel lazily at its first launch, and a
+ * load may allocate device memory). That first call may therefore allocate;
+ * no later call does. Make the first call on each device before any stream
+ * capture begins, and outside the code that must not allocate.
+ *
+ * Context: the call runs in the device's primary context, the one the CUDA
+ * runtime uses; it does not change the calling thread's current device or
+ * context. A thread that made another driver context current gets
+ * CMX_NOALLOC_EINVAL until it makes the primary context current again. The
+ * cached set-up belongs to the primary context: after a cudaDeviceReset the
+ * next call repeats the set-up when the new primary context has a new handle,
+ * but a handle can be reused, so do not mix this call with cudaDeviceReset.
  *
  * Returns CMX_NOALLOC_OK (0) or an error code; on error a NUL-terminated
  * message is written to `err` (at most `err_len` bytes, may be NULL).
@@ -70,7 +81,8 @@ extern "C" {
 
 enum {
   CMX_NOALLOC_OK = 0,
-  CMX_NOALLOC_EINVAL = 1,   /* bad argument (pointer, ndim, elem_bytes, alignment) */
+  CMX_NOALLOC_EINVAL = 1,   /* bad argument (pointer, ndim, elem_bytes, alignment), or a
+                               context other than the device's primary one is current */
   CMX_NOALLOC_ETOOBIG = 2,  /* more descriptors or units than the static scratch covers */
   CMX_NOALLOC_ELAYOUT = 3,  /* more than 4 dims after merging */
   CMX_NOALLOC_ERANGE = 4,   /* a view leaves its allocation or is not on the current device */

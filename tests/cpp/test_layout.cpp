@@ -12,6 +12,12 @@
 //     of the two views, each pair exactly once; check_desc() must accept them.
 //  3. A layout of more than 2^30 units is split into several descriptors whose
 //     unit counts and start offsets tile it.
+//  4. The allocation-free entry point's planner (noalloc_plan.hpp) on random
+//     views, negative strides and 16-byte elements included, with small caps
+//     on the units per descriptor so that copies split into many descriptors:
+//     the walked descriptors must cover each element pair exactly once, and
+//     a copy needing more descriptors than the static scratch holds must be
+//     rejected.
 //
 //   test_layout [iterations]    exit code 0 when every check passes
 
@@ -25,6 +31,7 @@
 #include <vector>
 
 #include "layout.hpp"
+#include "noalloc_plan.hpp"
 
 using commux::cuda::Dim;
 using commux::cuda::FastDiv;
@@ -257,6 +264,72 @@ void check_split() {
   if (descs.size() < 2) fail("a layout above 2^30 units was not split");
 }
 
+void check_noalloc_plan(std::mt19937_64& rng, int iters) {
+  namespace na = commux::cuda::noalloc;
+  const std::int64_t elems[] = {1, 2, 4, 8, 16};
+  static PullDesc descs[na::kDescs];
+  for (int it = 0; it < iters; ++it) {
+    const int nd = 1 + static_cast<int>(rng() % 5);
+    std::vector<std::int64_t> shape(nd);
+    for (auto& x : shape) x = 1 + static_cast<std::int64_t>(rng() % 7);
+    View a = random_view(shape, rng), b = random_view(shape, rng);
+    // negative strides: walk some dims backwards (the pointer moves to the
+    // dim's last element)
+    for (View* v : {&a, &b})
+      for (int k = 0; k < nd; ++k)
+        if (rng() % 4 == 0) {
+          v->offset += (shape[k] - 1) * v->strides[k];
+          v->strides[k] = -v->strides[k];
+        }
+    const std::int64_t elem = elems[rng() % 5];
+    const std::int64_t sbase = 1 << 16, dbase = 1 << 24;
+    char* sp = reinterpret_cast<char*>(sbase + a.offset * elem);
+    char* dp = reinterpret_cast<char*>(dbase + b.offset * elem);
+    const std::int64_t cap = 1 + static_cast<std::int64_t>(rng() % 40);
+    na::Plan plan;
+    char err[256];
+    const int rc = na::plan_copy(dp, b.strides.data(), sp, a.strides.data(), shape.data(), nd,
+                                 static_cast<int>(elem), nullptr, descs, plan, err, sizeof(err), cap);
+    if (rc == CMX_NOALLOC_ELAYOUT || rc == CMX_NOALLOC_ETOOBIG) continue;  // rejected before launch
+    if (rc != CMX_NOALLOC_OK) {
+      fail(err);
+      continue;
+    }
+    std::vector<std::pair<std::int64_t, std::int64_t>> got;
+    for (std::uint32_t i = 0; i < plan.ndesc; ++i) {
+      const PullDesc& d = descs[i];
+      if (d.units > static_cast<std::uint64_t>(cap)) fail("noalloc: a descriptor exceeds the unit cap");
+      if (d.counter_idx != i) fail("noalloc: counter slots are not one per descriptor");
+      std::vector<std::pair<std::int64_t, std::int64_t>> units;
+      walk(d, units);
+      const std::int64_t s0 = reinterpret_cast<std::int64_t>(d.src) - sbase;
+      const std::int64_t d0 = reinterpret_cast<std::int64_t>(d.dst) - dbase;
+      for (auto& u : units)
+        for (std::int64_t k = 0; k < d.unit; k += elem) {
+          const std::int64_t sb = s0 + u.first + k, db2 = d0 + u.second + k;
+          if (sb % elem || db2 % elem) fail("noalloc: a unit splits an element");
+          got.push_back({sb / elem, db2 / elem});
+        }
+    }
+    auto want = brute_pairs(a, b);
+    std::sort(want.begin(), want.end());
+    std::sort(got.begin(), got.end());
+    if (got != want) {
+      char buf[160];
+      std::snprintf(buf, sizeof(buf), "noalloc iteration %d: %zu pairs walked, %zu expected (nd %d, elem %lld, cap %lld)",
+                    it, got.size(), want.size(), nd, static_cast<long long>(elem), static_cast<long long>(cap));
+      fail(buf);
+    }
+  }
+  // more descriptors than the scratch has counters: rejected
+  std::int64_t sizes[2] = {na::kDescs + 1, 4}, ss[2] = {8, 1}, ds[2] = {4, 1};
+  na::Plan plan;
+  char err[256];
+  const int rc = na::plan_copy(reinterpret_cast<void*>(1 << 20), ds, reinterpret_cast<void*>(1 << 16), ss, sizes, 2,
+                               4, nullptr, descs, plan, err, sizeof(err), 1);
+  if (rc != CMX_NOALLOC_ETOOBIG) fail("noalloc: a copy needing 65 descriptors was not rejected");
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -265,6 +338,7 @@ int main(int argc, char** argv) {
   check_fastdiv(rng);
   check_layouts(rng, iters);
   check_split();
+  check_noalloc_plan(rng, iters);
   if (g_fail == 0) std::printf("ALL LAYOUT CHECKS PASSED\n");
   else std::printf("%d failure(s)\n", g_fail);
   return g_fail == 0 ? 0 : 1;

@@ -23,6 +23,7 @@ def test_descriptor_walks_match_brute_force():
         exe = os.path.join(d, "test_layout")
         r = subprocess.run([cxx, "-std=c++17", "-O2", "-Wall", "-Wno-unused-function",
                             "-I", os.path.join(ROOT, "commux_b200", "csrc", "cuda"), "-I", CUDA_INC,
+                            "-I", os.path.join(ROOT, "commux_b200", "include"),
                             os.path.join(ROOT, "tests", "cpp", "test_layout.cpp"), "-o", exe],
                            capture_output=True, text=True, timeout=600)
         assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
@@ -41,6 +42,7 @@ def test_descriptor_code_has_no_undefined_behaviour():
         r = subprocess.run([cxx, "-std=c++17", "-O1", "-g", "-fsanitize=address,undefined",
                             "-fno-sanitize-recover=undefined",
                             "-I", os.path.join(ROOT, "commux_b200", "csrc", "cuda"), "-I", CUDA_INC,
+                            "-I", os.path.join(ROOT, "commux_b200", "include"),
                             os.path.join(ROOT, "tests", "cpp", "test_layout.cpp"), "-o", exe],
                            capture_output=True, text=True, timeout=600)
         if r.returncode != 0 and "sanitize" in (r.stdout + r.stderr):

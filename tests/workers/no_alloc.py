@@ -1,8 +1,11 @@
 """commux_strided_copy_noalloc, called through ctypes, against the existing
 entry point that runs the same pull kernel (a CUDA self send/recv through the
 backend) and against a torch copy, on calls made back to back on one stream.
-Also checks that the calls leave the device memory in use unchanged and that
-oversize, unsupported and out-of-range inputs are rejected before launch."""
+Also checks that the calls leave the device memory in use unchanged -- first
+in this fresh process, where the set-up call loads the kernels and every
+later call's kernel build (16/8/4/2/1-byte units and the 64-bit-stride walk)
+is launched for the first time -- and that oversize, unsupported and
+out-of-range inputs are rejected before launch."""
 import ctypes
 import os
 import zlib
@@ -44,6 +47,65 @@ def data(shape, dtype, salt):
         return torch.randn(shape, generator=g).to(dtype)
     return torch.randint(-100, 100, shape, generator=g).to(dtype)
 
+
+def free_bytes():
+    torch.cuda.synchronize()
+    return torch.cuda.mem_get_info()[0], torch.cuda.memory_reserved()
+
+
+# -- fresh process: no pull kernel has run yet. Buffers first (torch's own
+# kernels load here), then the set-up call, then the first call of every
+# other kernel build, with the free device memory compared around them.
+f32 = data((64, 1024), torch.float32, "fresh").to(dev)
+f32_out = torch.zeros_like(f32)
+firsts = []  # (name, dst view, src view, elem bytes or None for dst.element_size())
+for name, dtype, step in (("8-byte units", torch.float64, 2), ("4-byte units", torch.float32, 2),
+                          ("2-byte units", torch.float16, 2), ("1-byte units", torch.uint8, 2)):
+    src_t = data((4096,), dtype, name).to(dev)
+    firsts.append((name, torch.zeros(2048, dtype=dtype, device=dev), src_t[::step]))
+# strides of 2^31 bytes and more (the 64-bit walk): two rows 2 GiB + 64 B apart
+wide_pitch = (1 << 28) + 8
+wide_src = torch.zeros(wide_pitch + 64, dtype=torch.float64, device=dev)
+wide_src[:64] = torch.arange(64, dtype=torch.float64, device=dev)
+wide_src[wide_pitch:wide_pitch + 64] = -torch.arange(64, dtype=torch.float64, device=dev)
+wide_out = torch.zeros(2, 64, dtype=torch.float64, device=dev)
+torch.cuda.synchronize()
+rc, msg = noalloc(f32_out, f32)  # the set-up call
+c.check("set-up call rc", rc == 0, msg)
+before = free_bytes()
+for name, out, sv in firsts:
+    rc, msg = noalloc(out, sv)
+    c.check(f"first call, {name}: rc", rc == 0, msg)
+rc, msg = raw(wide_out.data_ptr(), [64, 1], wide_src.data_ptr(), [wide_pitch, 1], [2, 64], 8)
+c.check("first call, 2 GiB stride: rc", rc == 0, msg)
+after = free_bytes()
+c.check("first calls of every kernel build allocate nothing", before == after, f"before {before} after {after}")
+c.equal("set-up call copy", f32_out.cpu(), f32.cpu())
+for name, out, sv in firsts:
+    c.equal(f"first call, {name}", out.cpu(), sv.cpu())
+c.equal("2 GiB stride copy", wide_out.cpu(),
+        torch.stack([torch.arange(64, dtype=torch.float64), -torch.arange(64, dtype=torch.float64)]))
+del wide_src
+torch.cuda.empty_cache()
+
+# negative strides (the raw C API allows them): a reversed copy, pointer at
+# the last element
+rev = data((1000,), torch.float32, "rev").to(dev)
+rev_out = torch.zeros_like(rev)
+rc, msg = raw(rev_out.data_ptr(), [1], rev.data_ptr() + 999 * 4, [-1], [1000], 4)
+c.check("reversed rc", rc == 0, msg)
+c.equal("reversed copy", rev_out.cpu(), rev.cpu().flip(0))
+rev2 = data((30, 40), torch.float64, "rev2").to(dev)
+rev2_out = torch.zeros(30, 20, dtype=torch.float64, device=dev)
+rc, msg = raw(rev2_out.data_ptr(), [20, 1], rev2.data_ptr() + (29 * 40 + 1) * 8, [-40, 2], [30, 20], 8)
+c.check("reversed rows rc", rc == 0, msg)
+c.equal("reversed rows copy", rev2_out.cpu(), rev2.cpu().flip(0)[:, 1::2])
+# 16-byte elements: every other 16-byte pair of a float64 buffer
+e16 = data((512,), torch.float64, "e16").to(dev)
+e16_out = torch.zeros(256, dtype=torch.float64, device=dev)
+rc, msg = raw(e16_out.data_ptr(), [1], e16.data_ptr(), [2], [128], 16)
+c.check("16-byte elements rc", rc == 0, msg)
+c.equal("16-byte elements", e16_out.cpu(), e16.cpu().view(128, 4)[:, :2].reshape(-1))
 
 # (name, full shape, dtype, source view, destination view of a same-shaped buffer)
 cases = [
