@@ -33,7 +33,9 @@ import time
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 
-METRIC = "tagged halo-exchange GB/s (26-direction, 1024^3 fp64, halo 2, 7-point Jacobi)"
+# every N runs 512^3 fp64 per GPU (weak scaling); the global size, which is
+# 512^3 times the process grid (1024^3 at 8 GPUs), is in config.model
+METRIC = "tagged halo-exchange GB/s (26-direction, halo 2, fp64, 512^3 per GPU, 7-point Jacobi)"
 BASELINE_VALUE = None  # the reference publishes no halo-exchange GB/s number
 
 
@@ -151,6 +153,15 @@ def main() -> None:
     dist.barrier()
     launches = cuda_launches() - launches0
     clocks = sampler.stop()
+    # which transport path the timed exchanges took, summed over ranks, and
+    # how many distinct GPUs the ranks drove
+    st = commux.stats(device="cpu")
+    path_keys = ("cuda_plan_device_msgs", "cuda_plan_shared_msgs", "cuda_plan_starts", "cuda_pulls_peer_gpu")
+    path_sums = rank_sum([float(st.get(k, 0)) for k in path_keys])
+    uuids = [None] * world
+    dist.all_gather_object(uuids, uuid or f"rank{rank}")
+    paths = {k: int(v) for k, v in zip(path_keys, path_sums)}
+    paths["gpus_active"] = len(set(uuids))
 
     # diagnostic: the same exchange back to back, no stencil in between (the
     # in-step exchange also absorbs the ranks' skew after each update)
@@ -233,6 +244,8 @@ def main() -> None:
                 "seq_len": 0,
                 "parallelism": f"domain decomposition {dims[0]}x{dims[1]}x{dims[2]} (periodic)",
                 "halo_bytes_per_step_per_rank": bytes_rank,
+                "nvlink_bytes_per_step_per_rank_max": remote_rank,
+                "paths": paths,
                 "exchange_only_us_p50": round(statistics.median(xonly) * 1e3, 2),
                 "halo_bytes_per_step_job": bytes_job,
                 "exchange_us_p50": round(exch_p50_us, 2),

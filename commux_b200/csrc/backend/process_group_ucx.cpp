@@ -912,9 +912,32 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::broadcast(std::vector<at::Tensor
   return completed_work(engine_.get(), c10d::OpType::BROADCAST, tensors);
 }
 
-c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::barrier(const c10d::BarrierOptions& /*opts*/) {
+// The reference's barrier is a token reduce + broadcast over its transport
+// (reference: src/process_group_ucx.cpp:813-823). Here: a group whose device
+// collectives are set up (or a call naming device_ids) runs a device flag
+// round on the current stream, ordered after the work already on it, and
+// the call returns once every rank's stream reached it -- so what any
+// rank's kernels wrote before the barrier is visible to every rank's kernels
+// after it. Other groups use the host barrier over shared memory.
+c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::barrier(const c10d::BarrierOptions& opts) {
   TraceRange trace_("commux.barrier");
-  if (getSize() > 1) coll_->barrier();
+  if (getSize() == 1) return completed_work(engine_.get(), c10d::OpType::BARRIER, {});
+  DeviceTransport* dev = engine_->any_remote() ? nullptr : engine_->device(false);
+  bool on_device = dev != nullptr && dev->collectives_ready();
+  if (!on_device && !opts.device_ids.empty() && !engine_->any_remote()) {
+    at::Tensor probe = at::empty({0}, at::TensorOptions().device(at::kCUDA, static_cast<c10::DeviceIndex>(opts.device_ids[0])));
+    on_device = device_coll(probe);
+    dev = engine_->device(false);
+  }
+  if (!on_device) {
+    coll_->barrier();
+    return completed_work(engine_.get(), c10d::OpType::BARRIER, {});
+  }
+  DevCollPtr r = dev->barrier();
+  r->stream_wait();
+  r->host_wait();
+  std::string e = r->error();
+  if (!e.empty()) C10_THROW_ERROR(DistBackendError, "commux barrier: " + e);
   return completed_work(engine_.get(), c10d::OpType::BARRIER, {});
 }
 

@@ -135,8 +135,16 @@ CollImpl::CollImpl(CudaTransport* tr, int dev)
     auto v = eng_->store().get(key + std::to_string(p));
     TORCH_CHECK(v.size() == sizeof(ExchangeRecord), "commux: malformed workspace record");
     std::memcpy(&recs[p], v.data(), sizeof(ExchangeRecord));
-    if (std::memcmp(recs[p].uuid, ctx_->uuid, 16) == 0) shared_gpu_ = true;
   }
+  // any two ranks of the group on one GPU: every rank decides alike (a
+  // rank alone on its GPU must not take the device path while the others
+  // stage through the host)
+  for (int p = 0; p < P_ && !shared_gpu_; ++p)
+    for (int q = p + 1; q < P_; ++q)
+      if (std::memcmp(recs[p].uuid, recs[q].uuid, 16) == 0) {
+        shared_gpu_ = true;
+        break;
+      }
   if (shared_gpu_) {  // kernels of two processes on one GPU must not wait on each other
     logf(LogLevel::Info, me_, "device collectives: ranks share a GPU, collectives are staged through the host");
     return;
@@ -380,10 +388,35 @@ DevCollPtr CollImpl::reduce_scatter(at::Tensor& out, const at::Tensor& in, RedOp
   return run(ls);
 }
 
+DevCollPtr CollImpl::barrier() {
+  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev_));
+  cudaStream_t cur = current_stream(dev_);
+  auto ready = ctx_->event();
+  CMX_CUDA(cudaEventRecord(ready->ev, cur));
+  CMX_CUDA(cudaStreamWaitEvent(stream_, ready->ev, 0));
+  CollArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.P = P_;
+  a.me = me_;
+  a.mode = kModeBarrier;
+  for (int p = 0; p < P_; ++p) a.flags[p] = flags_[p];
+  ++epoch_;
+  a.seq_base = epoch_ << 20;
+  a.timeout_ns = tr_->device_timeout_ns();
+  a.status = ctx_->status_d;
+  CMX_CUDA(launch_barrier(a, stream_));
+  tr_->kernel_launches++;
+  st_barriers_++;
+  auto done = ctx_->event();
+  CMX_CUDA(cudaEventRecord(done->ev, stream_));
+  return std::make_shared<CollResult>(tr_, dev_, stream_, done);
+}
+
 std::vector<std::pair<std::string, std::int64_t>> CollImpl::stats() const {
   return {{"coll_calls", st_calls_},   {"coll_oneshot", st_oneshot_}, {"coll_twoshot", st_twoshot_},
           {"coll_gather", st_gather_}, {"coll_bytes", st_bytes_},     {"coll_shared_gpu", shared_gpu_ ? 1 : 0},
-          {"coll_nvls", st_nvls_},     {"coll_nvls_enabled", nvls_ ? 1 : 0}};
+          {"coll_nvls", st_nvls_},     {"coll_nvls_enabled", nvls_ ? 1 : 0},
+          {"coll_barriers", st_barriers_}};
 }
 
 // ---------------------------------------------------------------------------
@@ -418,8 +451,11 @@ DevCollPtr CudaTransport::reduce_scatter(at::Tensor& out, const at::Tensor& in, 
   return coll_->reduce_scatter(out, in, op);
 }
 DevCollPtr CudaTransport::barrier() {
-  throw std::runtime_error("commux: the device barrier is not used (barrier runs on the host)");
+  TORCH_CHECK(collectives_ready(), "commux: the device barrier needs the group's device collectives");
+  return coll_->barrier();
 }
+
+bool CudaTransport::collectives_ready() { return coll_ && !coll_->shared_gpu(); }
 
 }  // namespace cuda
 }  // namespace commux

@@ -28,6 +28,9 @@ class CollImpl {
   DevCollPtr broadcast(std::vector<at::Tensor>& ts, int root);
   DevCollPtr allgather(at::Tensor& out, const at::Tensor& in);
   DevCollPtr reduce_scatter(at::Tensor& out, const at::Tensor& in, RedOp op);
+  // One flag round among all ranks on the current stream, ordered after
+  // the work already on it (bounded waits; a timeout sets the status word).
+  DevCollPtr barrier();
   std::vector<std::pair<std::string, std::int64_t>> stats() const;
   int device() const { return dev_; }
 
@@ -62,6 +65,7 @@ class CollImpl {
   std::string nvls_why_;              // why not (empty when enabled or not attempted)
   std::int64_t nvls_min_bytes_ = 0;
   int forced_algo_ = -1;  // COMMUX_ALGO
+  std::int64_t st_barriers_ = 0;
   unsigned long long* trace_h_ = nullptr;  // COMMUX_COLL_TRACE (host-mapped)
   unsigned long long* trace_d_ = nullptr;
   void report_trace(int algo, int mode, std::int64_t bytes, int ctas);

@@ -31,6 +31,7 @@ enum CollMode : int {
   kModeReduceScatter = 2,
   kModeAllgather = 3,
   kModeBroadcast = 4,
+  kModeBarrier = 5,
 };
 enum CollAlgo : int { kAlgoOneShot = 0, kAlgoTwoShot = 1, kAlgoNvls = 2 };
 enum CollOp : int { kOpSum = 0, kOpProd = 1, kOpMin = 2, kOpMax = 3, kOpAvg = 4 };
@@ -81,6 +82,8 @@ inline bool nvls_supported(int dtype, int op) {
 }
 
 cudaError_t launch_coll(const CollArgs& a, int ctas, cudaStream_t s);
+// The device barrier: one flag round among all ranks (see coll_kernels.cu).
+cudaError_t launch_barrier(const CollArgs& a, cudaStream_t s);
 
 }  // namespace cuda
 }  // namespace commux

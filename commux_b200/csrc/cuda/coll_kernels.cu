@@ -34,6 +34,10 @@
 //   gather   (allgather/broadcast), chunked: push my block into slot[me] of
 //            every rank's B (broadcast: the root's block into slot 0), flag
 //            round, copy out, flag round.
+//   barrier  one CTA: a system-scope fence (everything this rank's stream
+//            wrote before the barrier, local or into a peer's memory, is
+//            visible system-wide), a flag to every rank, a bounded wait for
+//            every rank's flag.
 //   nvls     (large allreduce of f32/f16/bf16), pipelined the same way:
 //            copy my data into my NVLS buffer, flag round, multimem.ld_reduce
 //            my segment through the multicast mapping (NVSwitch sums every
@@ -496,6 +500,19 @@ __global__ void __launch_bounds__(kCollThreads, 2) twoshot_kernel(const __grid_c
   }
 }
 
+// ---- barrier ---------------------------------------------------------------------
+
+constexpr int kBarrierPhase = 2;
+
+__global__ void barrier_kernel(const __grid_constant__ CollArgs a) {
+  const std::uint64_t seq = a.seq_base + 1;
+  // the writes of the kernels before this one on the stream (and any into
+  // peers' memory) are performed system-wide before the flags go out
+  fence_acq_rel_sys();
+  signal(a, kBarrierPhase, seq);
+  await(a, kBarrierPhase, seq);
+}
+
 // ---- gather (allgather / broadcast) ------------------------------------------
 
 template <typename T>
@@ -779,6 +796,12 @@ cudaError_t dispatch_op(const CollArgs& a, int ctas, cudaStream_t s) {
 }
 
 }  // namespace
+
+cudaError_t launch_barrier(const CollArgs& a, cudaStream_t s) {
+  if (a.P > kMaxCollRanks) return cudaErrorInvalidValue;
+  barrier_kernel<<<1, 32, 0, s>>>(a);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_coll(const CollArgs& a, int ctas, cudaStream_t s) {
   if (ctas < 1 || ctas > kMaxCollCtas || a.P > kMaxCollRanks) return cudaErrorInvalidValue;

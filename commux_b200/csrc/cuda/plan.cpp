@@ -201,6 +201,7 @@ class CudaPlan final : public DevicePlan {
 
   void start() override {
     ++starts_;
+    tr_->plan_starts++;
     c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(c_->dev));
     cudaStream_t cur = c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(c_->dev)).stream();
     // messages to/from a rank on this same GPU go through the host-gated path
@@ -582,6 +583,11 @@ DevicePlanPtr CudaTransport::create_plan(const std::vector<at::Tensor>& recv_t, 
     }
   }
   for (auto& s : pending_sends) eng_->wait(s, std::chrono::milliseconds(0));
+  for (auto* v : {&plan->sends, &plan->recvs})
+    for (auto& m : *v) {
+      if (m.mode == PlanMode::Device) plan_device_msgs++;
+      if (m.mode == PlanMode::Shared) plan_shared_msgs++;
+    }
   plan->finalize();
   return plan;
 }

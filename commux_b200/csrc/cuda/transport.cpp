@@ -410,6 +410,7 @@ void CudaTransport::prepare_send(const ReqPtr& s, int dst, std::vector<char>& bl
     bool known = ph->cuda_uuid_valid.load(std::memory_order_acquire) != 0;
     bool same = known && std::memcmp(ph->cuda_uuid, c->uuid, 16) == 0;
     st->device_wait = known && !same;
+    (st->device_wait ? st_sends_device_ : st_sends_host_)++;
   }
   w->sender_waits_on_device = st->device_wait ? 1u : 0u;
   auto* segs = reinterpret_cast<SegWire*>(blob.data() + sizeof(DrtsWire));
@@ -651,6 +652,8 @@ void CudaTransport::on_match(const ReqPtr& r, int src, std::uint64_t send_id, co
     return;
   }
   st_pulls_++;
+  if (!local && len >= sizeof(DrtsWire))
+    (std::memcmp(w->uuid, c->uuid, 16) == 0 ? st_pulls_same_gpu_ : st_pulls_peer_gpu_)++;
   if (!local) {
     {
       std::lock_guard<SpinMutex> lk(pend_mu_);
@@ -961,6 +964,13 @@ std::vector<std::pair<std::string, std::int64_t>> CudaTransport::stats() {
       {"cuda_export_staged", st_export_staged_.load()},
       {"cuda_ipc_exports", st_ipc_exports_.load()},
       {"cuda_staged_sends", st_staged_.load()},
+      {"cuda_sends_device_flag", st_sends_device_.load()},
+      {"cuda_sends_host_fin", st_sends_host_.load()},
+      {"cuda_pulls_peer_gpu", st_pulls_peer_gpu_.load()},
+      {"cuda_pulls_same_gpu", st_pulls_same_gpu_.load()},
+      {"cuda_plan_device_msgs", plan_device_msgs.load()},
+      {"cuda_plan_shared_msgs", plan_shared_msgs.load()},
+      {"cuda_plan_starts", plan_starts.load()},
   };
   if (coll_)
     for (auto& kv : coll_->stats()) v.push_back(kv);

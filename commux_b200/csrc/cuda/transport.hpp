@@ -186,6 +186,7 @@ class CudaTransport final : public DeviceTransport {
   DevCollPtr reduce_scatter(at::Tensor& out, const at::Tensor& in, RedOp op) override;
   DevCollPtr barrier() override;
   bool device_collectives(int dev) override;
+  bool collectives_ready() override;
   DevicePlanPtr create_plan(const std::vector<at::Tensor>& recv_t, const std::vector<int>& recv_peer,
                             const std::vector<int>& recv_tag, const std::vector<at::Tensor>& send_t,
                             const std::vector<int>& send_peer, const std::vector<int>& send_tag) override;
@@ -214,6 +215,10 @@ class CudaTransport final : public DeviceTransport {
   std::uint64_t device_timeout_ns() const { return timeout_ns_; }
   int pull_ctas(DevCtx* c) const;
   std::atomic<std::int64_t> kernel_launches{0};
+  // which path the messages took (tests assert the intended one ran):
+  // persistent-plan messages to a rank on another GPU (device flags) or on
+  // this same GPU (host-gated), and plan starts
+  std::atomic<std::int64_t> plan_device_msgs{0}, plan_shared_msgs{0}, plan_starts{0};
 
  private:
   void publish_uuid(DevCtx* c);
@@ -262,6 +267,10 @@ class CudaTransport final : public DeviceTransport {
 
   std::atomic<std::int64_t> st_pulls_{0}, st_pull_bytes_{0}, st_wait_kernels_{0}, st_fins_{0},
       st_ipc_opens_{0}, st_ipc_exports_{0}, st_staged_{0}, st_ipc_closes_{0}, st_export_staged_{0};
+  // sends to another process: completed by a device-side wait on this
+  // stream (receiver on another GPU) or by the receiver's host FIN (same
+  // GPU); pulls from a sender on another GPU or on this same GPU
+  std::atomic<std::int64_t> st_sends_device_{0}, st_sends_host_{0}, st_pulls_peer_gpu_{0}, st_pulls_same_gpu_{0};
 };
 
 }  // namespace cuda

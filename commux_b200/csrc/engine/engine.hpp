@@ -427,6 +427,9 @@ class DeviceTransport {
   // the host collectives instead. The first call is collective (workspace
   // exchange): all ranks make it in the same order.
   virtual bool device_collectives(int dev) = 0;
+  // True once the device collectives are set up on this group and run on
+  // the device (the same on every rank: the set-up is collective).
+  virtual bool collectives_ready() = 0;
 
   // Persistent plan over the given receives and sends (matched by (peer,
   // tag) in FIFO order, like the one-shot path). Collective among the ranks

@@ -42,6 +42,34 @@ def test_jacobi7_matches_reference(dtype, shape):
     assert float(vd[:h].abs().sum()) == 0.0
 
 
+# Counter conditions (CMX_EXPECT, checked by every worker at exit) that
+# prove which path ran. "peer": every rank on its own GPU, so p2p completes
+# through device flags (the sender waits on its stream, the receiver pulls
+# over NVLink) and collectives run the device kernels. "shared": every rank
+# on GPU 0, so p2p completes through host FINs and collectives are staged
+# through the host (kernels of two processes on one GPU never wait on each
+# other).
+# (A first send to a peer whose GPU is not yet known may still complete by a
+# host FIN, so the peer form does not require zero of those.)
+PEER_P2P = "cuda_sends_device_flag>0,cuda_wait_kernels>0,cuda_pulls_peer_gpu>0,cuda_pulls_same_gpu==0"
+SHARED_P2P = "cuda_sends_host_fin>0,cuda_pulls_same_gpu>0,cuda_sends_device_flag==0,cuda_pulls_peer_gpu==0"
+PEER_PLAN = "cuda_plan_device_msgs>0,cuda_plan_shared_msgs==0,cuda_plan_starts>0"
+SHARED_PLAN = "cuda_plan_shared_msgs>0,cuda_plan_device_msgs==0,cuda_plan_starts>0"
+PEER_COLL = "coll_shared_gpu==0,coll_calls>0"
+SHARED_COLL = "coll_shared_gpu==1"
+
+
+def topology(mode, world, expect):
+    """Environment of a multi-rank CUDA test in one topology; skips the peer
+    form where the box has fewer GPUs than ranks (it would silently run the
+    shared form instead)."""
+    if mode == "peer":
+        if ngpu() < world:
+            pytest.skip(f"peer-GPU path needs {world} GPUs, one per rank; this box has {ngpu()}")
+        return dict(CUDA, CMX_EXPECT=expect[0])
+    return dict(CUDA, CMX_SHARED_GPU="1", CMX_EXPECT=expect[1])
+
+
 def test_p2p_self_sends():
     check(run("gpu_p2p.py", 1, env=CUDA))
 
@@ -50,42 +78,76 @@ def test_p2p_self_sends_group_window():
     check(run("gpu_p2p.py", 1, env=dict(CUDA, COMMUX_GROUP="1")))
 
 
-def test_p2p_two_ranks():
-    # one GPU: both ranks share it (host-gated path); more: one GPU per rank
-    check(run("gpu_p2p.py", 2, env=CUDA, timeout=180))
+@pytest.mark.parametrize("mode", ["peer", "shared"])
+def test_p2p_two_ranks(mode):
+    check(run("gpu_p2p.py", 2, env=topology(mode, 2, (PEER_P2P, SHARED_P2P)), timeout=180))
 
 
-def test_torch_dist_cuda():
-    check(run("torch_dist.py", 2, env=CUDA, timeout=180))
+@pytest.mark.parametrize("mode", ["peer", "shared"])
+def test_torch_dist_cuda(mode):
+    env = topology(mode, 2, (PEER_P2P + "," + PEER_COLL, SHARED_P2P + "," + SHARED_COLL))
+    check(run("torch_dist.py", 2, env=env, timeout=180))
 
 
-def test_coalesce_cuda():
-    check(run("coalesce.py", 2, env=dict(CUDA, COMMUX_COALESCE="1", COMMUX_GROUP="1"), timeout=180))
+@pytest.mark.parametrize("mode", ["peer", "shared"])
+def test_coalesce_cuda(mode):
+    env = topology(mode, 2, (PEER_P2P, SHARED_P2P))
+    check(run("coalesce.py", 2, env=dict(env, COMMUX_COALESCE="1", COMMUX_GROUP="1"), timeout=180))
 
 
-@pytest.mark.parametrize("world", [1, 2])
-def test_halo_cuda(world):
-    check(run("halo.py", world, env=dict(CUDA, COMMUX_GROUP="1"), timeout=180))
+def test_halo_cuda_one_rank():
+    check(run("halo.py", 1, env=dict(CUDA, COMMUX_GROUP="1", CMX_EXPECT="cuda_plan_starts>0"), timeout=180))
 
 
-def test_collectives_cuda():
-    check(run("collectives.py", 2, env=dict(CUDA, CMX_A2A="1"), timeout=240))
+@pytest.mark.parametrize("mode,world", [("peer", 2), ("peer", 4), ("peer", 8), ("shared", 2)])
+def test_halo_cuda(mode, world):
+    env = topology(mode, world, (PEER_PLAN, SHARED_PLAN))
+    check(run("halo.py", world, env=dict(env, COMMUX_GROUP="1"), timeout=300))
 
 
-@pytest.mark.parametrize("variant", ["default", "nvls", "p2p", "twoshot"])
+@pytest.mark.parametrize("mode", ["peer", "shared"])
+def test_collectives_cuda(mode):
+    env = topology(mode, 2, (PEER_COLL, SHARED_COLL))
+    check(run("collectives.py", 2, env=dict(env, CMX_A2A="1"), timeout=240))
+
+
+COLL_VARIANTS = {
+    # env, counters that prove the variant's kernels ran
+    "default": ({}, "coll_oneshot>0,coll_twoshot>0"),
+    "nvls": ({"COMMUX_NVLS_MIN_RANKS": "2", "COMMUX_NVLS_MIN_BYTES": "0"}, "coll_nvls_enabled==1,coll_nvls>0"),
+    "p2p": ({"COMMUX_NVLS": "0"}, "coll_nvls_enabled==0,coll_nvls==0,coll_oneshot>0,coll_twoshot>0"),
+    "twoshot": ({"COMMUX_NVLS": "0", "COMMUX_ALGO": "twoshot"}, "coll_oneshot==0,coll_twoshot>0"),
+}
+
+
+@pytest.mark.parametrize("variant", sorted(COLL_VARIANTS))
 def test_collective_numerics_cuda(variant):
-    # every rank on its own GPU where there are enough (NVLS and peer kernels),
-    # else ranks share GPUs (host-staged path); "nvls" forces the multicast
-    # path at any rank count and size, "p2p" turns it off
+    # every rank on its own GPU (up to 8): the device kernels of the variant
     world = max(2, min(ngpu(), 8))
-    env = dict(CUDA)
-    if variant == "nvls":
-        env.update(COMMUX_NVLS_MIN_RANKS="2", COMMUX_NVLS_MIN_BYTES="0")
-    elif variant == "p2p":
-        env.update(COMMUX_NVLS="0")
-    elif variant == "twoshot":
-        env.update(COMMUX_NVLS="0", COMMUX_ALGO="twoshot")
-    check(run("gpu_coll_numerics.py", world, env=env, timeout=600))
+    extra, expect = COLL_VARIANTS[variant]
+    env = topology("peer", world, (PEER_COLL + "," + expect + ",coll_gather>0", None))
+    check(run("gpu_coll_numerics.py", world, env=dict(env, **extra), timeout=600))
+
+
+def test_collective_numerics_cuda_shared_gpu():
+    env = topology("shared", 2, (None, SHARED_COLL))
+    check(run("gpu_coll_numerics.py", 2, env=dict(env, CMX_SIZES="7,70001,1048576"), timeout=600))
+
+
+def test_device_barrier_orders_device_work():
+    # peer GPUs only: on a shared GPU the barrier runs on the host
+    env = topology("peer", 2, ("coll_barriers>0,coll_shared_gpu==0", None))
+    world = max(2, min(ngpu(), 8))
+    check(run("gpu_barrier.py", world, env=dict(env, CMX_BARRIER_MODE="order"), timeout=300))
+
+
+def test_device_barrier_times_out_without_peer():
+    # rank 1 never joins: rank 0's bounded wait runs out (1 s), the kernel
+    # records it and returns, the call raises; plain peer loads, no NVLS
+    env = topology("peer", 2, ("coll_barriers>0", None))
+    env.update(CMX_BARRIER_MODE="timeout", COMMUX_DEVICE_TIMEOUT_MS="1000", COMMUX_NVLS="0",
+               NCCL_NVLS_ENABLE="0")
+    check(run("gpu_barrier.py", 2, env=env, timeout=180))
 
 
 def test_smoke_entry():
@@ -95,30 +157,40 @@ def test_smoke_entry():
 
 
 def test_plan_self():
-    check(run("gpu_plan.py", 1, env=CUDA))
+    check(run("gpu_plan.py", 1, env=dict(CUDA, CMX_EXPECT="cuda_plan_starts>0,cuda_plan_device_msgs==0")))
 
 
-def test_plan_two_ranks():
-    # shared GPU: host-gated per start; one GPU per rank: device flags
-    check(run("gpu_plan.py", 2, env=CUDA, timeout=180))
+@pytest.mark.parametrize("mode", ["peer", "shared"])
+def test_plan_two_ranks(mode):
+    check(run("gpu_plan.py", 2, env=topology(mode, 2, (PEER_PLAN, SHARED_PLAN)), timeout=180))
 
 
-@pytest.mark.parametrize("world", [1, 2])
-def test_halo_cuda_batch_path(world):
-    check(run("halo.py", world, env=dict(CUDA, COMMUX_HALO_PLAN="0", COMMUX_GROUP="1"), timeout=180))
+def test_halo_cuda_batch_path_one_rank():
+    check(run("halo.py", 1, env=dict(CUDA, COMMUX_HALO_PLAN="0", COMMUX_GROUP="1",
+                                     CMX_EXPECT="cuda_plan_starts==0,cuda_pulls>0"), timeout=180))
 
 
-def test_ipc_mappings_bounded_under_allocator_churn():
-    # ranks share one GPU or have one each: either way the receiver maps the
-    # sender's segments through CUDA IPC
-    check(run("gpu_ipc_churn.py", 2, env=CUDA, timeout=240))
+@pytest.mark.parametrize("mode", ["peer", "shared"])
+def test_halo_cuda_batch_path(mode):
+    env = topology(mode, 2, (PEER_P2P + ",cuda_plan_starts==0", SHARED_P2P + ",cuda_plan_starts==0"))
+    check(run("halo.py", 2, env=dict(env, COMMUX_HALO_PLAN="0", COMMUX_GROUP="1"), timeout=180))
 
 
-def test_unexportable_memory_staged():
+@pytest.mark.parametrize("mode", ["peer", "shared"])
+def test_ipc_mappings_bounded_under_allocator_churn(mode):
+    # either way the receiver maps the sender's segments through CUDA IPC
+    env = topology(mode, 2, ("cuda_pulls_peer_gpu>0,cuda_pulls_same_gpu==0", "cuda_pulls_same_gpu>0"))
+    check(run("gpu_ipc_churn.py", 2, env=env, timeout=240))
+
+
+@pytest.mark.parametrize("mode", ["peer", "shared"])
+def test_unexportable_memory_staged(mode):
     # the caching allocator's expandable segments cannot be exported through
     # CUDA IPC: sends to another process travel through the export pool
-    env = dict(CUDA, PYTORCH_CUDA_ALLOC_CONF="expandable_segments:True")
+    alloc = {"PYTORCH_CUDA_ALLOC_CONF": "expandable_segments:True"}
+    env = dict(topology(mode, 2, (PEER_P2P, SHARED_P2P)), **alloc)
     check(run("gpu_p2p.py", 2, env=dict(env, CMX_EXPECT_EXPORT_STAGING="1"), timeout=240))
+    env = dict(topology(mode, 2, (PEER_PLAN, SHARED_PLAN)), **alloc)
     check(run("gpu_plan.py", 2, env=env, timeout=240))
     check(run("halo.py", 2, env=dict(env, COMMUX_GROUP="1"), timeout=240))
 

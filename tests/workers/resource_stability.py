@@ -29,6 +29,10 @@ for k in range(50):
 dist.barrier()
 time.sleep(0.2)  # FIN records of the last rendezvous messages land
 st = commux.stats()
+# every rank reads its gauges before any rank sends the next message (the
+# agreement all_reduce of finish() would otherwise land in a slower rank's
+# unexpected queue before that rank read its gauges)
+dist.barrier()
 c.check("at least 100 host sends", st["sends"] >= 100, str(st["sends"]))
 for g in ("posted_now", "unexpected_now", "partial_now", "sends_waiting_now", "pump_waiting_now"):
     c.check(f"{g} back to zero", st[g] == 0, f"{g}={st[g]}")
