@@ -63,6 +63,11 @@ struct PullDesc {
   // this GPU's memory that the sender's stream sets); nullptr: no wait
   const std::uint64_t* ready;
   std::uint64_t ready_val;
+  // interleaved group: ilv > 1 descriptors [ilv_first, ilv_first + ilv) with
+  // equal chunk0 and nchunks take their chunks round robin (see find_desc);
+  // ilv <= 1: a descriptor of its own
+  std::uint32_t ilv;
+  std::uint32_t ilv_first;
 #if defined(COMMUX_DEVICE_CHECKS)
   // bounds-check build: the byte offsets from src / dst that the copy may
   // touch, [lo, hi). A unit outside them is skipped and reported in the
@@ -92,6 +97,15 @@ struct PullBatch {
   // packing ride on its pull launch instead of a launch of their own
   std::uint32_t nsig;
   std::uint64_t* sig[kMaxEntrySignals];
+  // persistent plans, last launch of a start: the CTA that finishes last
+  // (counted in *cta_done, device memory, zero between launches) waits,
+  // bounded, until every fin[i] reaches *epoch -- the receivers' "consumed"
+  // flags of this rank's sends -- and then advances *bump (the epoch).
+  // bump == nullptr: nothing of the kind.
+  std::uint64_t* bump;
+  unsigned int* cta_done;
+  std::uint32_t nfin;
+  const std::uint64_t* fin[kMaxWaitFlags];
   PullDesc d[kMaxBatch];
 };
 // passed by value as a __grid_constant__ kernel parameter (limit 32764 bytes)
@@ -102,9 +116,7 @@ struct WaitBatch {
   std::uint32_t n;
   std::uint64_t timeout_ns;
   unsigned long long* status;
-  const std::uint64_t* epoch;  // non-null: every val is *epoch (plans)
-  std::uint64_t* bump;         // non-null: *bump += 1 once every wait is over
-  unsigned long long* trace;   // as PullBatch::trace (one CTA)
+  const std::uint64_t* epoch;  // non-null: every val is *epoch
   const std::uint64_t* flag[kMaxWaitFlags];
   std::uint64_t val[kMaxWaitFlags];
 };
@@ -126,6 +138,9 @@ cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStrea
 // 2, 1 byte units; 0 = wide strides).
 inline int pull_unit_class(const PullDesc& d) { return d.wide ? 0 : static_cast<int>(d.unit); }
 cudaError_t launch_wait(const WaitBatch& b, cudaStream_t s);
+// Launches the pull kernel on a batch already in device memory (`dev`, a
+// copy of `host`, whose descriptors share one unit class).
+cudaError_t launch_pull_dev(const PullBatch& host, const PullBatch* dev, int max_ctas, cudaStream_t s);
 // Loads every pull-kernel build into the current context (see p2p_kernels.cu).
 cudaError_t preload_pull_kernels();
 

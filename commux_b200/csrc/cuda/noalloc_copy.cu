@@ -178,6 +178,9 @@ extern "C" int commux_strided_copy_noalloc(void* dst, const int64_t* dst_strides
   b.trace = nullptr;
   b.trace_count = nullptr;
   b.nsig = 0;
+  b.bump = nullptr;
+  b.cta_done = nullptr;
+  b.nfin = 0;
   b.counters = reinterpret_cast<std::uint32_t*>(su.scratch);
   b.status = reinterpret_cast<unsigned long long*>(su.scratch + kNoAllocCounterBytes);
   b.timeout_ns = 0;

@@ -188,13 +188,34 @@ __device__ __forceinline__ bool wait_ready(const std::uint64_t* ready, std::uint
   return true;
 }
 
-// Descriptors in the kernel parameter block (read through the constant
-// cache); the epoch of a plan's launch comes from device memory.
-struct InlineSrc {
+// The batch of a launch: in the kernel parameter block (kGlobal false; read
+// through the constant cache), or in device memory (kGlobal true: a plan's
+// batches are uploaded once, so each launch passes one pointer instead of
+// about 27 KB of parameters, which the launch would copy every time). In
+// device memory, each chunk's descriptor is staged into shared memory by the
+// CTA before its warps copy. The epoch of a plan's launch comes from device
+// memory either way.
+template <bool kGlobal>
+struct BatchSrc {
   const PullBatch& b;
+  PullDesc* staged;  // shared memory (kGlobal)
   __device__ std::uint32_t n() const { return b.n; }
   __device__ std::uint32_t total() const { return b.total_chunks; }
   __device__ const PullDesc& desc(std::uint32_t i) const { return b.d[i]; }
+  // descriptor i for the copy loops (every thread of the CTA calls this)
+  __device__ const PullDesc& load(std::uint32_t i) const {
+    if constexpr (!kGlobal) {
+      return b.d[i];
+    } else {
+      static_assert(sizeof(PullDesc) % 8 == 0, "descriptor staged in 8-byte words");
+      __syncthreads();  // every warp is done with the previous descriptor
+      const uint2* from = reinterpret_cast<const uint2*>(&b.d[i]);
+      uint2* to = reinterpret_cast<uint2*>(staged);
+      for (std::uint32_t k = threadIdx.x; k < sizeof(PullDesc) / 8; k += blockDim.x) to[k] = from[k];
+      __syncthreads();
+      return *staged;
+    }
+  }
   __device__ std::uint32_t* counters() const { return b.counters; }
   __device__ unsigned long long* status() const { return b.status; }
   __device__ std::uint64_t timeout_ns() const { return b.timeout_ns; }
@@ -219,12 +240,47 @@ struct InlineSrc {
   __device__ void entry_signals(std::uint64_t epoch) const {
     if (blockIdx.x == 0 && threadIdx.x < b.nsig) st_release_sys(b.sig[threadIdx.x], epoch);
   }
+  // The last CTA to finish waits for the receivers' "consumed" flags and
+  // advances the epoch: every other CTA has read the epoch already (at its
+  // start) and has finished, so the next start sees the new value.
+  __device__ void finish(std::uint64_t epoch) const {
+    if (b.bump == nullptr) return;
+    __shared__ int last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      last = atomicAdd(b.cta_done, 1u) == gridDim.x - 1 ? 1 : 0;
+    }
+    __syncthreads();
+    if (!last) return;
+    for (std::uint32_t i = threadIdx.x; i < b.nfin; i += blockDim.x) {
+      const std::uint64_t t0 = globaltimer_ns();
+      std::uint32_t spins = 0;
+      while (ld_acquire_sys(b.fin[i]) < epoch) {
+        if ((++spins & 63u) == 0u && globaltimer_ns() - t0 > b.timeout_ns) {
+          report_status(b.status, kStatusWaitTimeout, reinterpret_cast<unsigned long long>(b.fin[i]), epoch,
+                        ld_acquire_sys(b.fin[i]));
+          break;
+        }
+        __nanosleep(128);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      *b.cta_done = 0u;
+      *b.bump = epoch + 1;
+    }
+  }
 };
 
-// Descriptor owning global chunk c: the last one whose chunk0 <= c (binary
-// search; descriptors are sorted by chunk0 and the first has chunk0 == 0).
+// Descriptor owning global chunk c and the chunk's index inside it. The
+// descriptors are sorted by chunk0 (the first has chunk0 == 0); the binary
+// search finds the last one whose chunk0 <= c. An interleaved group (ilv > 1:
+// descriptors [ilv_first, ilv_first + ilv), all with the same chunk0 and
+// chunk count) takes its chunks round robin, chunk k of each member in turn,
+// so row k of every member is copied at about the same time.
 template <class S>
-__device__ __forceinline__ std::uint32_t find_desc(const S& s, std::uint32_t c) {
+__device__ __forceinline__ std::uint32_t find_desc(const S& s, std::uint32_t c, std::uint32_t& local) {
   std::uint32_t lo = 0, hi = s.n();  // answer in [lo, hi)
   while (hi - lo > 1) {
     const std::uint32_t mid = (lo + hi) >> 1;
@@ -233,6 +289,13 @@ __device__ __forceinline__ std::uint32_t find_desc(const S& s, std::uint32_t c) 
     else
       hi = mid;
   }
+  const PullDesc& h = s.desc(lo);
+  const std::uint32_t off = c - h.chunk0;
+  if (h.ilv > 1) {
+    local = off / h.ilv;
+    return h.ilv_first + off % h.ilv;
+  }
+  local = off;
   return lo;
 }
 
@@ -252,8 +315,9 @@ __device__ __forceinline__ void pull_body(const S& s) {
   s.trace_start();
   s.entry_signals(epoch);
   for (std::uint32_t c = blockIdx.x; c < s.total(); c += gridDim.x) {
-    const PullDesc& d = s.desc(find_desc(s, c));
-    const std::uint32_t u0 = (c - d.chunk0) * kChunkUnits;
+    std::uint32_t local = 0;
+    const PullDesc& d = s.load(find_desc(s, c, local));
+    const std::uint32_t u0 = local * kChunkUnits;
     bool failed = false;
     if (d.ready != nullptr) {  // persistent plan: wait for the sender's data
       if (threadIdx.x == 0)
@@ -294,6 +358,7 @@ __device__ __forceinline__ void pull_body(const S& s) {
     }
   }
   s.trace_end();
+  s.finish(epoch);
 }
 
 // One instantiation per unit size U (U == 0: the 64-bit-stride walk for wide
@@ -301,7 +366,14 @@ __device__ __forceinline__ void pull_body(const S& s) {
 // 80 registers, one loop alone fits the 64 that four CTAs per SM allow.
 template <int U>
 __global__ void __launch_bounds__(kThreads, 4) pull_kernel(const __grid_constant__ PullBatch b) {
-  pull_body<U>(InlineSrc{b});
+  pull_body<U>(BatchSrc<false>{b, nullptr});
+}
+
+// The same copy with the batch in device memory (persistent plans).
+template <int U>
+__global__ void __launch_bounds__(kThreads, 4) pull_kernel_dev(const PullBatch* __restrict__ g) {
+  __shared__ PullDesc staged;
+  pull_body<U>(BatchSrc<true>{*g, &staged});
 }
 
 // One warp: lane i waits until *flag[i] >= val[i], giving up after the
@@ -319,30 +391,6 @@ __global__ void wait_kernel(const __grid_constant__ WaitBatch b) {
       return;
     }
     __nanosleep(128);
-  }
-}
-
-// As wait_kernel, then (plans) advance the epoch once every lane is done.
-__global__ void wait_bump_kernel(const __grid_constant__ WaitBatch b) {
-  const std::uint32_t i = threadIdx.x;
-  if (b.trace != nullptr && i == 0) b.trace[0] = globaltimer_ns();
-  if (i < b.n) {
-    const std::uint64_t want = *b.epoch;
-    const std::uint64_t t0 = globaltimer_ns();
-    std::uint32_t spins = 0;
-    while (ld_acquire_sys(b.flag[i]) < want) {
-      if ((++spins & 63u) == 0u && globaltimer_ns() - t0 > b.timeout_ns) {
-        report_status(b.status, kStatusWaitTimeout, reinterpret_cast<unsigned long long>(b.flag[i]), want,
-                      ld_acquire_sys(b.flag[i]));
-        break;
-      }
-      __nanosleep(128);
-    }
-  }
-  __syncthreads();
-  if (i == 0) {
-    *b.bump += 1;
-    if (b.trace != nullptr) b.trace[1] = globaltimer_ns();
   }
 }
 
@@ -376,7 +424,41 @@ cudaError_t launch_class(int cls, const PullBatch& b, int max_ctas, cudaStream_t
   return cudaGetLastError();
 }
 
+cudaError_t launch_class_dev(int cls, const PullBatch* g, std::uint32_t total_chunks, int max_ctas,
+                             cudaStream_t s) {
+  const int grid = static_cast<int>(total_chunks < static_cast<std::uint32_t>(max_ctas) ? total_chunks : max_ctas);
+  switch (cls) {
+    case 16:
+      pull_kernel_dev<16><<<grid, kThreads, 0, s>>>(g);
+      break;
+    case 8:
+      pull_kernel_dev<8><<<grid, kThreads, 0, s>>>(g);
+      break;
+    case 4:
+      pull_kernel_dev<4><<<grid, kThreads, 0, s>>>(g);
+      break;
+    case 2:
+      pull_kernel_dev<2><<<grid, kThreads, 0, s>>>(g);
+      break;
+    case 1:
+      pull_kernel_dev<1><<<grid, kThreads, 0, s>>>(g);
+      break;
+    default:
+      pull_kernel_dev<0><<<grid, kThreads, 0, s>>>(g);
+      break;
+  }
+  return cudaGetLastError();
+}
+
 }  // namespace
+
+cudaError_t launch_pull_dev(const PullBatch& host, const PullBatch* dev, int max_ctas, cudaStream_t s) {
+  if (host.n == 0 || host.total_chunks == 0) return cudaSuccess;
+  const int cls = pull_unit_class(host.d[0]);
+  for (std::uint32_t i = 1; i < host.n; ++i)
+    if (pull_unit_class(host.d[i]) != cls) return cudaErrorInvalidValue;
+  return launch_class_dev(cls, dev, host.total_chunks, max_ctas, s);
+}
 
 // A batch whose descriptors share one unit class is one launch; a mixed batch
 // becomes one launch per class, in order on the stream (completion counters
@@ -399,6 +481,11 @@ cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStrea
   sub.trace = b.trace;
   sub.trace_count = b.trace_count;
   sub.nsig = 0;  // entry signals go with the first class launched
+  sub.bump = nullptr;  // the end-of-start wait goes with the last one
+  int last_cls = -1;
+  for (int cls : {16, 8, 4, 2, 1, 0})
+    for (std::uint32_t i = 0; i < b.n && last_cls != cls; ++i)
+      if (pull_unit_class(b.d[i]) == cls && b.d[i].nchunks > 0) last_cls = cls;
   bool first_launch = true;
   for (int cls : {16, 8, 4, 2, 1, 0}) {
     sub.n = 0;
@@ -417,6 +504,12 @@ cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStrea
       first_launch = false;
     } else {
       sub.nsig = 0;
+    }
+    if (cls == last_cls) {
+      sub.bump = b.bump;
+      sub.cta_done = b.cta_done;
+      sub.nfin = b.nfin;
+      for (std::uint32_t k = 0; k < b.nfin; ++k) sub.fin[k] = b.fin[k];
     }
     if (launches != nullptr) ++*launches;
     cudaError_t e = launch_class(cls, sub, max_ctas, s);
@@ -438,10 +531,6 @@ cudaError_t preload_pull_kernels() {
 }
 
 cudaError_t launch_wait(const WaitBatch& b, cudaStream_t s) {
-  if (b.bump != nullptr) {
-    wait_bump_kernel<<<1, kMaxWaitFlags, 0, s>>>(b);
-    return cudaGetLastError();
-  }
   if (b.n == 0) return cudaSuccess;
   wait_kernel<<<1, kMaxWaitFlags, 0, s>>>(b);
   return cudaGetLastError();

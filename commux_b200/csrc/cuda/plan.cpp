@@ -76,8 +76,9 @@ class CudaPlan final : public DevicePlan {
 
   // Builds the launches every start() replays: (1) pack + "ready" signals of
   // the sends to other GPUs (without packing, the signals are stored by the
-  // first pull launch at entry instead), (2) the pulls of every receive, (3)
-  // the wait for the receivers' "consumed" flags, ending with the epoch bump.
+  // first pull launch at entry instead), (2) the pulls of every receive; the
+  // last CTA of the last launch then waits for the receivers' "consumed"
+  // flags and advances the epoch.
   // Every flag value is
   // the plan's epoch, read from device memory, so the launches never change:
   // they are captured once into a CUDA graph and a start is one graph launch.
@@ -133,8 +134,10 @@ class CudaPlan final : public DevicePlan {
       for (auto& m : packs) merge = merge && pull_unit_class(m[0]) == cls;
     }
     std::vector<std::vector<PullDesc>> pre;
+    std::size_t lead = 0;  // pack messages at the head of the pull launch
     if (merge) {
       pull.insert(pull.begin(), packs.begin(), packs.end());
+      lead = packs.size();
     } else {
       pre = packs;
     }
@@ -147,18 +150,20 @@ class CudaPlan final : public DevicePlan {
       x.nchunks = 1;
       pre.push_back({x});
     }
-    // device state: [epoch u64, starts at 1][counters u32 x kCounterSlots]
+    // device state: [epoch u64, starts at 1][finished-CTA count u32][pad to
+    // 64 bytes][counters u32 x kCounterSlots]
     const std::size_t state_bytes = 64 + kCounterSlots * sizeof(std::uint32_t);
     state_ = at::empty({static_cast<std::int64_t>(state_bytes)},
                        at::TensorOptions().dtype(at::kByte).device(at::kCUDA, c_->dev));
     epoch_d_ = reinterpret_cast<std::uint64_t*>(state_.data_ptr());
+    cta_done_d_ = reinterpret_cast<unsigned int*>(static_cast<char*>(state_.data_ptr()) + 8);
     counters_d_ = reinterpret_cast<std::uint32_t*>(static_cast<char*>(state_.data_ptr()) + 64);
     std::vector<char> init(state_bytes, 0);
     const std::uint64_t one = 1;
     std::memcpy(init.data(), &one, sizeof(one));
     CMX_CUDA(cudaMemcpy(state_.data_ptr(), init.data(), state_bytes, cudaMemcpyHostToDevice));
-    pre_ = batches(pre);
-    pulls_ = batches(pull);
+    pre_ = batches(pre, pre.size());
+    pulls_ = batches(pull, lead);
     if (!ready_only.empty()) {
       TORCH_CHECK(ready_only.size() <= static_cast<std::size_t>(kMaxEntrySignals), "commux plan: more than ",
                   kMaxEntrySignals, " unpacked sends to other GPUs");
@@ -166,21 +171,29 @@ class CudaPlan final : public DevicePlan {
       first.nsig = static_cast<std::uint32_t>(ready_only.size());
       for (std::size_t k = 0; k < ready_only.size(); ++k) first.sig[k] = ready_only[k];
     }
-    std::memset(&wait_, 0, sizeof(wait_));
-    wait_.timeout_ns = tr_->device_timeout_ns();
-    wait_.status = c_->status_d;
-    wait_.epoch = epoch_d_;
-    wait_.bump = epoch_d_;  // the wait launch also advances the epoch
+    std::memset(&wait_, 0, sizeof(wait_));  // the "consumed" flags of the sends to other GPUs
     for (auto& m : sends)
       if (m.mode == PlanMode::Device) {
         TORCH_CHECK(wait_.n < static_cast<std::uint32_t>(kMaxWaitFlags), "commux plan: more than ",
                     kMaxWaitFlags, " sends to other GPUs");
         wait_.flag[wait_.n++] = m.consumed_local;
       }
+    // the receivers' "consumed" flags and the epoch bump ride on the last
+    // launch: its last CTA waits for them and advances the epoch
+    bool flags = wait_.n > 0;
+    for (auto& m : recvs) flags |= m.mode == PlanMode::Device;
+    PullBatch* last = !pulls_.empty() ? pulls_.back().get() : !pre_.empty() ? pre_.back().get() : nullptr;
+    TORCH_CHECK(!flags || last != nullptr, "commux plan: internal error, flags without a launch");
+    if (flags) {
+      last->bump = epoch_d_;
+      last->cta_done = cta_done_d_;
+      last->nfin = wait_.n;
+      for (std::uint32_t k = 0; k < wait_.n; ++k) last->fin[k] = wait_.flag[k];
+    }
     // COMMUX_PLAN_TRACE: span of every launch of a start (earliest CTA start,
     // latest CTA end), printed after each start (which then synchronises)
     if (env_int("COMMUX_PLAN_TRACE", 0) != 0) {
-      const std::size_t n = pre_.size() + pulls_.size() + 1;
+      const std::size_t n = pre_.size() + pulls_.size();
       CMX_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&trace_h_), n * 2 * sizeof(unsigned long long),
                              cudaHostAllocMapped));
       unsigned long long* d = nullptr;
@@ -194,9 +207,21 @@ class CudaPlan final : public DevicePlan {
           b->trace = d + 2 * k++;
           b->trace_count = count;
         }
-      wait_.trace = d + 2 * k;
       trace_n_ = n;
     }
+    // every batch goes to device memory once: a launch passes one pointer
+    const std::size_t nb = pre_.size() + pulls_.size();
+    if (nb > 0) {
+      batches_d_ = at::empty({static_cast<std::int64_t>(nb * sizeof(PullBatch))},
+                             at::TensorOptions().dtype(at::kByte).device(at::kCUDA, c_->dev));
+      std::size_t k = 0;
+      for (auto* ls : {&pre_, &pulls_})
+        for (auto& b : *ls) CMX_CUDA(cudaMemcpy(dev_batch(k++), b.get(), sizeof(PullBatch), cudaMemcpyHostToDevice));
+    }
+  }
+
+  PullBatch* dev_batch(std::size_t k) {
+    return reinterpret_cast<PullBatch*>(static_cast<char*>(batches_d_.data_ptr()) + k * sizeof(PullBatch));
   }
 
   void start() override {
@@ -267,19 +292,32 @@ class CudaPlan final : public DevicePlan {
     };
     for (std::size_t i = 0; i < pre_.size(); ++i) span("pack");
     for (std::size_t i = 0; i < pulls_.size(); ++i) span("pull");
-    span("wait");
     std::fprintf(stderr, "[commux plan trace rank %d] start %llu, us from the first CTA:%s\n", eng_->rank(),
                  static_cast<unsigned long long>(starts_), line.c_str());
   }
 
-  // Messages -> parameter blocks of at most kMaxBatch descriptors, one unit
-  // class each; every message counts into its own counter slot (the plan's
+  // Messages -> batches of at most kMaxBatch descriptors, one unit class
+  // each; every message counts into its own counter slot (the plan's
   // launches run one after another and each message returns its counter to
-  // zero, so the slots are reused by the next start).
-  std::vector<std::unique_ptr<PullBatch>> batches(const std::vector<std::vector<PullDesc>>& msgs) {
-    std::map<int, std::vector<PullDesc>> by_cls;
+  // zero, so the slots are reused by the next start). Messages of one
+  // descriptor and equal chunk count (a halo's six faces) after the first
+  // `lead` messages (the packs, which run first) form an interleaved group
+  // placed where its first member was: their chunks go round robin, so row k
+  // of every face is copied at about the same time and faces that share
+  // DRAM sectors (the 16-byte x-face rows of both sides of a row) meet in L2
+  // (COMMUX_PLAN_INTERLEAVE=0 keeps the message order).
+  std::vector<std::unique_ptr<PullBatch>> batches(const std::vector<std::vector<PullDesc>>& msgs,
+                                                  std::size_t lead = 0) {
+    static const bool interleave = env_int("COMMUX_PLAN_INTERLEAVE", 1) != 0;
+    struct Unit {
+      std::vector<PullDesc> descs;  // one message, or an interleaved group
+      std::uint32_t ilv = 1;
+    };
+    std::map<int, std::vector<Unit>> by_cls;
+    std::map<std::pair<int, std::uint32_t>, std::size_t> group_at;  // (class, chunks) -> unit index
     std::uint32_t slot = 0;
-    for (auto& m : msgs) {
+    for (std::size_t mi = 0; mi < msgs.size(); ++mi) {
+      const auto& m = msgs[mi];
       if (m.empty()) continue;
       const int cls = pull_unit_class(m[0]);
       std::uint32_t chunks = 0;
@@ -289,33 +327,58 @@ class CudaPlan final : public DevicePlan {
       }
       TORCH_CHECK(slot < kCounterSlots - 1, "commux plan: too many messages");
       auto& v = by_cls[cls];
-      for (auto d : m) {
+      std::vector<PullDesc> ds(m);
+      for (auto& d : ds) {
         d.counter_idx = slot;
         d.msg_chunks = chunks;
-        v.push_back(d);
+        d.ilv = 1;
       }
       ++slot;
+      if (interleave && mi >= lead && ds.size() == 1 && chunks >= 2) {
+        auto key = std::make_pair(cls, chunks);
+        auto it = group_at.find(key);
+        if (it != group_at.end() && v[it->second].ilv < 32) {
+          v[it->second].descs.push_back(ds[0]);
+          v[it->second].ilv++;
+          continue;
+        }
+        group_at[key] = v.size();
+      }
+      v.push_back(Unit{std::move(ds), 1});
     }
     std::vector<std::unique_ptr<PullBatch>> out;
+    auto fresh = [&]() {
+      auto b = std::make_unique<PullBatch>();
+      b->n = 0;
+      b->total_chunks = 0;
+      b->counters = counters_d_;
+      b->status = c_->status_d;
+      b->timeout_ns = tr_->device_timeout_ns();
+      b->epoch = epoch_d_;
+      b->nsig = 0;
+      return b;
+    };
     for (auto& kv : by_cls) {
-      std::size_t i = 0;
-      while (i < kv.second.size()) {
-        auto b = std::make_unique<PullBatch>();
-        b->n = 0;
-        b->total_chunks = 0;
-        b->counters = counters_d_;
-        b->status = c_->status_d;
-        b->timeout_ns = tr_->device_timeout_ns();
-        b->epoch = epoch_d_;
-        b->nsig = 0;
-        while (i < kv.second.size() && b->n < static_cast<std::uint32_t>(kMaxBatch)) {
-          PullDesc d = kv.second[i++];
-          d.chunk0 = b->total_chunks;
+      std::unique_ptr<PullBatch> b = fresh();
+      for (auto& u : kv.second) {
+        if (b->n + u.descs.size() > static_cast<std::size_t>(kMaxBatch)) {
+          out.push_back(std::move(b));
+          b = fresh();
+        }
+        const std::uint32_t first = b->n, c0 = b->total_chunks;
+        for (auto d : u.descs) {
+          if (u.ilv > 1) {  // the group's members share chunk0 and their chunk range
+            d.chunk0 = c0;
+            d.ilv = u.ilv;
+            d.ilv_first = first;
+          } else {
+            d.chunk0 = b->total_chunks;
+          }
           b->total_chunks += d.nchunks;
           b->d[b->n++] = d;
         }
-        out.push_back(std::move(b));
       }
+      if (b->n > 0) out.push_back(std::move(b));
     }
     return out;
   }
@@ -332,20 +395,16 @@ class CudaPlan final : public DevicePlan {
     nodes_ = 0;
     CMX_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
     cudaError_t e = cudaSuccess;
+    std::size_t k = 0;
     for (auto* ls : {&pre_, &pulls_})
       for (auto& b : *ls) {
-        int launched = 0;
-        if (e == cudaSuccess) e = launch_pull(*b, ctas, 256, cs, &launched);
-        nodes_ += launched;
+        if (e == cudaSuccess) e = launch_pull_dev(*b, dev_batch(k), ctas, cs);
+        ++k;
+        ++nodes_;
       }
-    // waits (if any), then the epoch bump; a plan whose every message stays
-    // on this GPU has no flags, so no epoch to advance and no launch here
-    bool flags = wait_.n > 0;
-    for (auto& m : recvs) flags |= m.mode == PlanMode::Device;
-    if (e == cudaSuccess && flags) {
-      e = launch_wait(wait_, cs);
-      ++nodes_;
-    }
+    // the receivers' "consumed" flags and the epoch bump ride on the last
+    // launch (its last CTA waits and bumps; see PullBatch::bump); a plan
+    // whose every message stays on this GPU has no flags and no epoch
     cudaGraph_t g = nullptr;
     cudaError_t e2 = cudaStreamEndCapture(cs, &g);
     cudaStreamDestroy(cs);  // holds no tensors: safe to destroy
@@ -361,6 +420,8 @@ class CudaPlan final : public DevicePlan {
   std::uint64_t starts_ = 0;
   at::Tensor state_;
   std::uint64_t* epoch_d_ = nullptr;
+  unsigned int* cta_done_d_ = nullptr;
+  at::Tensor batches_d_;  // the launches' batches in device memory
   std::uint32_t* counters_d_ = nullptr;
   std::vector<std::unique_ptr<PullBatch>> pre_, pulls_;
   WaitBatch wait_{};

@@ -10,6 +10,7 @@
 #include <map>
 #include <cstdio>
 #include <cstring>
+#include <thread>
 #include <sstream>
 
 #include "coll.hpp"
@@ -643,6 +644,7 @@ void CudaTransport::on_match(const ReqPtr& r, int src, std::uint64_t send_id, co
   pp.src = src;
   pp.send_id = send_id;
   pp.ctx = c;
+  pp.sender_waits = !local && len >= sizeof(DrtsWire) && w->sender_waits_on_device != 0;
   try {
     build_descs(r, blob, len, local, pp);
   } catch (const std::exception& e) {
@@ -766,13 +768,18 @@ bool CudaTransport::poll() {
     for (auto& p : ready) by_ctx[p.ctx].push_back(std::move(p));
     for (auto& kv : by_ctx) {
       Flight f;
+      std::vector<std::pair<int, std::uint64_t>> launched;
       for (auto& p : kv.second) {
         f.fins.push_back({p.src, p.send_id});
+        if (p.sender_waits) launched.push_back({p.src, p.send_id});
         f.reqs.push_back(p.r);
       }
+      f.pulls = static_cast<int>(kv.second.size());
       launch_batch(kv.first, kv.second, kv.first->comm);
       f.done = state<RecvState>(f.reqs.front())->done;
       flights_.push_back(std::move(f));
+      // the copies are enqueued: their senders may now wait on the device
+      for (auto& x : launched) eng_->send_fin(x.first, x.second, proto::kFinLaunched);
     }
   }
   while (!flights_.empty()) {
@@ -788,25 +795,63 @@ bool CudaTransport::poll() {
       eng_->send_fin(fin.first, fin.second, e == cudaSuccess ? 0 : -5);
       st_fins_++;
     }
-    inflight_.fetch_sub(static_cast<int>(f.fins.size()));
+    inflight_.fetch_sub(f.pulls);  // == f.fins.size()
     flights_.pop_front();
     busy = true;
   }
   return busy;
 }
 
+namespace {
+
+std::string fin_error(std::int64_t status) {
+  const char* why = status == -3   ? "the receiver shares this GPU but the send expected a peer GPU"
+                    : status == -4 ? "the receiver could not describe the copy (layout/size mismatch)"
+                    : status == -5 ? "the receiver's copy kernel failed"
+                                   : "the receiver rejected the message";
+  return std::string("commux send: ") + why;
+}
+
+}  // namespace
+
 void CudaTransport::on_fin(const ReqPtr& s, std::int64_t status) {
   auto st = state<SendState>(s);
-  if (st) st->fin.store(true, std::memory_order_release);
+  if (status == proto::kFinLaunched) {
+    if (st) st->launched.store(true, std::memory_order_release);
+    return;
+  }
+  if (st) {
+    if (status != 0) st->fin_status.store(status, std::memory_order_relaxed);
+    st->fin.store(true, std::memory_order_release);
+  }
   if (status != 0) {
-    const char* why = status == -3   ? "the receiver shares this GPU but the send expected a peer GPU"
-                      : status == -4 ? "the receiver could not describe the copy (layout/size mismatch)"
-                      : status == -5 ? "the receiver's copy kernel failed"
-                                     : "the receiver rejected the message";
-    eng_->fail(s, std::string("commux send: ") + why);
+    eng_->fail(s, fin_error(status));
     return;
   }
   if (st && !st->device_wait) eng_->complete(s);
+}
+
+// Blocks the calling thread until the receiver of a device_wait send has
+// enqueued its copy (or failed, or the group aborted), bounded by the group
+// timeout. A wait kernel launched before that point would keep this GPU
+// busy on a copy that is not enqueued yet; a CUDA call of the receiver that
+// waits for its own GPU to go idle (mapping or unmapping peer memory) could
+// then wait, through the peers' spinning kernels, on this very call.
+void CudaTransport::wait_pull_launched(SendState& st) {
+  if (st.launched.load(std::memory_order_acquire) || st.fin.load(std::memory_order_acquire)) return;
+  const auto t0 = std::chrono::steady_clock::now();
+  int spins = 0;
+  while (!st.launched.load(std::memory_order_acquire) && !st.fin.load(std::memory_order_acquire)) {
+    if (eng_->aborted()) throw std::runtime_error("commux send: the group was aborted");
+    if (++spins < 2000) {
+      std::this_thread::yield();
+      continue;
+    }
+    if (std::chrono::steady_clock::now() - t0 > eng_->timeout())
+      throw std::runtime_error("commux send: the receiver did not start the copy within " +
+                               std::to_string(eng_->timeout().count()) + " ms");
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
 }
 
 void CudaTransport::wait_sends_on_stream(const std::vector<ReqPtr>& sends) {
@@ -814,7 +859,12 @@ void CudaTransport::wait_sends_on_stream(const std::vector<ReqPtr>& sends) {
   std::map<int, std::vector<std::shared_ptr<SendState>>> by_dev;
   for (auto& s : sends) {
     auto st = state<SendState>(s);
-    if (st->fin.load(std::memory_order_acquire)) continue;  // consumed already
+    wait_pull_launched(*st);
+    if (st->fin.load(std::memory_order_acquire)) {  // consumed already, or failed
+      const std::int64_t e = st->fin_status.load(std::memory_order_relaxed);
+      if (e != 0) throw std::runtime_error(fin_error(e));
+      continue;
+    }
     by_dev[st->device].push_back(st);
   }
   for (auto& kv : by_dev) {

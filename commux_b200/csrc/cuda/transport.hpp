@@ -134,6 +134,12 @@ struct SendState {
   bool device_wait = false;   // wait() polls the consumed flag on the GPU
   std::uint64_t slot = 0, value = 0;
   std::atomic<bool> fin{false};
+  // device_wait sends: the receiver enqueued the copy that will store the
+  // consumed flag (its FIN with proto::kFinLaunched); a wait kernel is only
+  // launched after that, so no stream ever spins on a copy that is not yet
+  // enqueued (see wait_sends_on_stream)
+  std::atomic<bool> launched{false};
+  std::atomic<std::int64_t> fin_status{0};  // an error FIN's status
   EventPtr local_done;        // self-send: copy finished (same process)
   std::vector<at::Tensor> staged;  // contiguous copies made for the wire
 };
@@ -150,6 +156,7 @@ struct PendingPull {
   ReqPtr r;
   int src = -1;
   std::uint64_t send_id = 0;
+  bool sender_waits = false;  // the sender waits on the device flag (a FIN at launch too)
   DevCtx* ctx = nullptr;
   std::vector<PullDesc> descs;
   std::uint32_t msg_chunks = 0;
@@ -226,6 +233,7 @@ class CudaTransport final : public DeviceTransport {
                    PendingPull& pp);
   void launch_batch(DevCtx* c, std::vector<PendingPull>& pulls, cudaStream_t stream);
   void wait_sends_on_stream(const std::vector<ReqPtr>& sends);
+  void wait_pull_launched(SendState& st);
 
   Engine* eng_;
   std::uint64_t timeout_ns_;
@@ -249,8 +257,9 @@ class CudaTransport final : public DeviceTransport {
   std::vector<PendingPull> pending_;
   struct Flight {
     EventPtr done;
-    std::vector<std::pair<int, std::uint64_t>> fins;
+    std::vector<std::pair<int, std::uint64_t>> fins;  // FINs owed at completion
     std::vector<ReqPtr> reqs;
+    int pulls = 0;  // counted in inflight_
   };
   std::deque<Flight> flights_;
   std::atomic<int> inflight_{0};

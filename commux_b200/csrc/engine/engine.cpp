@@ -1292,7 +1292,8 @@ void Engine::on_fin(int src, const proto::FinRec* rec) {
     auto it = sends_waiting_.find(rec->send_id);
     if (it == sends_waiting_.end()) return;
     s = it->second;
-    sends_waiting_.erase(it);
+    // the copy of a device message was enqueued: its completion FIN follows
+    if (rec->status != proto::kFinLaunched) sends_waiting_.erase(it);
   }
   if (rec->status == -2) {
     fail(s, "commux send: rank " + std::to_string(src) +

@@ -114,8 +114,11 @@ struct DrtsRec {
 struct FinRec {
   shm::WireHdr h;
   std::uint64_t send_id;
-  std::int64_t status;  // 0 ok, else error code
+  std::int64_t status;  // 0 ok, kFinLaunched, else error code (negative)
 };
+// FIN status of a device message whose sender waits on its GPU: the receiver
+// has enqueued the copy (a second FIN with status 0 follows its completion)
+constexpr std::int64_t kFinLaunched = 1;
 
 struct AbortRec {
   shm::WireHdr h;

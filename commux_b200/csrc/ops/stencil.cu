@@ -14,6 +14,7 @@
 #include <cuda_runtime.h>
 #include <torch/extension.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdint>
 #include <cstdlib>
@@ -32,14 +33,15 @@ std::atomic<std::int64_t> g_launches{0};
 template <typename T>
 __global__ void __launch_bounds__(kTX* kTY)
     jacobi7_kernel(const T* __restrict__ u, T* __restrict__ v, int nz, int ny, int nx, int h,
-                   int iz, int iy, int ix, double* __restrict__ residual) {
+                   stencil::SubBox sb, double* __restrict__ residual) {
   __shared__ T plane[kTY + 2][kTX + 2];
   __shared__ double red[kTX * kTY / 32];
   const int tx = threadIdx.x, ty = threadIdx.y;
-  const int x = h + blockIdx.x * kTX + tx;  // interior coordinates offset by the halo
-  const int y = h + blockIdx.y * kTY + ty;
-  const int z0 = h + blockIdx.z * kZB;
-  const int z1 = min(z0 + kZB, h + iz);
+  const int x = h + sb.ox + blockIdx.x * kTX + tx;  // padded coordinates
+  const int y = h + sb.oy + blockIdx.y * kTY + ty;
+  const int z0 = h + sb.oz + blockIdx.z * kZB;
+  const int z1 = min(z0 + kZB, h + sb.oz + sb.ez);
+  const int ix = sb.ox + sb.ex, iy = sb.oy + sb.ey;  // end of the box (interior coordinates)
   const bool active = x < h + ix && y < h + iy;
   const std::int64_t sy = nx, sz = static_cast<std::int64_t>(ny) * nx;
   const std::int64_t col = static_cast<std::int64_t>(y) * sy + x;
@@ -76,6 +78,68 @@ __global__ void __launch_bounds__(kTX* kTY)
     __syncthreads();
     if (warp == 0) {
       acc = lane < kTX * kTY / 32 ? red[lane] : 0.0;
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
+      if (lane == 0) atomicAdd(residual, acc);
+    }
+  }
+}
+
+// The interior's one-cell boundary layer: the cells whose 7-point stencil
+// reads a ghost cell, i.e. what a core sub-box update (origin 1, extent
+// n - 2 per dim) leaves out. One thread per cell over six slabs: z = 0 and
+// z = iz-1 (all y, x), y = 0 and y = iy-1 (z inside, all x), x = 0 and
+// x = ix-1 (z and y inside). Needs iz, iy, ix >= 3.
+template <typename T>
+__global__ void __launch_bounds__(256)
+    jacobi7_shell_kernel(const T* __restrict__ u, T* __restrict__ v, int ny, int nx, int h, int iz, int iy,
+                         int ix, double* __restrict__ residual) {
+  __shared__ double red[8];
+  const std::int64_t A = static_cast<std::int64_t>(iy) * ix;         // z slab
+  const std::int64_t B = static_cast<std::int64_t>(iz - 2) * ix;     // y slab
+  const std::int64_t C = static_cast<std::int64_t>(iz - 2) * (iy - 2);  // x slab
+  const std::int64_t total = 2 * (A + B + C);
+  const std::int64_t sy = nx, sz = static_cast<std::int64_t>(ny) * nx;
+  double acc = 0.0;
+  for (std::int64_t t = blockIdx.x * static_cast<std::int64_t>(blockDim.x) + threadIdx.x; t < total;
+       t += static_cast<std::int64_t>(gridDim.x) * blockDim.x) {
+    int z, y, x;
+    std::int64_t r = t;
+    if (r < 2 * A) {
+      const int slab = static_cast<int>(r / A);
+      r -= slab * A;
+      z = slab ? iz - 1 : 0;
+      y = static_cast<int>(r / ix);
+      x = static_cast<int>(r - static_cast<std::int64_t>(y) * ix);
+    } else if ((r -= 2 * A) < 2 * B) {
+      const int slab = static_cast<int>(r / B);
+      r -= slab * B;
+      y = slab ? iy - 1 : 0;
+      z = 1 + static_cast<int>(r / ix);
+      x = static_cast<int>(r - static_cast<std::int64_t>(z - 1) * ix);
+    } else {
+      r -= 2 * B;
+      const int slab = static_cast<int>(r / C);
+      r -= slab * C;
+      x = slab ? ix - 1 : 0;
+      z = 1 + static_cast<int>(r / (iy - 2));
+      y = 1 + static_cast<int>(r - static_cast<std::int64_t>(z - 1) * (iy - 2));
+    }
+    const std::int64_t o = (z + h) * sz + (y + h) * sy + (x + h);
+    const T ctr = u[o];
+    // same summation order as the tiled kernels (z, then x, then y), so a
+    // core + shell update equals the whole-interior one bit for bit
+    const T nv = (u[o - sz] + u[o + sz] + u[o - 1] + u[o + 1] + u[o - sy] + u[o + sy]) / T(6);
+    v[o] = nv;
+    const double d = static_cast<double>(nv) - static_cast<double>(ctr);
+    acc += d * d;
+  }
+  if (residual != nullptr) {
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) red[warp] = acc;
+    __syncthreads();
+    if (warp == 0) {
+      acc = lane < 8 ? red[lane] : 0.0;
       for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
       if (lane == 0) atomicAdd(residual, acc);
     }
@@ -123,7 +187,7 @@ EncodeTiledFn encode_tiled() {
 }
 
 template <typename T>
-void launch_tma(const at::Tensor& u, at::Tensor& v, int nz, int ny, int nx, int h, int iz, int iy, int ix,
+void launch_tma(const at::Tensor& u, at::Tensor& v, int nz, int ny, int nx, int h, stencil::SubBox sb,
                 double* res, cudaStream_t stream) {
   using B = stencil::Box<T>;
   CUtensorMap map;
@@ -150,10 +214,10 @@ void launch_tma(const at::Tensor& u, at::Tensor& v, int nz, int ny, int nx, int 
     const char* e = std::getenv("COMMUX_KERNEL_WAIT_MS");
     return static_cast<std::uint64_t>(e ? std::atoll(e) : 2000) * 1000000ull;
   }();
-  dim3 grid((ix + stencil::kTX - 1) / stencil::kTX, (iy + stencil::kTY - 1) / stencil::kTY,
-            (iz + stencil::kZB - 1) / stencil::kZB);
+  dim3 grid((sb.ex + stencil::kTX - 1) / stencil::kTX, (sb.ey + stencil::kTY - 1) / stencil::kTY,
+            (sb.ez + stencil::kZB - 1) / stencil::kZB);
   stencil::jacobi7_tma_kernel<T><<<grid, stencil::kThreads, B::kSmem, stream>>>(
-      map, v.data_ptr<T>(), nz, ny, nx, h, iz, iy, ix, res, st_dev, limit_ns);
+      map, v.data_ptr<T>(), nz, ny, nx, h, sb, res, st_dev, limit_ns);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -166,8 +230,12 @@ int64_t kernel_status(bool reset) {
   return v;
 }
 
-// v[interior] = jacobi(u); residual (optional, fp64 scalar on the device) += sum (v-u)^2
-void jacobi7(const at::Tensor& u, at::Tensor& v, int64_t halo, c10::optional<at::Tensor> residual) {
+// v[interior] = jacobi(u); residual (optional, fp64 scalar on the device) += sum (v-u)^2.
+// part 0: the whole interior; 1: its core (cells whose stencil reads no ghost
+// cell); 2: the one-cell boundary layer around the core. Parts 1 and 2
+// together write exactly what part 0 writes.
+void jacobi7(const at::Tensor& u, at::Tensor& v, int64_t halo, c10::optional<at::Tensor> residual,
+             int64_t part) {
   TORCH_CHECK(u.is_cuda() && v.is_cuda(), "jacobi7: CUDA tensors");
   TORCH_CHECK(u.dim() == 3 && u.sizes() == v.sizes(), "jacobi7: matching 3-D fields");
   TORCH_CHECK(u.is_contiguous() && v.is_contiguous(), "jacobi7: contiguous fields");
@@ -182,28 +250,51 @@ void jacobi7(const at::Tensor& u, at::Tensor& v, int64_t halo, c10::optional<at:
                 "jacobi7: residual must be a CUDA float64 tensor");
     res = residual->data_ptr<double>();
   }
+  TORCH_CHECK(part >= 0 && part <= 2, "jacobi7: part is 0 (all), 1 (core) or 2 (shell)");
+  TORCH_CHECK(part == 0 || (iz >= 3 && iy >= 3 && ix >= 3), "jacobi7: a core/shell split needs an interior of "
+              "at least 3 points per dim");
   c10::cuda::CUDAGuard g(u.device());
   auto stream = c10::cuda::getCurrentCUDAStream(u.device().index()).stream();
+  if (part == 2) {
+    const std::int64_t cells = 2 * (static_cast<std::int64_t>(iy) * ix + static_cast<std::int64_t>(iz - 2) * ix +
+                                    static_cast<std::int64_t>(iz - 2) * (iy - 2));
+    int sms = 0;
+    C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, u.device().index()));
+    const int blocks = static_cast<int>(std::min<std::int64_t>((cells + 255) / 256, 8ll * sms));
+    if (u.scalar_type() == at::kDouble)
+      jacobi7_shell_kernel<double><<<blocks, 256, 0, stream>>>(u.data_ptr<double>(), v.data_ptr<double>(), ny, nx,
+                                                               h, iz, iy, ix, res);
+    else if (u.scalar_type() == at::kFloat)
+      jacobi7_shell_kernel<float><<<blocks, 256, 0, stream>>>(u.data_ptr<float>(), v.data_ptr<float>(), ny, nx, h,
+                                                              iz, iy, ix, res);
+    else
+      TORCH_CHECK(false, "jacobi7: float32 or float64 fields");
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    g_launches++;
+    return;
+  }
+  const stencil::SubBox sb = part == 1 ? stencil::SubBox{1, 1, 1, iz - 2, iy - 2, ix - 2}
+                                       : stencil::SubBox{0, 0, 0, iz, iy, ix};
   const bool tma_ok = (static_cast<std::int64_t>(nx) * u.element_size()) % 16 == 0 &&
                       (reinterpret_cast<std::uintptr_t>(u.data_ptr()) & 15u) == 0 && ix >= 1;
   if (tma_ok && !use_simple()) {
     if (u.scalar_type() == at::kDouble)
-      launch_tma<double>(u, v, nz, ny, nx, h, iz, iy, ix, res, stream);
+      launch_tma<double>(u, v, nz, ny, nx, h, sb, res, stream);
     else if (u.scalar_type() == at::kFloat)
-      launch_tma<float>(u, v, nz, ny, nx, h, iz, iy, ix, res, stream);
+      launch_tma<float>(u, v, nz, ny, nx, h, sb, res, stream);
     else
       TORCH_CHECK(false, "jacobi7: float32 or float64 fields");
     g_launches++;
     return;
   }
   dim3 block(kTX, kTY);
-  dim3 grid((ix + kTX - 1) / kTX, (iy + kTY - 1) / kTY, (iz + kZB - 1) / kZB);
+  dim3 grid((sb.ex + kTX - 1) / kTX, (sb.ey + kTY - 1) / kTY, (sb.ez + kZB - 1) / kZB);
   if (u.scalar_type() == at::kDouble)
     jacobi7_kernel<double><<<grid, block, 0, stream>>>(u.data_ptr<double>(), v.data_ptr<double>(), nz, ny,
-                                                       nx, h, iz, iy, ix, res);
+                                                       nx, h, sb, res);
   else if (u.scalar_type() == at::kFloat)
     jacobi7_kernel<float><<<grid, block, 0, stream>>>(u.data_ptr<float>(), v.data_ptr<float>(), nz, ny, nx,
-                                                      h, iz, iy, ix, res);
+                                                      h, sb, res);
   else
     TORCH_CHECK(false, "jacobi7: float32 or float64 fields");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -216,7 +307,8 @@ int64_t launches() { return g_launches.load(); }
 
 PYBIND11_MODULE(_ops, m) {
   m.doc() = "commux_b200 compute kernels (sm_100a)";
-  m.def("jacobi7", &jacobi7, py::arg("u"), py::arg("v"), py::arg("halo"), py::arg("residual") = py::none());
+  m.def("jacobi7", &jacobi7, py::arg("u"), py::arg("v"), py::arg("halo"), py::arg("residual") = py::none(),
+        py::arg("part") = 0);
   m.def("launches", &launches);
   m.def("kernel_status", &kernel_status, py::arg("reset") = false);
 }

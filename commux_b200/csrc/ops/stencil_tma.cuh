@@ -98,10 +98,18 @@ __device__ __forceinline__ void box_x(int h, int bx, int& x0, int& shift) {
   shift = want - x0;
 }
 
+// Output sub-box of the interior: origin (oz, oy, ox) and extent (ez, ey, ex)
+// in interior coordinates (the whole interior: origin 0, extent iz/iy/ix).
+// A sub-box lets the core of the field (cells whose stencil reads no ghost
+// cell) be updated while the halo exchange is still filling the ghosts.
+struct SubBox {
+  int oz, oy, ox, ez, ey, ex;
+};
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads) jacobi7_tma_kernel(const __grid_constant__ CUtensorMap umap,
                                                                 T* __restrict__ v, int nz, int ny, int nx,
-                                                                int h, int iz, int iy, int ix,
+                                                                int h, SubBox sb,
                                                                 double* __restrict__ residual,
                                                                 unsigned* __restrict__ status,
                                                                 std::uint64_t limit_ns) {
@@ -112,10 +120,10 @@ __global__ void __launch_bounds__(kThreads) jacobi7_tma_kernel(const __grid_cons
 
   const int bx = blockIdx.x, by = blockIdx.y;
   int x0, shift;
-  box_x<T>(h, bx, x0, shift);
-  const int y0 = h - 1 + by * kTY;
-  const int zs = h + blockIdx.z * kZB;                 // first output plane
-  const int nout = min(kZB, h + iz - zs);              // output planes of this CTA
+  box_x<T>(h + sb.ox, bx, x0, shift);
+  const int y0 = h + sb.oy - 1 + by * kTY;
+  const int zs = h + sb.oz + blockIdx.z * kZB;         // first output plane
+  const int nout = min(kZB, h + sb.oz + sb.ez - zs);   // output planes of this CTA
   const int nload = nout + 2;                          // input planes z-1 .. z+nout
   const int tid = threadIdx.x;
 
@@ -132,7 +140,7 @@ __global__ void __launch_bounds__(kThreads) jacobi7_tma_kernel(const __grid_cons
   }
   // thread -> (row ty, columns tx + 16k)
   const int ty = tid / 16, tx = tid % 16;
-  const int gy = h + by * kTY + ty;
+  const int gy = h + sb.oy + by * kTY + ty;
   double acc = 0.0;
   bool ok = true;
   int done_iters = 0;  // iterations that freed their buffer
@@ -151,12 +159,12 @@ __global__ void __launch_bounds__(kThreads) jacobi7_tma_kernel(const __grid_cons
     const T* zp = plane((i + 2) % kStages);
     const int z = zs + i;
     const int r = ty + 1;
-    if (gy < h + iy) {
+    if (gy < h + sb.oy + sb.ey) {
 #pragma unroll
       for (int k = 0; k < kTX / 16; ++k) {
         const int lx = tx + 16 * k;
-        const int gx = h + bx * kTX + lx;
-        if (gx < h + ix) {
+        const int gx = h + sb.ox + bx * kTX + lx;
+        if (gx < h + sb.ox + sb.ex) {
           const int c = shift + 1 + lx;
           const T ctr = zc[r * B::kW + c];
           const T s = zm[r * B::kW + c] + zp[r * B::kW + c] + zc[r * B::kW + c - 1] +

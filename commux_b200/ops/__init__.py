@@ -19,12 +19,21 @@ def _need_native():
     return _native
 
 
-def jacobi7(u: torch.Tensor, v: torch.Tensor, halo: int, residual: torch.Tensor | None = None) -> None:
+_PARTS = {"all": 0, "core": 1, "shell": 2}
+
+
+def jacobi7(u: torch.Tensor, v: torch.Tensor, halo: int, residual: torch.Tensor | None = None,
+            part: str = "all") -> None:
     """v[interior] = mean of the 6 face neighbours of u; residual += sum((v-u)^2).
+
+    ``part`` selects the cells: "all" (the interior), "core" (cells whose
+    stencil reads no ghost cell, so it may run while the halo exchange fills
+    the ghosts) or "shell" (the one-cell layer around the core). "core" and
+    "shell" together write exactly what "all" writes.
 
     CUDA only (sm_100a kernel); fails loudly if the extension is missing.
     """
-    _need_native().jacobi7(u, v, halo, residual)
+    _need_native().jacobi7(u, v, halo, residual, _PARTS[part])
 
 
 def launches() -> int:

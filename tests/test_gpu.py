@@ -70,6 +70,38 @@ def topology(mode, world, expect):
     return dict(CUDA, CMX_SHARED_GPU="1", CMX_EXPECT=expect[1])
 
 
+@pytest.mark.parametrize("dtype", [torch.float64, torch.float32])
+@pytest.mark.parametrize("shape", [(20, 20, 20), (37, 45, 71), (132, 68, 36), (7, 9, 11)])
+def test_jacobi7_core_plus_shell_is_whole(dtype, shape):
+    # the overlapped step's two updates write exactly the whole-interior update
+    from commux_b200.ops import jacobi7, jacobi7_reference
+
+    h = 2
+    g = torch.Generator().manual_seed(5)
+    u = (torch.rand(shape, generator=g, dtype=torch.float64) * 2 - 1).to(dtype).cuda()
+    whole, parts = torch.zeros_like(u), torch.zeros_like(u)
+    r_whole = torch.zeros(1, dtype=torch.float64, device="cuda")
+    r_parts = torch.zeros(1, dtype=torch.float64, device="cuda")
+    jacobi7(u, whole, h, r_whole)
+    jacobi7(u, parts, h, r_parts, part="core")
+    core_only = parts.clone()
+    jacobi7(u, parts, h, r_parts, part="shell")
+    torch.cuda.synchronize()
+    assert torch.equal(whole, parts)
+    # the core part leaves the one-cell boundary layer alone
+    assert float(core_only[h, h:-h, h:-h].abs().sum()) == 0.0
+    assert float(core_only[h:-h, h:-h, -h - 1].abs().sum()) == 0.0
+    v_ref = torch.zeros(shape, dtype=torch.float64)
+    r_ref = jacobi7_reference(u.double().cpu(), v_ref, h)
+    tol = 1e-12 if dtype == torch.float64 else 1e-5
+    assert torch.allclose(parts.double().cpu()[h:-h, h:-h, h:-h], v_ref[h:-h, h:-h, h:-h], rtol=tol, atol=tol)
+    assert abs(float(r_parts) - float(r_whole)) <= 1e-9 * max(1.0, abs(r_ref))
+
+
+def test_overlapped_steps_match_sequential():
+    check(run("halo_overlap.py", 1, env=CUDA, timeout=240))
+
+
 def test_p2p_self_sends():
     check(run("gpu_p2p.py", 1, env=CUDA))
 
@@ -117,6 +149,9 @@ COLL_VARIANTS = {
     "nvls": ({"COMMUX_NVLS_MIN_RANKS": "2", "COMMUX_NVLS_MIN_BYTES": "0"}, "coll_nvls_enabled==1,coll_nvls>0"),
     "p2p": ({"COMMUX_NVLS": "0"}, "coll_nvls_enabled==0,coll_nvls==0,coll_oneshot>0,coll_twoshot>0"),
     "twoshot": ({"COMMUX_NVLS": "0", "COMMUX_ALGO": "twoshot"}, "coll_oneshot==0,coll_twoshot>0"),
+    # a 1 MiB workspace: every two-shot reduction and broadcast runs through
+    # dozens of double-buffered chunks (pipeline fill, steady state, drain)
+    "pipeline": ({"COMMUX_NVLS": "0", "COMMUX_CUDA_WS_BYTES": "1048576"}, "coll_twoshot>0"),
 }
 
 
@@ -144,7 +179,7 @@ def test_device_barrier_orders_device_work():
 def test_device_barrier_times_out_without_peer():
     # rank 1 never joins: rank 0's bounded wait runs out (1 s), the kernel
     # records it and returns, the call raises; plain peer loads, no NVLS
-    env = topology("peer", 2, ("coll_barriers>0", None))
+    env = topology("peer", 2, ("coll_shared_gpu==0", None))
     env.update(CMX_BARRIER_MODE="timeout", COMMUX_DEVICE_TIMEOUT_MS="1000", COMMUX_NVLS="0",
                NCCL_NVLS_ENABLE="0")
     check(run("gpu_barrier.py", 2, env=env, timeout=180))

@@ -18,6 +18,8 @@ import time
 
 from common import Checker, init, torch, dist
 
+import commux_b200 as commux
+
 rank, world, dev = init(timeout_s=120)
 c = Checker(rank)
 mode = os.environ.get("CMX_BARRIER_MODE", "order")
@@ -28,6 +30,10 @@ t = torch.ones(4, device=dev)
 dist.all_reduce(t)
 c.check("set-up all_reduce", float(t[0]) == world)
 
+class IpcHandle(ctypes.Structure):  # CUipcMemHandle, passed by value
+    _fields_ = [("reserved", ctypes.c_char * 64)]
+
+
 if mode == "order":
     cuda = ctypes.CDLL("libcuda.so.1")
     n = 1 << 20
@@ -36,18 +42,19 @@ if mode == "order":
     # export this rank's allocation (base + offset) through CUDA IPC
     base, size = ctypes.c_uint64(), ctypes.c_size_t()
     assert cuda.cuMemGetAddressRange_v2(ctypes.byref(base), ctypes.byref(size), ctypes.c_uint64(x.data_ptr())) == 0
-    handle = (ctypes.c_char * 64)()
-    assert cuda.cuIpcGetMemHandle(handle, base) == 0
+    handle = IpcHandle()
+    assert cuda.cuIpcGetMemHandle(ctypes.byref(handle), base) == 0
     store.set(f"barrier/ipc/{rank}", bytes(handle) + (x.data_ptr() - base.value).to_bytes(8, "little"))
     peers, mapped = {}, []
     for p in range(world):
         if p == rank:
             continue
         blob = store.get(f"barrier/ipc/{p}")
-        h = (ctypes.c_char * 64).from_buffer_copy(blob[:64])
+        h = IpcHandle.from_buffer_copy(blob[:64])
         ptr = ctypes.c_uint64()
         # CU_IPC_MEM_LAZY_ENABLE_PEER_ACCESS
-        assert cuda.cuIpcOpenMemHandle_v2(ctypes.byref(ptr), h, ctypes.c_uint(1)) == 0
+        rc = cuda.cuIpcOpenMemHandle_v2(ctypes.byref(ptr), h, ctypes.c_uint(1))
+        assert rc == 0, f"cuIpcOpenMemHandle: {rc}"
         mapped.append(ptr.value)
         peers[p] = ptr.value + int.from_bytes(blob[64:72], "little")
     dist.barrier()  # every mapping is open
@@ -86,6 +93,7 @@ elif mode == "timeout":
         # the context still works
         y = torch.arange(8.0, device=dev) * 2
         c.check("context usable after the timeout", float(y.sum()) == 56.0)
+        c.check("the device barrier ran", commux.stats().get("coll_barriers", 0) > 0, str(commux.stats()))
         store.set("barrier/timeout/done", b"1")
     else:
         store.wait(["barrier/timeout/done"])
