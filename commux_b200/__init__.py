@@ -145,18 +145,20 @@ def batch_p2p(sends=(), recvs=(), group=None):
                         [t for t, _, _ in s], [int(p) for _, p, _ in s], [int(g) for _, _, g in s])
 
 
-def p2p_plan(sends=(), recvs=(), group=None):
+def p2p_plan(sends=(), recvs=(), group=None, max_ctas=0):
     """Persistent plan of CUDA sends and receives, matched once.
 
     ``sends``/``recvs`` are ``(tensor, peer, tag)`` like :func:`batch_p2p`.
     ``plan.start()`` enqueues one exchange of the same buffers on the current
     stream as one CUDA graph: a pull launch that stores this rank's "ready"
-    signals, packs narrow rows for peers on other GPUs, and copies every
-    receive (waiting on the peers' ready flags on the device), then -- when
-    peers on other GPUs read this rank's data -- a wait launch for their
+    signals, packs narrow rows for peers on other GPUs and copies every
+    receive (waiting on the peers' ready flags on the device); when peers on
+    other GPUs read this rank's data, its last CTA waits for their
     "consumed" flags. No host matching and no host round trip per step.
     Every rank the plan talks to creates its side in the same order and calls
     start() the same number of times (the analogue of MPI_Startall).
+    ``max_ctas`` (or ``plan.set_max_ctas``) caps the launches' grid, leaving
+    SMs to kernels that run beside the exchange.
     """
     group = group if group is not None else dist.distributed_c10d._get_default_group()
     r = list(recvs)
@@ -165,8 +167,11 @@ def p2p_plan(sends=(), recvs=(), group=None):
         raise ValueError("commux.p2p_plan: no sends and no receives")
     first = (r + s)[0][0]
     backend = group._get_backend(first.device)
-    return _C.p2p_plan(backend, [t for t, _, _ in r], [int(p) for _, p, _ in r], [int(g) for _, _, g in r],
+    plan = _C.p2p_plan(backend, [t for t, _, _ in r], [int(p) for _, p, _ in r], [int(g) for _, _, g in r],
                        [t for t, _, _ in s], [int(p) for _, p, _ in s], [int(g) for _, _, g in s])
+    if max_ctas:
+        plan.set_max_ctas(int(max_ctas))
+    return plan
 
 
 def transports(group=None) -> list:

@@ -185,12 +185,10 @@ CollImpl::CollImpl(CudaTransport* tr, int dev)
 }
 
 // COMMUX_COLL_TRACE=1: after each collective (synchronously), one line per
-// call with the phase durations of CTA 0, averaged over the iterations of
-// the two-shot pipeline: wait-B = the peers' flags of chunk c-2, push =
-// stores of chunk c into the peers' workspaces, wait-A = the peers' flags
-// of chunk c-1, fold+push2 = fold of chunk c-1 and its stores out, out =
-// copy-out of chunk c-2, flags = the flag stores (they wait until this CTA's
-// stores have landed), tail = the last copy-out.
+// call with the phase durations of CTA 0, averaged over the chunks: push =
+// stores into peers' workspaces, sig = the flag store (waits for those
+// stores to land), wait = until every peer's flag arrived, fold, push2 =
+// folded segment out, wait2, out = copy-out.
 void CollImpl::report_trace(int algo, int mode, std::int64_t bytes, int ctas) {
   CMX_CUDA(cudaStreamSynchronize(stream_));
   const unsigned long long* t = trace_h_;
@@ -213,9 +211,8 @@ void CollImpl::report_trace(int algo, int mode, std::int64_t bytes, int ctas) {
     break;
   }
   std::fprintf(stderr,
-               "[commux trace rank %d] algo %d mode %d bytes %lld ctas %d chunks %d total %.1f us | per chunk "
-               "(two-shot iteration): wait-B %.1f push %.1f wait-A %.1f fold+push2 %.1f out %.1f flags %.1f "
-               "tail %.1f\n",
+               "[commux trace rank %d] algo %d mode %d bytes %lld ctas %d chunks %d total %.1f us | per chunk: "
+               "push %.1f sig %.1f wait %.1f fold %.1f push2 %.1f wait2 %.1f out %.1f\n",
                me_, algo, mode, static_cast<long long>(bytes), ctas, nch, total, sum[1] / nch, sum[2] / nch,
                sum[3] / nch, sum[4] / nch, sum[5] / nch, sum[6] / nch, sum[7] / nch);
 }

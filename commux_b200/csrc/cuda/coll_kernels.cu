@@ -25,16 +25,22 @@
 // Kernels:
 //   oneshot  (small allreduce/reduce): push my data into slot[me] of every
 //            rank's A, one flag round, fold the P slots locally.
-//   twoshot  (large allreduce/reduce/reduce_scatter), software-pipelined
-//            over chunks: push segment s of chunk c into slot[me] of rank
-//            s's A (reduce-scatter by writes) while folding my segment of
-//            chunk c-1 (its own part read from the input) and pushing it
-//            into slot[me] of B on every rank that needs it, and copying
-//            chunk c-2 out; A and B are double-buffered by chunk parity.
-//   gather   (allgather), chunked: push my block into slot[me] of every
-//            rank's B, flag round, copy out, flag round.
-//   bcast    (broadcast): scatter from the root + allgather among the
-//            ranks, pipelined over double-buffered chunks (see bcast_kernel).
+//   twoshot  (large allreduce/reduce/reduce_scatter), chunk by chunk, the
+//            phases of a chunk in sequence within each CTA: push segment s of
+//            the chunk into slot[me] of rank s's A (reduce-scatter by
+//            writes), flag round, rank s folds its segment (its own part read
+//            from its input) and pushes it into slot[s] of B on every rank
+//            that needs it, flag round, copy out. (A software pipeline over
+//            half-size, double-buffered chunks, which folded chunk c-1 while
+//            chunk c crossed NVLink, measured 14 % slower at 1 GiB on 2 GPUs:
+//            its flag stores still waited for every store to land, and NVLink
+//            idled during the flag waits.)
+//   gather   (allgather/broadcast at 2 ranks), chunked: push my block into
+//            slot[me] of every rank's B (broadcast: the root's block into
+//            slot 0), flag round, copy out, flag round.
+//   bcast    (broadcast from 3 ranks): scatter from the root + allgather
+//            among the ranks, pipelined over double-buffered chunks (see
+//            bcast_kernel).
 //   barrier  one CTA: a system-scope fence (everything this rank's stream
 //            wrote before the barrier, local or into a peer's memory, is
 //            visible system-wide), a flag to every rank, a bounded wait for
@@ -435,21 +441,6 @@ __device__ __forceinline__ void stamp(const CollArgs& a, std::int64_t c, int k) 
     a.trace[c * kTracePoints + k] = globaltimer_ns();
 }
 
-// Software-pipelined over chunks. Each call's half of A and of B is split
-// into two quarters by chunk parity (chunk c uses quarter c & 1, P slots of
-// `cap` elements). Iteration c of every CTA:
-//   0. wait: every rank's phase-1 flag of chunk c-2 (it folded chunk c-2 out
-//      of its A quarter c & 1 and copied chunk c-2 out of its B quarter)
-//   1. push my parts of chunk c into slot[me] of each owner's A quarter
-//   2. wait phase-0 flags of chunk c-1, fold my segment of chunk c-1 and
-//      push it into slot[me] of the B quarter of every rank that needs it
-//   3. copy chunk c-2 out of my B quarter
-//   4. flags: phase 0 of chunk c (its pushes, and my copy-out of c-2),
-//      phase 1 of chunk c-1 (its fold and pushes)
-// The flag stores are releases at system scope: they wait until this CTA's
-// posted stores to the peers have landed. Issuing them after the fold and
-// the copy-out lets that local HBM work run while chunk c's stores cross
-// NVLink, instead of after them.
 template <typename T, int OP>
 __global__ void __launch_bounds__(kCollThreads, 2) twoshot_kernel(const __grid_constant__ CollArgs a) {
   constexpr int N = Packs<T>::N;
@@ -457,79 +448,63 @@ __global__ void __launch_bounds__(kCollThreads, 2) twoshot_kernel(const __grid_c
   T* out = static_cast<T*>(a.out);
   const int P = a.P;
   const bool rs = a.mode == kModeReduceScatter;
-  const bool red = a.mode == kModeReduce;
-  const std::int64_t cap = slot_elems<T>(a, 2 * P);
+  const std::int64_t seg_cap = slot_elems<T>(a, P);
   const std::int64_t total = rs ? a.n * P : a.n;
   // segment s of the tensor: [s*seg, s*seg + seg) (reduce_scatter: block s)
   const std::int64_t seg = rs ? a.n : (((total + P - 1) / P + N - 1) / N) * N;
-  const std::int64_t nchunks = (seg + cap - 1) / cap;
-  const bool to_out = rs || a.mode == kModeAllreduce || a.me == a.root;
-  const bool copies_out = !rs && !(red && a.me != a.root);
-  auto quarter_a = [&](int p, std::int64_t c) { return region_a<T>(a, p) + (c & 1) * P * cap; };
-  auto quarter_b = [&](int p, std::int64_t c) { return region_b<T>(a, p) + (c & 1) * P * cap; };
-  auto seq = [&](std::int64_t c) { return a.seq_base + static_cast<std::uint64_t>(c) + 1; };
-  // this CTA's piece [lo, hi) of chunk c and the chunk's offset s0 in a segment
-  auto span = [&](std::int64_t c, std::int64_t& s0, std::int64_t& lo, std::int64_t& hi) {
-    s0 = c * cap;
-    piece<T>(min(cap, seg - s0), gridDim.x, blockIdx.x, lo, hi);
-  };
-  auto copy_out = [&](std::int64_t c) {
-    std::int64_t s0, lo, hi;
-    span(c, s0, lo, hi);
-    for (int q = 1; q < P; ++q) {
-      const int p = (a.me + q) % P;
-      const std::int64_t g = static_cast<std::int64_t>(p) * seg + s0;
-      copy_range(out + g, quarter_b(a.me, c) + p * cap, lo, min(hi, total - g));
-    }
-  };
-  for (std::int64_t c = 0; c <= nchunks; ++c) {
+  const std::int64_t nchunks = (seg + seg_cap - 1) / seg_cap;
+  T* a_me = region_a<T>(a, a.me);
+  T* b_me = region_b<T>(a, a.me);
+  for (std::int64_t c = 0; c < nchunks; ++c) {
+    const std::int64_t s0 = c * seg_cap;
+    const std::int64_t slen = min(seg_cap, seg - s0);
+    std::int64_t lo, hi;
+    piece<T>(slen, gridDim.x, blockIdx.x, lo, hi);
+    const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
     stamp(a, c, 0);
-    if (c >= 2 && !await(a, 1, seq(c - 2))) return;
+    // phase 0: my part of segment s -> slot[me] of rank s's A (my own
+    // segment's part stays in `in` and is read from there by the fold)
+    for (int q = 1; q < P; ++q) {
+      const int s = (a.me + q) % P;
+      const std::int64_t g = static_cast<std::int64_t>(s) * seg + s0;
+      const std::int64_t ghi = rs ? g + hi : min(g + hi, total);
+      copy_range(region_a<T>(a, s) + a.me * seg_cap - g, in, g + lo, ghi);
+    }
     stamp(a, c, 1);
-    if (c < nchunks) {
-      std::int64_t s0, lo, hi;
-      span(c, s0, lo, hi);
-      // my part of segment s -> slot[me] of rank s's A quarter (my own
-      // segment's part stays in `in`; the fold reads it from there)
-      for (int q = 1; q < P; ++q) {
-        const int s = (a.me + q) % P;
-        const std::int64_t g = static_cast<std::int64_t>(s) * seg + s0;
-        const std::int64_t ghi = rs ? g + hi : min(g + hi, total);
-        copy_range(quarter_a(s, c) + a.me * cap - g, in, g + lo, ghi);
-      }
-    }
+    signal(a, 0, seq);
     stamp(a, c, 2);
-    if (c >= 1) {
-      const std::int64_t f = c - 1;
-      std::int64_t s0, lo, hi;
-      span(f, s0, lo, hi);
-      if (!await(a, 0, seq(f))) return;
-      stamp(a, c, 3);
-      // reduce_scatter and allreduce fold straight into `out` (allreduce
-      // then pushes from there); reduce folds into my B slot, except at root
-      const std::int64_t mine = static_cast<std::int64_t>(a.me) * seg + s0;
-      const std::int64_t mhi = rs ? hi : min(hi, total - mine);
-      T* folded = to_out ? (rs ? out + s0 : out + mine) : quarter_b(a.me, f) + a.me * cap;
-      gfold<T, OP>(Grp{0, 0, static_cast<int>(blockDim.x)}, folded, quarter_a(a.me, f), cap, P, a.me,
-                   in + mine, lo, mhi);
-      if (!rs) {
-        __syncthreads();
-        for (int q = 1; q < P; ++q) {
-          const int p = (a.me + q) % P;
-          if (red && p != a.root) continue;
-          copy_range(quarter_b(p, f) + a.me * cap, folded, lo, mhi);
-        }
+    if (!await(a, 0, seq)) return;
+    stamp(a, c, 3);
+    // fold my segment: reduce_scatter and allreduce write it straight into
+    // `out` (allreduce then pushes it from there), reduce into my B slot
+    const std::int64_t mine = static_cast<std::int64_t>(a.me) * seg + s0;
+    const std::int64_t mhi = rs ? hi : min(hi, total - mine);
+    const bool to_out = rs || a.mode == kModeAllreduce || a.me == a.root;
+    T* folded = to_out ? (rs ? out + s0 : out + mine) : b_me + a.me * seg_cap;
+    gfold<T, OP>(Grp{0, 0, static_cast<int>(blockDim.x)}, folded, a_me, seg_cap, P, a.me, in + mine, lo, mhi);
+    stamp(a, c, 4);
+    if (!rs) {
+      __syncthreads();
+      // phase 1: my folded segment -> slot[me] of B on every rank that needs it
+      for (int q = 1; q < P; ++q) {
+        const int p = (a.me + q) % P;
+        if (a.mode == kModeReduce && p != a.root) continue;
+        copy_range(region_b<T>(a, p) + a.me * seg_cap, folded, lo, mhi);
       }
     }
-    stamp(a, c, 4);
-    if (c >= 2 && copies_out) copy_out(c - 2);
     stamp(a, c, 5);
-    if (c < nchunks) signal(a, 0, seq(c));
-    if (c >= 1) signal(a, 1, seq(c - 1));
+    signal(a, 1, seq);
+    if (!await(a, 1, seq)) return;
     stamp(a, c, 6);
+    if (rs || (a.mode == kModeReduce && a.me != a.root)) continue;
+    for (int p = 0; p < P; ++p) {
+      if (p == a.me) continue;  // folded in place above
+      const std::int64_t g = static_cast<std::int64_t>(p) * seg + s0;
+      const std::int64_t phi = min(hi, total - g);
+      copy_range(out + g, b_me + p * seg_cap - 0, lo, phi);
+    }
+    stamp(a, c, 7);
   }
-  if (nchunks >= 1 && await(a, 1, seq(nchunks - 1)) && copies_out) copy_out(nchunks - 1);
-  stamp(a, nchunks + 1, 7);
 }
 
 // ---- barrier ---------------------------------------------------------------------
@@ -552,7 +527,8 @@ __global__ void __launch_bounds__(kCollThreads, 2) gather_kernel(const __grid_co
   const T* in = static_cast<const T*>(a.in);
   T* out = static_cast<T*>(a.out);
   const int P = a.P;
-  const std::int64_t slot = slot_elems<T>(a, P);
+  const bool bcast = a.mode == kModeBroadcast;
+  const std::int64_t slot = slot_elems<T>(a, bcast ? 1 : P);
   const std::int64_t nchunks = (a.n + slot - 1) / slot;
   T* b_me = region_b<T>(a, a.me);
   for (std::int64_t c = 0; c < nchunks; ++c) {
@@ -561,16 +537,30 @@ __global__ void __launch_bounds__(kCollThreads, 2) gather_kernel(const __grid_co
     std::int64_t lo, hi;
     piece<T>(clen, gridDim.x, blockIdx.x, lo, hi);
     const std::uint64_t seq = a.seq_base + static_cast<std::uint64_t>(c) + 1;
-    for (int q = 1; q < P; ++q) {
-      const int p = (a.me + q) % P;
-      copy_range(region_b<T>(a, p) + a.me * slot - c0, in, c0 + lo, c0 + hi);
-    }
-    copy_range(out + static_cast<std::int64_t>(a.me) * a.n, in, c0 + lo, c0 + hi);
-    signal(a, 0, seq);
-    if (!await(a, 0, seq)) return;
-    for (int q = 1; q < P; ++q) {
-      const int p = (a.me + q) % P;
-      copy_range(out + static_cast<std::int64_t>(p) * a.n, b_me + p * slot - c0, c0 + lo, c0 + hi);
+    if (bcast) {
+      if (a.me == a.root) {
+        for (int q = 1; q < P; ++q) {
+          const int p = (a.me + q) % P;
+          copy_range(region_b<T>(a, p) - c0, in, c0 + lo, c0 + hi);
+        }
+        if (out != in) copy_range(out, in, c0 + lo, c0 + hi);
+        signal(a, 0, seq);
+      } else {
+        if (!await(a, 0, seq, a.root)) return;
+        copy_range(out, b_me - c0, c0 + lo, c0 + hi);
+      }
+    } else {
+      for (int q = 1; q < P; ++q) {
+        const int p = (a.me + q) % P;
+        copy_range(region_b<T>(a, p) + a.me * slot - c0, in, c0 + lo, c0 + hi);
+      }
+      copy_range(out + static_cast<std::int64_t>(a.me) * a.n, in, c0 + lo, c0 + hi);
+      signal(a, 0, seq);
+      if (!await(a, 0, seq)) return;
+      for (int q = 1; q < P; ++q) {
+        const int p = (a.me + q) % P;
+        copy_range(out + static_cast<std::int64_t>(p) * a.n, b_me + p * slot - c0, c0 + lo, c0 + hi);
+      }
     }
     // everyone has consumed this chunk before anyone refills the slots
     signal(a, 1, seq);
@@ -629,6 +619,10 @@ __global__ void __launch_bounds__(kCollThreads, 2) bcast_kernel(const __grid_con
       signal(a, 1, seq(c));
       signal(a, 2, seq(c));
     }
+    // every rank has copied the last chunk out before the root leaves: a
+    // later call cannot reach this call's half of the workspace while a peer
+    // still reads it
+    if (nchunks >= 1) await(a, 2, seq(nchunks - 1));
     return;
   }
   for (std::int64_t c = 0; c <= nchunks; ++c) {
@@ -902,7 +896,10 @@ cudaError_t launch_barrier(const CollArgs& a, cudaStream_t s) {
 
 cudaError_t launch_coll(const CollArgs& a, int ctas, cudaStream_t s) {
   if (ctas < 1 || ctas > kMaxCollCtas || a.P > kMaxCollRanks) return cudaErrorInvalidValue;
-  if (a.mode == kModeBroadcast) {
+  // broadcast: the root pushes to every peer at 2 ranks (one link either
+  // way); from 3 ranks scatter + allgather, so the root's link carries about
+  // 2(P-1)/P of the message instead of P-1 times it
+  if (a.mode == kModeBroadcast && a.P > 2) {
     switch (a.elem_bytes) {
       case 1:
         bcast_kernel<std::uint8_t><<<ctas, kCollThreads, 0, s>>>(a);
@@ -921,7 +918,7 @@ cudaError_t launch_coll(const CollArgs& a, int ctas, cudaStream_t s) {
     }
     return cudaGetLastError();
   }
-  if (a.mode == kModeAllgather) {
+  if (a.mode == kModeAllgather || a.mode == kModeBroadcast) {
     switch (a.elem_bytes) {
       case 1:
         gather_kernel<std::uint8_t><<<ctas, kCollThreads, 0, s>>>(a);

@@ -74,7 +74,9 @@ class CudaPlan final : public DevicePlan {
   }
   std::vector<Msg> sends, recvs;
 
-  // Builds the launches every start() replays: (1) pack + "ready" signals of
+  // Builds the launches every start() replays (one launch is issued
+  // directly; several are captured into a CUDA graph at the first start):
+  // (1) pack + "ready" signals of
   // the sends to other GPUs (without packing, the signals are stored by the
   // first pull launch at entry instead), (2) the pulls of every receive; the
   // last CTA of the last launch then waits for the receivers' "consumed"
@@ -220,6 +222,18 @@ class CudaPlan final : public DevicePlan {
     }
   }
 
+  // Grid cap of the launches. A launch whose CTAs wait on peers keeps every
+  // CTA resident at once, so a CTA never waits while another CTA of the
+  // launch that still has pack work waits for an SM; launches without waits
+  // keep the wider grid.
+  int grid_ctas() const {
+    bool waits = false;
+    for (auto& m : recvs) waits |= m.mode == PlanMode::Device;
+    int ctas = waits ? std::min(tr_->pull_ctas(c_), 4 * c_->sm_count) : tr_->pull_ctas(c_);
+    if (max_ctas_ > 0) ctas = std::min(ctas, max_ctas_);
+    return ctas;
+  }
+
   PullBatch* dev_batch(std::size_t k) {
     return reinterpret_cast<PullBatch*>(static_cast<char*>(batches_d_.data_ptr()) + k * sizeof(PullBatch));
   }
@@ -246,15 +260,25 @@ class CudaPlan final : public DevicePlan {
       }
       tr_->end_batch();
     }
-    if (!exec_) capture();
     last_stream_ = cur;
     if (trace_h_ != nullptr)
       for (std::size_t k = 0; k < trace_n_; ++k) {
         trace_h_[2 * k] = ~0ull;
         trace_h_[2 * k + 1] = 0;
       }
-    CMX_CUDA(cudaGraphLaunch(exec_, cur));
-    tr_->kernel_launches += nodes_;
+    const std::size_t nlaunch = pre_.size() + pulls_.size();
+    static const bool graph_always = env_int("COMMUX_PLAN_GRAPH", 0) != 0;
+    if (nlaunch == 1 && !graph_always) {
+      // one launch: the kernel itself, its batch already on the device (a
+      // graph of one node adds device-side launch work and saves nothing)
+      const PullBatch& hb = pre_.empty() ? *pulls_[0] : *pre_[0];
+      CMX_CUDA(launch_pull_dev(hb, dev_batch(0), grid_ctas(), cur));
+      tr_->kernel_launches += 1;
+    } else if (nlaunch > 0) {
+      if (!exec_) capture();
+      CMX_CUDA(cudaGraphLaunch(exec_, cur));
+      tr_->kernel_launches += nodes_;
+    }
     if (trace_h_ != nullptr) report_trace(cur);
     if (!shared.empty()) {
       for (auto& r : shared) eng_->wait(r, std::chrono::milliseconds(0));
@@ -264,13 +288,27 @@ class CudaPlan final : public DevicePlan {
     if (!e.empty()) C10_THROW_ERROR(DistBackendError, e);
   }
 
+  void set_max_ctas(int ctas) override {
+    TORCH_CHECK(ctas >= 0, "commux plan: max_ctas must be >= 0");
+    if (ctas == max_ctas_) return;
+    max_ctas_ = ctas;
+    if (exec_) {  // captured with the old grid: capture again at the next start
+      c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(c_->dev));
+      if (last_stream_ != nullptr) CMX_CUDA(cudaStreamSynchronize(last_stream_));
+      cudaGraphExecDestroy(exec_);
+      cudaGraphDestroy(graph_);
+      exec_ = nullptr;
+      graph_ = nullptr;
+    }
+  }
+
   std::vector<std::pair<std::string, std::int64_t>> info() override {
     std::int64_t loc = 0, dev = 0, packed = 0;
     for (auto* v : {&sends, &recvs})
       for (auto& m : *v) (m.mode == PlanMode::Local ? loc : dev) += m.mode != PlanMode::Shared;
     for (auto& m : sends) packed += (m.mode == PlanMode::Device && !m.pack.empty()) ? 1 : 0;
     return {{"local", loc},      {"device", dev},       {"shared", n_shared_}, {"packed_sends", packed},
-            {"graph_nodes", nodes_}, {"starts", static_cast<std::int64_t>(starts_)}};
+            {"graph_nodes", nodes_}, {"starts", static_cast<std::int64_t>(starts_)}, {"max_ctas", max_ctas_}};
   }
 
   std::int64_t n_shared_ = 0;
@@ -386,12 +424,7 @@ class CudaPlan final : public DevicePlan {
   void capture() {
     cudaStream_t cs = nullptr;
     CMX_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
-    // a launch whose CTAs wait on peers keeps every CTA resident at once, so
-    // a CTA never waits while another CTA of the launch that still has pack
-    // work waits for an SM; launches without waits keep the wider grid
-    bool waits = false;
-    for (auto& m : recvs) waits |= m.mode == PlanMode::Device;
-    const int ctas = waits ? std::min(tr_->pull_ctas(c_), 4 * c_->sm_count) : tr_->pull_ctas(c_);
+    const int ctas = grid_ctas();
     nodes_ = 0;
     CMX_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
     cudaError_t e = cudaSuccess;
@@ -422,6 +455,7 @@ class CudaPlan final : public DevicePlan {
   std::uint64_t* epoch_d_ = nullptr;
   unsigned int* cta_done_d_ = nullptr;
   at::Tensor batches_d_;  // the launches' batches in device memory
+  int max_ctas_ = 0;      // set_max_ctas (0: the default grid)
   std::uint32_t* counters_d_ = nullptr;
   std::vector<std::unique_ptr<PullBatch>> pre_, pulls_;
   WaitBatch wait_{};

@@ -366,6 +366,9 @@ class DevicePlan {
   virtual ~DevicePlan() = default;
   virtual void start() = 0;
   virtual std::vector<std::pair<std::string, std::int64_t>> info() = 0;
+  // Caps the CTAs of the plan's launches (0: the default grid). A smaller
+  // grid leaves SMs to kernels that run beside the exchange.
+  virtual void set_max_ctas(int ctas) = 0;
 };
 using DevicePlanPtr = std::shared_ptr<DevicePlan>;
 

@@ -80,6 +80,10 @@ PYBIND11_MODULE(_C, m) {
   py::class_<commux::DevicePlan, std::shared_ptr<commux::DevicePlan>>(m, "P2PPlan")
       .def("start", &commux::DevicePlan::start, py::call_guard<py::gil_scoped_release>(),
            "Enqueue one exchange of the plan's buffers on the current CUDA stream.")
+      .def("set_max_ctas", &commux::DevicePlan::set_max_ctas, py::arg("ctas"),
+           py::call_guard<py::gil_scoped_release>(),
+           "Cap the CTAs of the plan's launches (0: default), e.g. to leave SMs to a kernel that runs "
+           "beside the exchange.")
       .def("info", [](commux::DevicePlan& p) {
         py::dict d;
         for (auto& kv : p.info()) d[py::str(kv.first)] = kv.second;

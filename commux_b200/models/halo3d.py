@@ -10,6 +10,8 @@ kernel) from ``u`` into ``v``; the fields swap roles each step.
 
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
@@ -19,7 +21,7 @@ from ..parallel.halo import CartGrid, HaloExchange, factor3
 
 class Jacobi3D:
     def __init__(self, global_n: int = 1024, halo: int = 2, dims=None, dtype=torch.float64,
-                 device=None, group=None, seed: int = 0):
+                 device=None, group=None, seed: int = 0, overlap_ctas: int | None = None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -43,6 +45,13 @@ class Jacobi3D:
         self.residual = torch.zeros(1, dtype=torch.float64, device=self.device)
         self.grid = CartGrid(self.dims, self.rank)
         self.halo = HaloExchange(self.interior, halo, self.grid, group=group)
+        # step_overlapped() exchanges through its own plans, whose launches
+        # take at most `overlap_ctas` CTAs (default one per SM) so the core
+        # update keeps most of every SM while the exchange runs
+        if overlap_ctas is None:
+            overlap_ctas = int(os.environ.get(
+                "COMMUX_OVERLAP_CTAS", torch.cuda.get_device_properties(self.device).multi_processor_count))
+        self.halo_overlap = HaloExchange(self.interior, halo, self.grid, group=group, max_ctas=overlap_ctas)
         self._xstream = None  # side stream of step_overlapped()
 
     @property
@@ -82,7 +91,7 @@ class Jacobi3D:
         xs = self._xstream
         xs.wait_stream(main)  # u complete (the previous step's update)
         with torch.cuda.stream(xs):
-            self.halo.exchange(self.u)
+            self.halo_overlap.exchange(self.u)
         self.residual.zero_()
         jacobi7(self.u, self.v, h, self.residual, part="core")
         main.wait_stream(xs)

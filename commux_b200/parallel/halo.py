@@ -83,7 +83,8 @@ class HaloExchange:
     the current stream.
     """
 
-    def __init__(self, interior, halo: int, grid: CartGrid, group=None, directions=None):
+    def __init__(self, interior, halo: int, grid: CartGrid, group=None, directions=None, max_ctas: int = 0):
+        self.max_ctas = max_ctas  # grid cap of the persistent plans (0: default)
         self.n = tuple(interior)
         self.h = halo
         self.grid = grid
@@ -157,7 +158,8 @@ class HaloExchange:
             if u.is_cuda and self.use_plans and "tcp" not in commux_b200.transports(self.group):
                 # matched once; every later exchange of this field replays
                 # one CUDA graph (collective: all ranks reach this together)
-                persistent = commux_b200.p2p_plan(sends=sends, recvs=recvs, group=self.group)
+                persistent = commux_b200.p2p_plan(sends=sends, recvs=recvs, group=self.group,
+                                                  max_ctas=self.max_ctas)
             plan = self._plans[key] = (sends, recvs, persistent)
         if plan[2] is not None:
             plan[2].start()

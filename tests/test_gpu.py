@@ -51,7 +51,7 @@ def test_jacobi7_matches_reference(dtype, shape):
 # other).
 # (A first send to a peer whose GPU is not yet known may still complete by a
 # host FIN, so the peer form does not require zero of those.)
-PEER_P2P = "cuda_sends_device_flag>0,cuda_wait_kernels>0,cuda_pulls_peer_gpu>0,cuda_pulls_same_gpu==0"
+PEER_P2P = "cuda_sends_device_flag>0,cuda_pulls_peer_gpu>0,cuda_pulls_same_gpu==0"
 SHARED_P2P = "cuda_sends_host_fin>0,cuda_pulls_same_gpu>0,cuda_sends_device_flag==0,cuda_pulls_peer_gpu==0"
 PEER_PLAN = "cuda_plan_device_msgs>0,cuda_plan_shared_msgs==0,cuda_plan_starts>0"
 SHARED_PLAN = "cuda_plan_shared_msgs>0,cuda_plan_device_msgs==0,cuda_plan_starts>0"
