@@ -257,6 +257,10 @@ void CollImpl::fill(CollArgs& a, const Launch& l, const at::Tensor& in, const at
   a.op = l.op;
   a.dtype = dtype_code(in.scalar_type());
   a.elem_bytes = static_cast<int>(in.element_size());
+  // COMMUX_BCAST_SCATTER_RANKS: group size from which broadcasts scatter
+  // from the root and allgather (below it the root pushes to every peer)
+  static const int scatter_ranks = static_cast<int>(env_int("COMMUX_BCAST_SCATTER_RANKS", 3));
+  a.bcast_scatter_ranks = scatter_ranks;
   a.n = l.n;
   a.in = in.data_ptr();
   a.out = out.data_ptr();

@@ -46,6 +46,7 @@ struct CollArgs {
   int op;
   int dtype;
   int elem_bytes;
+  int bcast_scatter_ranks;  // broadcast: scatter + allgather from this many ranks
   std::int64_t n;  // elements: allreduce/reduce total; reduce_scatter and
                    // allgather per-rank block; broadcast total
   const void* in;

@@ -896,10 +896,10 @@ cudaError_t launch_barrier(const CollArgs& a, cudaStream_t s) {
 
 cudaError_t launch_coll(const CollArgs& a, int ctas, cudaStream_t s) {
   if (ctas < 1 || ctas > kMaxCollCtas || a.P > kMaxCollRanks) return cudaErrorInvalidValue;
-  // broadcast: the root pushes to every peer at 2 ranks (one link either
-  // way); from 3 ranks scatter + allgather, so the root's link carries about
-  // 2(P-1)/P of the message instead of P-1 times it
-  if (a.mode == kModeBroadcast && a.P > 2) {
+  // broadcast: the root pushes to every peer below a.bcast_scatter_ranks
+  // ranks (at 2 ranks one link either way); from there scatter + allgather,
+  // so the root's link carries about 2(P-1)/P of the message, not P-1 times it
+  if (a.mode == kModeBroadcast && a.P >= a.bcast_scatter_ranks) {
     switch (a.elem_bytes) {
       case 1:
         bcast_kernel<std::uint8_t><<<ctas, kCollThreads, 0, s>>>(a);

@@ -188,34 +188,16 @@ __device__ __forceinline__ bool wait_ready(const std::uint64_t* ready, std::uint
   return true;
 }
 
-// The batch of a launch: in the kernel parameter block (kGlobal false; read
-// through the constant cache), or in device memory (kGlobal true: a plan's
-// batches are uploaded once, so each launch passes one pointer instead of
-// about 27 KB of parameters, which the launch would copy every time). In
-// device memory, each chunk's descriptor is staged into shared memory by the
-// CTA before its warps copy. The epoch of a plan's launch comes from device
-// memory either way.
-template <bool kGlobal>
-struct BatchSrc {
+// Descriptors in the kernel parameter block (read through the constant
+// cache); the epoch of a plan's launch comes from device memory. (Batches in
+// device memory, passed as one pointer, measured about 2 us slower on a
+// small exchange: the dependent loads of the descriptor search cost more
+// than copying the parameter block at launch.)
+struct InlineSrc {
   const PullBatch& b;
-  PullDesc* staged;  // shared memory (kGlobal)
   __device__ std::uint32_t n() const { return b.n; }
   __device__ std::uint32_t total() const { return b.total_chunks; }
   __device__ const PullDesc& desc(std::uint32_t i) const { return b.d[i]; }
-  // descriptor i for the copy loops (every thread of the CTA calls this)
-  __device__ const PullDesc& load(std::uint32_t i) const {
-    if constexpr (!kGlobal) {
-      return b.d[i];
-    } else {
-      static_assert(sizeof(PullDesc) % 8 == 0, "descriptor staged in 8-byte words");
-      __syncthreads();  // every warp is done with the previous descriptor
-      const uint2* from = reinterpret_cast<const uint2*>(&b.d[i]);
-      uint2* to = reinterpret_cast<uint2*>(staged);
-      for (std::uint32_t k = threadIdx.x; k < sizeof(PullDesc) / 8; k += blockDim.x) to[k] = from[k];
-      __syncthreads();
-      return *staged;
-    }
-  }
   __device__ std::uint32_t* counters() const { return b.counters; }
   __device__ unsigned long long* status() const { return b.status; }
   __device__ std::uint64_t timeout_ns() const { return b.timeout_ns; }
@@ -316,7 +298,7 @@ __device__ __forceinline__ void pull_body(const S& s) {
   s.entry_signals(epoch);
   for (std::uint32_t c = blockIdx.x; c < s.total(); c += gridDim.x) {
     std::uint32_t local = 0;
-    const PullDesc& d = s.load(find_desc(s, c, local));
+    const PullDesc& d = s.desc(find_desc(s, c, local));
     const std::uint32_t u0 = local * kChunkUnits;
     bool failed = false;
     if (d.ready != nullptr) {  // persistent plan: wait for the sender's data
@@ -366,14 +348,7 @@ __device__ __forceinline__ void pull_body(const S& s) {
 // 80 registers, one loop alone fits the 64 that four CTAs per SM allow.
 template <int U>
 __global__ void __launch_bounds__(kThreads, 4) pull_kernel(const __grid_constant__ PullBatch b) {
-  pull_body<U>(BatchSrc<false>{b, nullptr});
-}
-
-// The same copy with the batch in device memory (persistent plans).
-template <int U>
-__global__ void __launch_bounds__(kThreads, 4) pull_kernel_dev(const PullBatch* __restrict__ g) {
-  __shared__ PullDesc staged;
-  pull_body<U>(BatchSrc<true>{*g, &staged});
+  pull_body<U>(InlineSrc{b});
 }
 
 // One warp: lane i waits until *flag[i] >= val[i], giving up after the
@@ -424,41 +399,7 @@ cudaError_t launch_class(int cls, const PullBatch& b, int max_ctas, cudaStream_t
   return cudaGetLastError();
 }
 
-cudaError_t launch_class_dev(int cls, const PullBatch* g, std::uint32_t total_chunks, int max_ctas,
-                             cudaStream_t s) {
-  const int grid = static_cast<int>(total_chunks < static_cast<std::uint32_t>(max_ctas) ? total_chunks : max_ctas);
-  switch (cls) {
-    case 16:
-      pull_kernel_dev<16><<<grid, kThreads, 0, s>>>(g);
-      break;
-    case 8:
-      pull_kernel_dev<8><<<grid, kThreads, 0, s>>>(g);
-      break;
-    case 4:
-      pull_kernel_dev<4><<<grid, kThreads, 0, s>>>(g);
-      break;
-    case 2:
-      pull_kernel_dev<2><<<grid, kThreads, 0, s>>>(g);
-      break;
-    case 1:
-      pull_kernel_dev<1><<<grid, kThreads, 0, s>>>(g);
-      break;
-    default:
-      pull_kernel_dev<0><<<grid, kThreads, 0, s>>>(g);
-      break;
-  }
-  return cudaGetLastError();
-}
-
 }  // namespace
-
-cudaError_t launch_pull_dev(const PullBatch& host, const PullBatch* dev, int max_ctas, cudaStream_t s) {
-  if (host.n == 0 || host.total_chunks == 0) return cudaSuccess;
-  const int cls = pull_unit_class(host.d[0]);
-  for (std::uint32_t i = 1; i < host.n; ++i)
-    if (pull_unit_class(host.d[i]) != cls) return cudaErrorInvalidValue;
-  return launch_class_dev(cls, dev, host.total_chunks, max_ctas, s);
-}
 
 // A batch whose descriptors share one unit class is one launch; a mixed batch
 // becomes one launch per class, in order on the stream (completion counters

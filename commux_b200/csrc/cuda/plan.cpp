@@ -74,9 +74,8 @@ class CudaPlan final : public DevicePlan {
   }
   std::vector<Msg> sends, recvs;
 
-  // Builds the launches every start() replays (one launch is issued
-  // directly; several are captured into a CUDA graph at the first start):
-  // (1) pack + "ready" signals of
+  // Builds the launches every start() replays (captured into a CUDA graph
+  // at the first start): (1) pack + "ready" signals of
   // the sends to other GPUs (without packing, the signals are stored by the
   // first pull launch at entry instead), (2) the pulls of every receive; the
   // last CTA of the last launch then waits for the receivers' "consumed"
@@ -164,6 +163,10 @@ class CudaPlan final : public DevicePlan {
     const std::uint64_t one = 1;
     std::memcpy(init.data(), &one, sizeof(one));
     CMX_CUDA(cudaMemcpy(state_.data_ptr(), init.data(), state_bytes, cudaMemcpyHostToDevice));
+    // a plan whose messages all stay on this GPU has no flags: its launches
+    // skip the epoch (one dependent load less at kernel start)
+    for (auto* v : {&sends, &recvs})
+      for (auto& m : *v) has_flags_ |= m.mode == PlanMode::Device;
     pre_ = batches(pre, pre.size());
     pulls_ = batches(pull, lead);
     if (!ready_only.empty()) {
@@ -211,15 +214,6 @@ class CudaPlan final : public DevicePlan {
         }
       trace_n_ = n;
     }
-    // every batch goes to device memory once: a launch passes one pointer
-    const std::size_t nb = pre_.size() + pulls_.size();
-    if (nb > 0) {
-      batches_d_ = at::empty({static_cast<std::int64_t>(nb * sizeof(PullBatch))},
-                             at::TensorOptions().dtype(at::kByte).device(at::kCUDA, c_->dev));
-      std::size_t k = 0;
-      for (auto* ls : {&pre_, &pulls_})
-        for (auto& b : *ls) CMX_CUDA(cudaMemcpy(dev_batch(k++), b.get(), sizeof(PullBatch), cudaMemcpyHostToDevice));
-    }
   }
 
   // Grid cap of the launches. A launch whose CTAs wait on peers keeps every
@@ -234,9 +228,6 @@ class CudaPlan final : public DevicePlan {
     return ctas;
   }
 
-  PullBatch* dev_batch(std::size_t k) {
-    return reinterpret_cast<PullBatch*>(static_cast<char*>(batches_d_.data_ptr()) + k * sizeof(PullBatch));
-  }
 
   void start() override {
     ++starts_;
@@ -266,15 +257,7 @@ class CudaPlan final : public DevicePlan {
         trace_h_[2 * k] = ~0ull;
         trace_h_[2 * k + 1] = 0;
       }
-    const std::size_t nlaunch = pre_.size() + pulls_.size();
-    static const bool graph_always = env_int("COMMUX_PLAN_GRAPH", 0) != 0;
-    if (nlaunch == 1 && !graph_always) {
-      // one launch: the kernel itself, its batch already on the device (a
-      // graph of one node adds device-side launch work and saves nothing)
-      const PullBatch& hb = pre_.empty() ? *pulls_[0] : *pre_[0];
-      CMX_CUDA(launch_pull_dev(hb, dev_batch(0), grid_ctas(), cur));
-      tr_->kernel_launches += 1;
-    } else if (nlaunch > 0) {
+    if (pre_.size() + pulls_.size() > 0) {
       if (!exec_) capture();
       CMX_CUDA(cudaGraphLaunch(exec_, cur));
       tr_->kernel_launches += nodes_;
@@ -392,7 +375,7 @@ class CudaPlan final : public DevicePlan {
       b->counters = counters_d_;
       b->status = c_->status_d;
       b->timeout_ns = tr_->device_timeout_ns();
-      b->epoch = epoch_d_;
+      b->epoch = has_flags_ ? epoch_d_ : nullptr;
       b->nsig = 0;
       return b;
     };
@@ -428,12 +411,11 @@ class CudaPlan final : public DevicePlan {
     nodes_ = 0;
     CMX_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
     cudaError_t e = cudaSuccess;
-    std::size_t k = 0;
     for (auto* ls : {&pre_, &pulls_})
       for (auto& b : *ls) {
-        if (e == cudaSuccess) e = launch_pull_dev(*b, dev_batch(k), ctas, cs);
-        ++k;
-        ++nodes_;
+        int launched = 0;
+        if (e == cudaSuccess) e = launch_pull(*b, ctas, 256, cs, &launched);
+        nodes_ += launched;
       }
     // the receivers' "consumed" flags and the epoch bump ride on the last
     // launch (its last CTA waits and bumps; see PullBatch::bump); a plan
@@ -454,8 +436,8 @@ class CudaPlan final : public DevicePlan {
   at::Tensor state_;
   std::uint64_t* epoch_d_ = nullptr;
   unsigned int* cta_done_d_ = nullptr;
-  at::Tensor batches_d_;  // the launches' batches in device memory
   int max_ctas_ = 0;      // set_max_ctas (0: the default grid)
+  bool has_flags_ = false;  // some message crosses to another GPU
   std::uint32_t* counters_d_ = nullptr;
   std::vector<std::unique_ptr<PullBatch>> pre_, pulls_;
   WaitBatch wait_{};
