@@ -92,6 +92,10 @@ struct PullBatch {
   // last CTA. nullptr otherwise
   unsigned long long* trace;
   unsigned int* trace_count;
+  // COMMUX_PLAN_TRACE=2: per CTA, 4 words (host-mapped): first and last
+  // %globaltimer stamp of the CTA, ns its thread 0 spent waiting on ready
+  // flags, chunks it copied that had a ready flag. nullptr otherwise
+  unsigned long long* cta_trace;
   // flags stored (release, system scope) by the first CTA at kernel entry,
   // value *epoch: the "data ready" signals of a plan whose sends need no
   // packing ride on its pull launch instead of a launch of their own

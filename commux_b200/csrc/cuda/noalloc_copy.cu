@@ -177,6 +177,7 @@ extern "C" int commux_strided_copy_noalloc(void* dst, const int64_t* dst_strides
   b.epoch = nullptr;
   b.trace = nullptr;
   b.trace_count = nullptr;
+  b.cta_trace = nullptr;
   b.nsig = 0;
   b.bump = nullptr;
   b.cta_done = nullptr;

@@ -202,6 +202,7 @@ struct InlineSrc {
   __device__ unsigned long long* status() const { return b.status; }
   __device__ std::uint64_t timeout_ns() const { return b.timeout_ns; }
   __device__ std::uint64_t epoch() const { return b.epoch ? *b.epoch : 0; }
+  __device__ unsigned long long* cta_trace() const { return b.cta_trace; }
   __device__ void trace_start() const {
     if (b.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0) b.trace[0] = globaltimer_ns();
   }
@@ -295,6 +296,9 @@ __device__ __forceinline__ void pull_body(const S& s) {
   const std::uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const std::uint64_t epoch = s.epoch();
   s.trace_start();
+  unsigned long long* ct = s.cta_trace();
+  std::uint64_t t_begin = 0, waited = 0, flagged = 0;
+  if (ct != nullptr && threadIdx.x == 0) t_begin = globaltimer_ns();
   s.entry_signals(epoch);
   for (std::uint32_t c = blockIdx.x; c < s.total(); c += gridDim.x) {
     std::uint32_t local = 0;
@@ -302,8 +306,14 @@ __device__ __forceinline__ void pull_body(const S& s) {
     const std::uint32_t u0 = local * kChunkUnits;
     bool failed = false;
     if (d.ready != nullptr) {  // persistent plan: wait for the sender's data
-      if (threadIdx.x == 0)
+      if (threadIdx.x == 0) {
+        const std::uint64_t w0 = ct != nullptr ? globaltimer_ns() : 0;
         skip = wait_ready(d.ready, epoch ? epoch : d.ready_val, s.status(), s.timeout_ns()) ? 0 : 1;
+        if (ct != nullptr) {
+          waited += globaltimer_ns() - w0;
+          ++flagged;
+        }
+      }
       __syncthreads();
       failed = skip != 0;
       __syncthreads();  // every thread read `skip` before it is rewritten
@@ -340,6 +350,13 @@ __device__ __forceinline__ void pull_body(const S& s) {
     }
   }
   s.trace_end();
+  if (ct != nullptr && threadIdx.x == 0) {
+    unsigned long long* r = ct + 4ull * blockIdx.x;
+    r[0] = t_begin;
+    r[1] = globaltimer_ns();
+    r[2] = waited;
+    r[3] = flagged;
+  }
   s.finish(epoch);
 }
 
@@ -421,6 +438,7 @@ cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStrea
   sub.epoch = b.epoch;
   sub.trace = b.trace;
   sub.trace_count = b.trace_count;
+  sub.cta_trace = nullptr;
   sub.nsig = 0;  // entry signals go with the first class launched
   sub.bump = nullptr;  // the end-of-start wait goes with the last one
   int last_cls = -1;

@@ -70,6 +70,7 @@ class CudaPlan final : public DevicePlan {
     if (exec_) cudaGraphExecDestroy(exec_);
     if (graph_) cudaGraphDestroy(graph_);
     if (trace_h_) cudaFreeHost(trace_h_);
+    if (cta_trace_h_) cudaFreeHost(cta_trace_h_);
     cudaGetLastError();
   }
   std::vector<Msg> sends, recvs;
@@ -213,6 +214,15 @@ class CudaPlan final : public DevicePlan {
           b->trace_count = count;
         }
       trace_n_ = n;
+      // COMMUX_PLAN_TRACE=2: per-CTA stamps of the last launch (the pulls)
+      if (env_int("COMMUX_PLAN_TRACE", 0) >= 2 && (!pulls_.empty() || !pre_.empty())) {
+        cta_trace_n_ = static_cast<std::size_t>(8 * c_->sm_count);
+        CMX_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&cta_trace_h_), cta_trace_n_ * 4 * sizeof(unsigned long long),
+                               cudaHostAllocMapped));
+        unsigned long long* dd = nullptr;
+        CMX_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&dd), cta_trace_h_, 0));
+        (pulls_.empty() ? pre_.back() : pulls_.back())->cta_trace = dd;
+      }
     }
   }
 
@@ -302,7 +312,7 @@ class CudaPlan final : public DevicePlan {
     unsigned long long t0 = ~0ull;
     for (std::size_t k = 0; k < trace_n_; ++k) t0 = std::min(t0, trace_h_[2 * k]);
     std::string line;
-    char buf[96];
+    char buf[160];
     std::size_t k = 0;
     auto span = [&](const char* what) {
       const unsigned long long a = trace_h_[2 * k], b = trace_h_[2 * k + 1];
@@ -313,6 +323,34 @@ class CudaPlan final : public DevicePlan {
     };
     for (std::size_t i = 0; i < pre_.size(); ++i) span("pack");
     for (std::size_t i = 0; i < pulls_.size(); ++i) span("pull");
+    if (cta_trace_h_ != nullptr) {
+      // CTAs that ran (end stamp set): spans, ready-flag waits, flagged chunks
+      std::vector<double> span_us;
+      double wait_sum = 0, wait_max = 0, first = 1e300, last = 0;
+      unsigned long long flagged = 0;
+      int waited_ctas = 0;
+      for (std::size_t k = 0; k < cta_trace_n_; ++k) {
+        const unsigned long long* r = cta_trace_h_ + 4 * k;
+        if (r[1] == 0) continue;
+        span_us.push_back((r[1] - r[0]) / 1e3);
+        first = std::min(first, static_cast<double>(r[0]));
+        last = std::max(last, static_cast<double>(r[1]));
+        wait_sum += r[2] / 1e3;
+        wait_max = std::max(wait_max, r[2] / 1e3);
+        flagged += r[3];
+        waited_ctas += r[3] > 0 ? 1 : 0;
+      }
+      if (!span_us.empty()) {
+        std::sort(span_us.begin(), span_us.end());
+        std::snprintf(buf, sizeof(buf), " | ctas %zu span p50 %.1f max %.1f us, first-to-last %.1f us",
+                      span_us.size(), span_us[span_us.size() / 2], span_us.back(), (last - first) / 1e3);
+        line += buf;
+        std::snprintf(buf, sizeof(buf), ", flagged chunks %llu on %d ctas, ready wait sum %.1f max %.1f us",
+                      flagged, waited_ctas, wait_sum, wait_max);
+        line += buf;
+      }
+      for (std::size_t k = 0; k < cta_trace_n_ * 4; ++k) cta_trace_h_[k] = 0;
+    }
     std::fprintf(stderr, "[commux plan trace rank %d] start %llu, us from the first CTA:%s\n", eng_->rank(),
                  static_cast<unsigned long long>(starts_), line.c_str());
   }
@@ -445,6 +483,8 @@ class CudaPlan final : public DevicePlan {
   cudaGraphExec_t exec_ = nullptr;
   std::int64_t nodes_ = 0;
   unsigned long long* trace_h_ = nullptr;  // COMMUX_PLAN_TRACE (host-mapped)
+  unsigned long long* cta_trace_h_ = nullptr;  // COMMUX_PLAN_TRACE=2: per-CTA stamps
+  std::size_t cta_trace_n_ = 0;
   std::size_t trace_n_ = 0;
   cudaStream_t last_stream_ = nullptr;      // stream of the last start
 };
