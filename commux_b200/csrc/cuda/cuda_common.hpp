@@ -142,6 +142,10 @@ cudaError_t launch_pull(const PullBatch& b, int max_ctas, int threads, cudaStrea
 // 2, 1 byte units; 0 = wide strides).
 inline int pull_unit_class(const PullDesc& d) { return d.wide ? 0 : static_cast<int>(d.unit); }
 cudaError_t launch_wait(const WaitBatch& b, cudaStream_t s);
+// Launches the pull kernel on a batch already in device memory (`dev`, a
+// copy of `host`, whose descriptors share one unit class); each CTA stages
+// the batch into shared memory first.
+cudaError_t launch_pull_staged(const PullBatch& host, const PullBatch* dev, int max_ctas, cudaStream_t s);
 
 // Loads every pull-kernel build into the current context (see p2p_kernels.cu).
 cudaError_t preload_pull_kernels();

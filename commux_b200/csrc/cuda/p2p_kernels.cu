@@ -16,6 +16,8 @@
 // zeroes the message's counter so the scratch is clean for the next launch on
 // that stream.
 
+#include <cstddef>
+
 #include "cuda_common.hpp"
 #include "device_utils.cuh"
 
@@ -188,11 +190,10 @@ __device__ __forceinline__ bool wait_ready(const std::uint64_t* ready, std::uint
   return true;
 }
 
-// Descriptors in the kernel parameter block (read through the constant
-// cache); the epoch of a plan's launch comes from device memory. (Batches in
-// device memory, passed as one pointer, measured about 2 us slower on a
-// small exchange: the dependent loads of the descriptor search cost more
-// than copying the parameter block at launch.)
+// The batch a launch works from: its kernel parameter block (pull_kernel;
+// read through the constant cache), or a copy in shared memory that each CTA
+// stages from device memory at its start (pull_kernel_staged, persistent
+// plans). The epoch of a plan's launch comes from device memory.
 struct InlineSrc {
   const PullBatch& b;
   __device__ std::uint32_t n() const { return b.n; }
@@ -296,9 +297,14 @@ __device__ __forceinline__ void pull_body(const S& s) {
   const std::uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const std::uint64_t epoch = s.epoch();
   s.trace_start();
-  unsigned long long* ct = s.cta_trace();
-  std::uint64_t t_begin = 0, waited = 0, flagged = 0;
-  if (ct != nullptr && threadIdx.x == 0) t_begin = globaltimer_ns();
+  // COMMUX_PLAN_TRACE=2 tallies of this CTA (thread 0), in shared memory so
+  // they hold no registers across the copy loop
+  __shared__ unsigned long long t_begin, waited, flagged;
+  if (threadIdx.x == 0) {
+    t_begin = s.cta_trace() != nullptr ? globaltimer_ns() : 0;
+    waited = 0;
+    flagged = 0;
+  }
   s.entry_signals(epoch);
   for (std::uint32_t c = blockIdx.x; c < s.total(); c += gridDim.x) {
     std::uint32_t local = 0;
@@ -307,9 +313,10 @@ __device__ __forceinline__ void pull_body(const S& s) {
     bool failed = false;
     if (d.ready != nullptr) {  // persistent plan: wait for the sender's data
       if (threadIdx.x == 0) {
-        const std::uint64_t w0 = ct != nullptr ? globaltimer_ns() : 0;
+        const bool tr = s.cta_trace() != nullptr;
+        const std::uint64_t w0 = tr ? globaltimer_ns() : 0;
         skip = wait_ready(d.ready, epoch ? epoch : d.ready_val, s.status(), s.timeout_ns()) ? 0 : 1;
-        if (ct != nullptr) {
+        if (tr) {
           waited += globaltimer_ns() - w0;
           ++flagged;
         }
@@ -350,8 +357,8 @@ __device__ __forceinline__ void pull_body(const S& s) {
     }
   }
   s.trace_end();
-  if (ct != nullptr && threadIdx.x == 0) {
-    unsigned long long* r = ct + 4ull * blockIdx.x;
+  if (s.cta_trace() != nullptr && threadIdx.x == 0) {
+    unsigned long long* r = s.cta_trace() + 4ull * blockIdx.x;
     r[0] = t_begin;
     r[1] = globaltimer_ns();
     r[2] = waited;
@@ -367,6 +374,26 @@ template <int U>
 __global__ void __launch_bounds__(kThreads, 4) pull_kernel(const __grid_constant__ PullBatch b) {
   pull_body<U>(InlineSrc{b});
 }
+
+// The same copy for a batch in device memory (persistent plans): each CTA
+// first copies the batch header and its n descriptors (at most about 28 KB)
+// into shared memory, then works only from there. A plan's descriptor table
+// (26 descriptors for a halo, up to 128) does not fit the per-SM constant
+// cache, so from the parameter block every chunk's descriptor search and
+// field reads were a chain of cache misses: CTAs of the 1-GPU halo spent
+// about 7 us per 16 KB chunk.
+template <int U>
+__global__ void __launch_bounds__(kThreads, 4) pull_kernel_staged(const PullBatch* __restrict__ g) {
+  extern __shared__ __align__(16) unsigned char staged[];
+  const std::size_t bytes = offsetof(PullBatch, d) + static_cast<std::size_t>(g->n) * sizeof(PullDesc);
+  const uint2* from = reinterpret_cast<const uint2*>(g);
+  uint2* to = reinterpret_cast<uint2*>(staged);
+  for (std::size_t k = threadIdx.x; k < bytes / sizeof(uint2); k += blockDim.x) to[k] = from[k];
+  __syncthreads();
+  pull_body<U>(InlineSrc{*reinterpret_cast<const PullBatch*>(staged)});
+}
+static_assert(offsetof(PullBatch, d) % sizeof(uint2) == 0 && sizeof(PullDesc) % sizeof(uint2) == 0,
+              "the batch is staged in 8-byte words");
 
 // One warp: lane i waits until *flag[i] >= val[i], giving up after the
 // timeout (status word set, kernel returns; never traps).
@@ -417,6 +444,37 @@ cudaError_t launch_class(int cls, const PullBatch& b, int max_ctas, cudaStream_t
 }
 
 }  // namespace
+
+cudaError_t launch_pull_staged(const PullBatch& host, const PullBatch* dev, int max_ctas, cudaStream_t s) {
+  if (host.n == 0 || host.total_chunks == 0) return cudaSuccess;
+  const int cls = pull_unit_class(host.d[0]);
+  for (std::uint32_t i = 1; i < host.n; ++i)
+    if (pull_unit_class(host.d[i]) != cls) return cudaErrorInvalidValue;
+  const int grid =
+      static_cast<int>(host.total_chunks < static_cast<std::uint32_t>(max_ctas) ? host.total_chunks : max_ctas);
+  const std::size_t smem = offsetof(PullBatch, d) + static_cast<std::size_t>(host.n) * sizeof(PullDesc);
+  switch (cls) {
+    case 16:
+      pull_kernel_staged<16><<<grid, kThreads, smem, s>>>(dev);
+      break;
+    case 8:
+      pull_kernel_staged<8><<<grid, kThreads, smem, s>>>(dev);
+      break;
+    case 4:
+      pull_kernel_staged<4><<<grid, kThreads, smem, s>>>(dev);
+      break;
+    case 2:
+      pull_kernel_staged<2><<<grid, kThreads, smem, s>>>(dev);
+      break;
+    case 1:
+      pull_kernel_staged<1><<<grid, kThreads, smem, s>>>(dev);
+      break;
+    default:
+      pull_kernel_staged<0><<<grid, kThreads, smem, s>>>(dev);
+      break;
+  }
+  return cudaGetLastError();
+}
 
 // A batch whose descriptors share one unit class is one launch; a mixed batch
 // becomes one launch per class, in order on the stream (completion counters

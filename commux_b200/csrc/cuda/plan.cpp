@@ -224,6 +224,20 @@ class CudaPlan final : public DevicePlan {
         (pulls_.empty() ? pre_.back() : pulls_.back())->cta_trace = dd;
       }
     }
+    // every batch goes to device memory once: a launch passes one pointer,
+    // and each CTA stages the batch into shared memory (pull_kernel_staged)
+    const std::size_t nb = pre_.size() + pulls_.size();
+    if (nb > 0) {
+      batches_d_ = at::empty({static_cast<std::int64_t>(nb * sizeof(PullBatch))},
+                             at::TensorOptions().dtype(at::kByte).device(at::kCUDA, c_->dev));
+      std::size_t k = 0;
+      for (auto* ls : {&pre_, &pulls_})
+        for (auto& b : *ls) CMX_CUDA(cudaMemcpy(dev_batch(k++), b.get(), sizeof(PullBatch), cudaMemcpyHostToDevice));
+    }
+  }
+
+  PullBatch* dev_batch(std::size_t k) {
+    return reinterpret_cast<PullBatch*>(static_cast<char*>(batches_d_.data_ptr()) + k * sizeof(PullBatch));
   }
 
   // Grid cap of the launches. A launch whose CTAs wait on peers keeps every
@@ -449,11 +463,12 @@ class CudaPlan final : public DevicePlan {
     nodes_ = 0;
     CMX_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
     cudaError_t e = cudaSuccess;
+    std::size_t k = 0;
     for (auto* ls : {&pre_, &pulls_})
       for (auto& b : *ls) {
-        int launched = 0;
-        if (e == cudaSuccess) e = launch_pull(*b, ctas, 256, cs, &launched);
-        nodes_ += launched;
+        if (e == cudaSuccess) e = launch_pull_staged(*b, dev_batch(k), ctas, cs);
+        ++k;
+        ++nodes_;
       }
     // the receivers' "consumed" flags and the epoch bump ride on the last
     // launch (its last CTA waits and bumps; see PullBatch::bump); a plan
@@ -474,6 +489,7 @@ class CudaPlan final : public DevicePlan {
   at::Tensor state_;
   std::uint64_t* epoch_d_ = nullptr;
   unsigned int* cta_done_d_ = nullptr;
+  at::Tensor batches_d_;  // the launches' batches in device memory
   int max_ctas_ = 0;      // set_max_ctas (0: the default grid)
   bool has_flags_ = false;  // some message crosses to another GPU
   std::uint32_t* counters_d_ = nullptr;
