@@ -97,6 +97,7 @@ CollImpl::CollImpl(CudaTransport* tr, int dev)
     CMX_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&trace_d_), trace_h_, 0));
   }
   oneshot_bytes_ = env_int("COMMUX_ONESHOT_BYTES", P_ <= 2 ? 4ll << 20 : P_ <= 4 ? 2ll << 20 : 1ll << 20);
+  chain_ranks_ = static_cast<int>(env_int("COMMUX_CHAIN_RANKS", 3));
   // COMMUX_ALGO=oneshot|twoshot|nvls forces an algorithm for the reductions
   // where it applies (the others keep the size-based choice)
   if (const char* f = std::getenv("COMMUX_ALGO")) {
@@ -257,10 +258,10 @@ void CollImpl::fill(CollArgs& a, const Launch& l, const at::Tensor& in, const at
   a.op = l.op;
   a.dtype = dtype_code(in.scalar_type());
   a.elem_bytes = static_cast<int>(in.element_size());
-  // COMMUX_BCAST_SCATTER_RANKS: group size from which broadcasts scatter
-  // from the root and allgather (below it the root pushes to every peer)
-  static const int scatter_ranks = static_cast<int>(env_int("COMMUX_BCAST_SCATTER_RANKS", 3));
-  a.bcast_scatter_ranks = scatter_ranks;
+  // COMMUX_CHAIN_RANKS: group size from which broadcasts, and reduces of
+  // messages beyond one-shot, run along a chain of the ranks (below it the
+  // root pushes to every peer, and reduces take two-shot)
+  a.bcast_chain_ranks = chain_ranks_;
   a.n = l.n;
   a.in = in.data_ptr();
   a.out = out.data_ptr();
@@ -326,6 +327,8 @@ DevCollPtr CollImpl::run(const std::vector<Launch>& launches) {
       algo = kAlgoTwoShot;
     else if (oneshot_fits && bytes <= oneshot_bytes_)
       algo = kAlgoOneShot;
+    else if (l.mode == kModeReduce && P_ >= chain_ranks_)
+      algo = kAlgoChain;
     else if (nvls_fits && bytes >= nvls_min_bytes_)
       algo = kAlgoNvls;
     a.algo = algo;
@@ -336,8 +339,12 @@ DevCollPtr CollImpl::run(const std::vector<Launch>& launches) {
     if (trace_h_ != nullptr) report_trace(algo, l.mode, bytes, ctas);
     st_calls_++;
     st_bytes_ += bytes;
-    if (l.mode == kModeAllgather || l.mode == kModeBroadcast)
+    if (l.mode == kModeBroadcast && P_ >= chain_ranks_)
+      st_chain_++;
+    else if (l.mode == kModeAllgather || l.mode == kModeBroadcast)
       st_gather_++;
+    else if (algo == kAlgoChain)
+      st_chain_++;
     else if (algo == kAlgoOneShot)
       st_oneshot_++;
     else if (algo == kAlgoNvls)
@@ -420,7 +427,7 @@ std::vector<std::pair<std::string, std::int64_t>> CollImpl::stats() const {
   return {{"coll_calls", st_calls_},   {"coll_oneshot", st_oneshot_}, {"coll_twoshot", st_twoshot_},
           {"coll_gather", st_gather_}, {"coll_bytes", st_bytes_},     {"coll_shared_gpu", shared_gpu_ ? 1 : 0},
           {"coll_nvls", st_nvls_},     {"coll_nvls_enabled", nvls_ ? 1 : 0},
-          {"coll_barriers", st_barriers_}};
+          {"coll_barriers", st_barriers_}, {"coll_chain", st_chain_}};
 }
 
 // ---------------------------------------------------------------------------

@@ -65,7 +65,8 @@ class CollImpl {
   std::string nvls_why_;              // why not (empty when enabled or not attempted)
   std::int64_t nvls_min_bytes_ = 0;
   int forced_algo_ = -1;  // COMMUX_ALGO
-  std::int64_t st_barriers_ = 0;
+  std::int64_t st_barriers_ = 0, st_chain_ = 0;
+  int chain_ranks_ = 3;  // COMMUX_CHAIN_RANKS
   unsigned long long* trace_h_ = nullptr;  // COMMUX_COLL_TRACE (host-mapped)
   unsigned long long* trace_d_ = nullptr;
   void report_trace(int algo, int mode, std::int64_t bytes, int ctas);

@@ -33,7 +33,7 @@ enum CollMode : int {
   kModeBroadcast = 4,
   kModeBarrier = 5,
 };
-enum CollAlgo : int { kAlgoOneShot = 0, kAlgoTwoShot = 1, kAlgoNvls = 2 };
+enum CollAlgo : int { kAlgoOneShot = 0, kAlgoTwoShot = 1, kAlgoNvls = 2, kAlgoChain = 3 };
 enum CollOp : int { kOpSum = 0, kOpProd = 1, kOpMin = 2, kOpMax = 3, kOpAvg = 4 };
 enum CollDtype : int { kF32 = 0, kF64, kF16, kBF16, kI32, kI64, kU8, kI8 };
 
@@ -46,7 +46,7 @@ struct CollArgs {
   int op;
   int dtype;
   int elem_bytes;
-  int bcast_scatter_ranks;  // broadcast: scatter + allgather from this many ranks
+  int bcast_chain_ranks;  // broadcast: along a chain from this many ranks
   std::int64_t n;  // elements: allreduce/reduce total; reduce_scatter and
                    // allgather per-rank block; broadcast total
   const void* in;

@@ -38,9 +38,9 @@
 //   gather   (allgather/broadcast at 2 ranks), chunked: push my block into
 //            slot[me] of every rank's B (broadcast: the root's block into
 //            slot 0), flag round, copy out, flag round.
-//   bcast    (broadcast from 3 ranks): scatter from the root + allgather
-//            among the ranks, pipelined over double-buffered chunks (see
-//            bcast_kernel).
+//   chain    (broadcast, and reduce of large messages, from 3 ranks): the
+//            chunks of the message flow along a chain of the ranks, so
+//            every link carries the message once (see chain_kernel).
 //   barrier  one CTA: a system-scope fence (everything this rank's stream
 //            wrote before the barrier, local or into a peer's memory, is
 //            visible system-wide), a flag to every rank, a bounded wait for
@@ -568,91 +568,74 @@ __global__ void __launch_bounds__(kCollThreads, 2) gather_kernel(const __grid_co
   }
 }
 
-// ---- broadcast: scatter + allgather, pipelined over chunks ---------------------
+// ---- chain: pipelined broadcast and reduce (3 ranks and more) -----------------------
 //
-// Chunk c of the message is P pieces of `cap` elements; piece k belongs to
-// rank k. The root stores piece k into slot k of rank k's B quarter (c & 1)
-// and its own piece into slot root of every rank's quarter; each other rank
-// k forwards its piece to every rank but the root and itself, then copies
-// all P pieces out. The root's link carries about 2(P-1)/P of the message
-// (not P-1 times it), every other rank's about (P-2)/P. Flag phases: 0 =
-// root's stores of chunk c landed, 1 = rank k's forward of chunk c landed,
-// 2 = rank k copied chunk c out (its quarter may be refilled). A rank's
-// iteration c forwards chunk c and copies chunk c-1 out before its flag
-// stores, so the copy-out overlaps the forward's NVLink transfer.
-template <typename T>
-__global__ void __launch_bounds__(kCollThreads, 2) bcast_kernel(const __grid_constant__ CollArgs a) {
+// The ranks form a chain, and chunks of the message flow along it, so every
+// link carries the message once. In broadcast the chain starts at the root
+// and each rank copies every chunk out. In reduce it ends at the root: each
+// rank folds its own input into the partial result it received and passes it
+// on (the fold order is the chain order, rank root+1 first; partial results
+// travel in the message's type), and the root's fold writes the output.
+// Each call's half of region B holds kChainSlots chunk slots per rank; chunk c
+// goes to slot c % kChainSlots of the next rank. Flag phases, CTA b to CTA b:
+// 0 = "slot holds chunk c" (to the next rank), 1 = "slot of chunk c is free
+// again" (to the previous rank), 2 = the end-of-call round among all ranks
+// (no rank starts a call that reuses this half while another still reads
+// it). A rank waits on its predecessor's phase 0 and its successor's
+// phase 1, so no wait cycle can form.
+constexpr int kChainSlots = 4;
+
+template <typename T, int OP>
+__global__ void __launch_bounds__(kCollThreads, 2) chain_kernel(const __grid_constant__ CollArgs a) {
+  using Acc = typename AccT<T>::type;
+  constexpr int N = Packs<T>::N;
   const T* in = static_cast<const T*>(a.in);
   T* out = static_cast<T*>(a.out);
-  const int P = a.P, root = a.root, me = a.me;
-  const std::int64_t cap = slot_elems<T>(a, 2 * P);
-  const std::int64_t chunk = cap * P;
-  const std::int64_t nchunks = (a.n + chunk - 1) / chunk;
-  auto quarter = [&](int p, std::int64_t c) { return region_b<T>(a, p) + (c & 1) * P * cap; };
+  const int P = a.P;
+  const bool bcast = a.mode == kModeBroadcast;
+  // chain position: broadcast starts at the root, reduce ends at it
+  const int head = bcast ? a.root : (a.root + 1) % P;
+  const int k = (a.me - head + P) % P;
+  const int prev = (a.me + P - 1) % P, next = (a.me + 1) % P;
+  const std::int64_t cap = (a.region_bytes / 2) / static_cast<std::int64_t>(sizeof(T)) / kChainSlots / N * N;
+  const std::int64_t nchunks = (a.n + cap - 1) / cap;
+  auto slot = [&](int p, std::int64_t c) { return region_b<T>(a, p) + (c % kChainSlots) * cap; };
   auto seq = [&](std::int64_t c) { return a.seq_base + static_cast<std::uint64_t>(c) + 1; };
-  // element range [lo, hi) of this CTA's share of piece k of chunk c, as
-  // offsets in the message; base = first element of the piece
-  auto share = [&](std::int64_t c, int k, std::int64_t& base, std::int64_t& lo, std::int64_t& hi) {
-    base = c * chunk + static_cast<std::int64_t>(k) * cap;
-    const std::int64_t len = max(static_cast<std::int64_t>(0), min(cap, a.n - base));
-    piece<T>(len, gridDim.x, blockIdx.x, lo, hi);
-  };
-  if (me == root) {
-    for (std::int64_t c = 0; c < nchunks; ++c) {
-      if (c >= 2 && !await(a, 2, seq(c - 2))) return;
-      for (int q = 1; q < P; ++q) {
-        const int p = (me + q) % P;
-        std::int64_t base, lo, hi;
-        share(c, p, base, lo, hi);  // p's own piece
-        copy_range(quarter(p, c) + p * cap - base, in, base + lo, base + hi);
-        share(c, root, base, lo, hi);  // the root's piece
-        copy_range(quarter(p, c) + root * cap - base, in, base + lo, base + hi);
+  const std::uint64_t last = a.seq_base + static_cast<std::uint64_t>(nchunks) + 1;
+  for (std::int64_t c = 0; c < nchunks; ++c) {
+    const std::int64_t c0 = c * cap;
+    std::int64_t lo, hi;
+    piece<T>(min(cap, a.n - c0), gridDim.x, blockIdx.x, lo, hi);
+    const bool first = k == 0, tail = k == P - 1;
+    if (!first && !await(a, 0, seq(c), prev)) return;
+    T* mine = slot(a.me, c) - c0;  // index the slot with message offsets
+    if (!tail && c >= kChainSlots && !await(a, 1, seq(c - kChainSlots), next)) return;
+    T* dst = tail ? nullptr : slot(next, c) - c0;
+    if (bcast) {
+      const T* src = first ? in : mine;
+      if (!tail) copy_range(dst, src, c0 + lo, c0 + hi);
+      if (!first || out != in) copy_range(out, src, c0 + lo, c0 + hi);
+    } else if (first) {
+      copy_range(dst, in, c0 + lo, c0 + hi);
+    } else {
+      // partial (from the previous rank) op my input -> the next rank, or
+      // (at the root) -> the output; elementwise, fp32 accumulation
+      T* to = tail ? out : dst;
+      for (std::int64_t i = c0 + lo + static_cast<std::int64_t>(threadIdx.x); i < c0 + hi; i += blockDim.x) {
+        Acc v = combine<OP>(to_acc<Acc>(mine[i]), to_acc<Acc>(in[i]));
+        if constexpr (OP == kOpAvg)
+          if (tail) v = v / static_cast<Acc>(P);
+        to[i] = from_acc<T>(v);
       }
-      if (out != in) {
-        std::int64_t lo, hi;
-        piece<T>(min(chunk, a.n - c * chunk), gridDim.x, blockIdx.x, lo, hi);
-        copy_range(out, in, c * chunk + lo, c * chunk + hi);
-      }
-      signal(a, 0, seq(c));
-      // the root forwards and copies out nothing: its phases 1 and 2 of the
-      // chunk hold at once (the others wait on every rank's flags)
-      signal(a, 1, seq(c));
-      signal(a, 2, seq(c));
     }
-    // every rank has copied the last chunk out before the root leaves: a
-    // later call cannot reach this call's half of the workspace while a peer
-    // still reads it
-    if (nchunks >= 1) await(a, 2, seq(nchunks - 1));
-    return;
+    if (!tail) signal(a, 0, seq(c), next);
+    if (!first) signal(a, 1, seq(c), prev);
   }
-  for (std::int64_t c = 0; c <= nchunks; ++c) {
-    if (c < nchunks) {
-      if (c >= 2 && !await(a, 2, seq(c - 2))) return;
-      if (!await(a, 0, seq(c), root)) return;
-      std::int64_t base, lo, hi;
-      share(c, me, base, lo, hi);
-      const T* mine = quarter(me, c) + me * cap - base;
-      for (int q = 1; q < P; ++q) {
-        const int p = (me + q) % P;
-        if (p == root) continue;
-        copy_range(quarter(p, c) + me * cap - base, mine, base + lo, base + hi);
-      }
-    }
-    if (c >= 1) {
-      const std::int64_t f = c - 1;
-      if (!await(a, 1, seq(f))) return;
-      for (int k = 0; k < P; ++k) {
-        std::int64_t base, lo, hi;
-        share(f, k, base, lo, hi);
-        copy_range(out, quarter(me, f) + k * cap - base, base + lo, base + hi);
-      }
-    }
-    if (c < nchunks) signal(a, 1, seq(c));
-    if (c >= 1) signal(a, 2, seq(c - 1));
-  }
+  signal(a, 2, last);
+  await(a, 2, last);
 }
 
-// ---- nvls ------------------------------------------------------------------------
+// ---- nvls ----// ---- nvls ------------------------------------------------------------------------
 
 __device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
 
@@ -862,6 +845,10 @@ cudaError_t launch_nvls(const CollArgs& a, int ctas, cudaStream_t s) {
 template <typename T, int OP>
 cudaError_t launch_reduce_family(const CollArgs& a, int ctas, cudaStream_t s) {
   if (a.algo == kAlgoNvls) return launch_nvls<T>(a, ctas, s);
+  if (a.algo == kAlgoChain) {
+    chain_kernel<T, OP><<<ctas, kCollThreads, 0, s>>>(a);
+    return cudaGetLastError();
+  }
   if (a.algo == kAlgoOneShot)
     oneshot_kernel<T, OP><<<ctas, kCollThreads, 0, s>>>(a);
   else
@@ -896,22 +883,22 @@ cudaError_t launch_barrier(const CollArgs& a, cudaStream_t s) {
 
 cudaError_t launch_coll(const CollArgs& a, int ctas, cudaStream_t s) {
   if (ctas < 1 || ctas > kMaxCollCtas || a.P > kMaxCollRanks) return cudaErrorInvalidValue;
-  // broadcast: the root pushes to every peer below a.bcast_scatter_ranks
-  // ranks (at 2 ranks one link either way); from there scatter + allgather,
-  // so the root's link carries about 2(P-1)/P of the message, not P-1 times it
-  if (a.mode == kModeBroadcast && a.P >= a.bcast_scatter_ranks) {
+  // broadcast: the root pushes to every peer below a.bcast_chain_ranks
+  // ranks (at 2 ranks one link either way); from there along a chain, so
+  // every link carries the message once instead of the root's P-1 times
+  if (a.mode == kModeBroadcast && a.P >= a.bcast_chain_ranks) {
     switch (a.elem_bytes) {
       case 1:
-        bcast_kernel<std::uint8_t><<<ctas, kCollThreads, 0, s>>>(a);
+        chain_kernel<std::uint8_t, kOpSum><<<ctas, kCollThreads, 0, s>>>(a);
         break;
       case 2:
-        bcast_kernel<std::uint16_t><<<ctas, kCollThreads, 0, s>>>(a);
+        chain_kernel<std::uint16_t, kOpSum><<<ctas, kCollThreads, 0, s>>>(a);
         break;
       case 4:
-        bcast_kernel<std::uint32_t><<<ctas, kCollThreads, 0, s>>>(a);
+        chain_kernel<std::uint32_t, kOpSum><<<ctas, kCollThreads, 0, s>>>(a);
         break;
       case 8:
-        bcast_kernel<std::uint64_t><<<ctas, kCollThreads, 0, s>>>(a);
+        chain_kernel<std::uint64_t, kOpSum><<<ctas, kCollThreads, 0, s>>>(a);
         break;
       default:
         return cudaErrorInvalidValue;

@@ -160,7 +160,10 @@ def test_collective_numerics_cuda(variant):
     # every rank on its own GPU (up to 8): the device kernels of the variant
     world = max(2, min(ngpu(), 8))
     extra, expect = COLL_VARIANTS[variant]
-    env = topology("peer", world, (PEER_COLL + "," + expect + ",coll_gather>0", None))
+    # broadcasts: the root pushes at 2 ranks, and run along a chain from 3
+    # ranks (where large reduces take the chain too)
+    bcast = ",coll_gather>0" if world == 2 else ",coll_chain>0"
+    env = topology("peer", world, (PEER_COLL + "," + expect + bcast, None))
     check(run("gpu_coll_numerics.py", world, env=dict(env, **extra), timeout=600))
 
 
