@@ -97,7 +97,7 @@ CollImpl::CollImpl(CudaTransport* tr, int dev)
     CMX_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&trace_d_), trace_h_, 0));
   }
   oneshot_bytes_ = env_int("COMMUX_ONESHOT_BYTES", P_ <= 2 ? 4ll << 20 : P_ <= 4 ? 2ll << 20 : 1ll << 20);
-  chain_ranks_ = static_cast<int>(env_int("COMMUX_CHAIN_RANKS", 3));
+  chain_ranks_ = static_cast<int>(env_int("COMMUX_CHAIN_RANKS", 0));
   // COMMUX_ALGO=oneshot|twoshot|nvls forces an algorithm for the reductions
   // where it applies (the others keep the size-based choice)
   if (const char* f = std::getenv("COMMUX_ALGO")) {
@@ -259,8 +259,8 @@ void CollImpl::fill(CollArgs& a, const Launch& l, const at::Tensor& in, const at
   a.dtype = dtype_code(in.scalar_type());
   a.elem_bytes = static_cast<int>(in.element_size());
   // COMMUX_CHAIN_RANKS: group size from which broadcasts, and reduces of
-  // messages beyond one-shot, run along a chain of the ranks (below it the
-  // root pushes to every peer, and reduces take two-shot)
+  // messages beyond one-shot, run along a chain of the ranks (0: never, the
+  // default; the chain measured slower than scatter + allgather and two-shot)
   a.bcast_chain_ranks = chain_ranks_;
   a.n = l.n;
   a.in = in.data_ptr();
@@ -327,7 +327,7 @@ DevCollPtr CollImpl::run(const std::vector<Launch>& launches) {
       algo = kAlgoTwoShot;
     else if (oneshot_fits && bytes <= oneshot_bytes_)
       algo = kAlgoOneShot;
-    else if (l.mode == kModeReduce && P_ >= chain_ranks_)
+    else if (l.mode == kModeReduce && chain_ranks_ > 0 && P_ >= chain_ranks_)
       algo = kAlgoChain;
     else if (nvls_fits && bytes >= nvls_min_bytes_)
       algo = kAlgoNvls;
@@ -339,7 +339,7 @@ DevCollPtr CollImpl::run(const std::vector<Launch>& launches) {
     if (trace_h_ != nullptr) report_trace(algo, l.mode, bytes, ctas);
     st_calls_++;
     st_bytes_ += bytes;
-    if (l.mode == kModeBroadcast && P_ >= chain_ranks_)
+    if (l.mode == kModeBroadcast && chain_ranks_ > 0 && P_ >= chain_ranks_)
       st_chain_++;
     else if (l.mode == kModeAllgather || l.mode == kModeBroadcast)
       st_gather_++;

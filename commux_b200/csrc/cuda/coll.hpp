@@ -66,7 +66,7 @@ class CollImpl {
   std::int64_t nvls_min_bytes_ = 0;
   int forced_algo_ = -1;  // COMMUX_ALGO
   std::int64_t st_barriers_ = 0, st_chain_ = 0;
-  int chain_ranks_ = 3;  // COMMUX_CHAIN_RANKS
+  int chain_ranks_ = 0;  // COMMUX_CHAIN_RANKS (0: the chain is off)
   unsigned long long* trace_h_ = nullptr;  // COMMUX_COLL_TRACE (host-mapped)
   unsigned long long* trace_d_ = nullptr;
   void report_trace(int algo, int mode, std::int64_t bytes, int ctas);

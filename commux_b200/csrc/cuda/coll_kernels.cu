@@ -38,7 +38,10 @@
 //   gather   (allgather/broadcast at 2 ranks), chunked: push my block into
 //            slot[me] of every rank's B (broadcast: the root's block into
 //            slot 0), flag round, copy out, flag round.
-//   chain    (broadcast, and reduce of large messages, from 3 ranks): the
+//   bcast    (broadcast from 3 ranks): scatter from the root + allgather
+//            among the ranks, pipelined over double-buffered chunks (see
+//            bcast_kernel).
+//   chain    (opt-in, COMMUX_CHAIN_RANKS: broadcast and large reduce): the
 //            chunks of the message flow along a chain of the ranks, so
 //            every link carries the message once (see chain_kernel).
 //   barrier  one CTA: a system-scope fence (everything this rank's stream
@@ -568,7 +571,97 @@ __global__ void __launch_bounds__(kCollThreads, 2) gather_kernel(const __grid_co
   }
 }
 
-// ---- chain: pipelined broadcast and reduce (3 ranks and more) -----------------------
+// ---- broadcast: scatter + allgather, pipelined over chunks ---------------------
+//
+// Chunk c of the message is P pieces of `cap` elements; piece k belongs to
+// rank k. The root stores piece k into slot k of rank k's B quarter (c & 1)
+// and its own piece into slot root of every rank's quarter; each other rank
+// k forwards its piece to every rank but the root and itself, then copies
+// all P pieces out. The root's link carries about 2(P-1)/P of the message
+// (not P-1 times it), every other rank's about (P-2)/P. Flag phases: 0 =
+// root's stores of chunk c landed, 1 = rank k's forward of chunk c landed,
+// 2 = rank k copied chunk c out (its quarter may be refilled). A rank's
+// iteration c forwards chunk c and copies chunk c-1 out before its flag
+// stores, so the copy-out overlaps the forward's NVLink transfer.
+template <typename T>
+__global__ void __launch_bounds__(kCollThreads, 2) bcast_kernel(const __grid_constant__ CollArgs a) {
+  const T* in = static_cast<const T*>(a.in);
+  T* out = static_cast<T*>(a.out);
+  const int P = a.P, root = a.root, me = a.me;
+  const std::int64_t cap = slot_elems<T>(a, 2 * P);
+  const std::int64_t chunk = cap * P;
+  const std::int64_t nchunks = (a.n + chunk - 1) / chunk;
+  auto quarter = [&](int p, std::int64_t c) { return region_b<T>(a, p) + (c & 1) * P * cap; };
+  auto seq = [&](std::int64_t c) { return a.seq_base + static_cast<std::uint64_t>(c) + 1; };
+  // element range [lo, hi) of this CTA's share of piece k of chunk c, as
+  // offsets in the message; base = first element of the piece
+  auto share = [&](std::int64_t c, int k, std::int64_t& base, std::int64_t& lo, std::int64_t& hi) {
+    base = c * chunk + static_cast<std::int64_t>(k) * cap;
+    const std::int64_t len = max(static_cast<std::int64_t>(0), min(cap, a.n - base));
+    piece<T>(len, gridDim.x, blockIdx.x, lo, hi);
+  };
+  if (me == root) {
+    for (std::int64_t c = 0; c < nchunks; ++c) {
+      if (c >= 2 && !await(a, 2, seq(c - 2))) return;
+      for (int q = 1; q < P; ++q) {
+        const int p = (me + q) % P;
+        std::int64_t base, lo, hi;
+        share(c, p, base, lo, hi);  // p's own piece
+        copy_range(quarter(p, c) + p * cap - base, in, base + lo, base + hi);
+        share(c, root, base, lo, hi);  // the root's piece
+        copy_range(quarter(p, c) + root * cap - base, in, base + lo, base + hi);
+      }
+      if (out != in) {
+        std::int64_t lo, hi;
+        piece<T>(min(chunk, a.n - c * chunk), gridDim.x, blockIdx.x, lo, hi);
+        copy_range(out, in, c * chunk + lo, c * chunk + hi);
+      }
+      signal(a, 0, seq(c));
+      // the root forwards and copies out nothing: its phases 1 and 2 of the
+      // chunk hold at once (the others wait on every rank's flags)
+      signal(a, 1, seq(c));
+      signal(a, 2, seq(c));
+    }
+    // every rank has copied the last chunk out before the root leaves: a
+    // later call cannot reach this call's half of the workspace while a peer
+    // still reads it
+    if (nchunks >= 1) await(a, 2, seq(nchunks - 1));
+    return;
+  }
+  for (std::int64_t c = 0; c <= nchunks; ++c) {
+    if (c < nchunks) {
+      if (c >= 2 && !await(a, 2, seq(c - 2))) return;
+      if (!await(a, 0, seq(c), root)) return;
+      std::int64_t base, lo, hi;
+      share(c, me, base, lo, hi);
+      const T* mine = quarter(me, c) + me * cap - base;
+      for (int q = 1; q < P; ++q) {
+        const int p = (me + q) % P;
+        if (p == root) continue;
+        copy_range(quarter(p, c) + me * cap - base, mine, base + lo, base + hi);
+      }
+    }
+    if (c >= 1) {
+      const std::int64_t f = c - 1;
+      if (!await(a, 1, seq(f))) return;
+      for (int k = 0; k < P; ++k) {
+        std::int64_t base, lo, hi;
+        share(f, k, base, lo, hi);
+        copy_range(out, quarter(me, f) + k * cap - base, base + lo, base + hi);
+      }
+    }
+    if (c < nchunks) signal(a, 1, seq(c));
+    if (c >= 1) signal(a, 2, seq(c - 1));
+  }
+}
+
+// ---- chain: pipelined broadcast and reduce (opt-in) ---------------------------------
+//
+// Measured at 4 ranks (1 GiB fp32): broadcast 3556 us against 3200 us for
+// scatter + allgather and 1630 us for NCCL; reduce 3730 us against 2637 us
+// for two-shot. Every hop waits for its predecessor's per-chunk flag, which
+// a CTA stores only after its posted stores have landed, so a link runs at
+// about 300 GB/s. COMMUX_CHAIN_RANKS=<n> selects it from n ranks.
 //
 // The ranks form a chain, and chunks of the message flow along it, so every
 // link carries the message once. In broadcast the chain starts at the root
@@ -883,10 +976,30 @@ cudaError_t launch_barrier(const CollArgs& a, cudaStream_t s) {
 
 cudaError_t launch_coll(const CollArgs& a, int ctas, cudaStream_t s) {
   if (ctas < 1 || ctas > kMaxCollCtas || a.P > kMaxCollRanks) return cudaErrorInvalidValue;
-  // broadcast: the root pushes to every peer below a.bcast_chain_ranks
-  // ranks (at 2 ranks one link either way); from there along a chain, so
-  // every link carries the message once instead of the root's P-1 times
-  if (a.mode == kModeBroadcast && a.P >= a.bcast_chain_ranks) {
+  // broadcast: the root pushes to every peer at 2 ranks (one link either
+  // way); from 3 ranks scatter + allgather (the root's link carries about
+  // 2(P-1)/P of the message, not P-1 times it), or the pipelined chain where
+  // COMMUX_CHAIN_RANKS enables it (a.bcast_chain_ranks > 0)
+  if (a.mode == kModeBroadcast && a.P > 2 && !(a.bcast_chain_ranks > 0 && a.P >= a.bcast_chain_ranks)) {
+    switch (a.elem_bytes) {
+      case 1:
+        bcast_kernel<std::uint8_t><<<ctas, kCollThreads, 0, s>>>(a);
+        break;
+      case 2:
+        bcast_kernel<std::uint16_t><<<ctas, kCollThreads, 0, s>>>(a);
+        break;
+      case 4:
+        bcast_kernel<std::uint32_t><<<ctas, kCollThreads, 0, s>>>(a);
+        break;
+      case 8:
+        bcast_kernel<std::uint64_t><<<ctas, kCollThreads, 0, s>>>(a);
+        break;
+      default:
+        return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+  }
+  if (a.mode == kModeBroadcast && a.P > 2) {
     switch (a.elem_bytes) {
       case 1:
         chain_kernel<std::uint8_t, kOpSum><<<ctas, kCollThreads, 0, s>>>(a);

@@ -152,6 +152,9 @@ COLL_VARIANTS = {
     # a 1 MiB workspace: every two-shot reduction and broadcast runs through
     # dozens of double-buffered chunks (pipeline fill, steady state, drain)
     "pipeline": ({"COMMUX_NVLS": "0", "COMMUX_CUDA_WS_BYTES": "1048576"}, "coll_twoshot>0"),
+    # the opt-in chain (broadcast and large reduce along a chain of the
+    # ranks), through many chunks; at 2 ranks it is not selected
+    "chain": ({"COMMUX_NVLS": "0", "COMMUX_CUDA_WS_BYTES": "1048576", "COMMUX_CHAIN_RANKS": "3"}, "coll_calls>0"),
 }
 
 
@@ -160,10 +163,9 @@ def test_collective_numerics_cuda(variant):
     # every rank on its own GPU (up to 8): the device kernels of the variant
     world = max(2, min(ngpu(), 8))
     extra, expect = COLL_VARIANTS[variant]
-    # broadcasts: the root pushes at 2 ranks, and run along a chain from 3
-    # ranks (where large reduces take the chain too)
-    bcast = ",coll_gather>0" if world == 2 else ",coll_chain>0"
-    env = topology("peer", world, (PEER_COLL + "," + expect + bcast, None))
+    if variant == "chain" and world >= 3:
+        expect += ",coll_chain>0"
+    env = topology("peer", world, (PEER_COLL + "," + expect + ",coll_gather>0", None))
     check(run("gpu_coll_numerics.py", world, env=dict(env, **extra), timeout=600))
 
 
