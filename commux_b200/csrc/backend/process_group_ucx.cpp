@@ -754,7 +754,8 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::recvAnysource(std::vector<at::Te
       engine_->wait(reqs[0], std::chrono::milliseconds(0));
       int src = reqs[0]->source;
       for (std::size_t i = 1; i < tensors.size(); ++i)
-        reqs.push_back(engine_->post_recv({tensors[i]}, src, make_ucp_tag(0, ut, static_cast<std::uint32_t>(i), false)));
+        reqs.push_back(
+            engine_->post_recv({tensors[i]}, src, make_ucp_tag(0, ut, static_cast<std::uint32_t>(i), false)));
     }
   }
   return c10::make_intrusive<CommuxWork>(engine_.get(), c10d::OpType::RECVANYSOURCE, reqs, tensors);
@@ -925,7 +926,8 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupUCX::barrier(const c10d::BarrierOptio
   DeviceTransport* dev = engine_->any_remote() ? nullptr : engine_->device(false);
   bool on_device = dev != nullptr && dev->collectives_ready();
   if (!on_device && !opts.device_ids.empty() && !engine_->any_remote()) {
-    at::Tensor probe = at::empty({0}, at::TensorOptions().device(at::kCUDA, static_cast<c10::DeviceIndex>(opts.device_ids[0])));
+    const auto idx = static_cast<c10::DeviceIndex>(opts.device_ids[0]);
+    at::Tensor probe = at::empty({0}, at::TensorOptions().device(at::kCUDA, idx));
     on_device = device_coll(probe);
     dev = engine_->device(false);
   }

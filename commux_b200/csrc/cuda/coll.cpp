@@ -182,7 +182,10 @@ CollImpl::CollImpl(CudaTransport* tr, int dev)
        "(>= %lld bytes), COMMUX_ALGO %s",
        dev_, static_cast<long long>(region_bytes_), static_cast<long long>(oneshot_bytes_),
        nvls_ ? "on" : "off: ", nvls_ ? "" : nvls_why_.c_str(), static_cast<long long>(nvls_min_bytes_),
-       forced_algo_ < 0 ? "auto" : forced_algo_ == kAlgoOneShot ? "oneshot" : forced_algo_ == kAlgoTwoShot ? "twoshot" : "nvls");
+       forced_algo_ < 0                ? "auto"
+       : forced_algo_ == kAlgoOneShot ? "oneshot"
+       : forced_algo_ == kAlgoTwoShot ? "twoshot"
+                                      : "nvls");
 }
 
 // COMMUX_COLL_TRACE=1: after each collective (synchronously), one line per

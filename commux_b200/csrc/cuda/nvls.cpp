@@ -175,7 +175,8 @@ std::unique_ptr<NvlsBuffer> NvlsBuffer::create(Engine* eng, int dev, std::size_t
           break;
         }
         int c = ::accept4(lsock, nullptr, nullptr, SOCK_CLOEXEC);
-        if (c < 0 || !send_fd(c, fd)) fail_here(std::string("nvls: sending the handle: ") + std::strerror(errno));
+        if (c < 0 || !send_fd(c, fd))
+          fail_here(std::string("nvls: sending the handle: ") + std::strerror(errno));
         if (c >= 0) ::close(c);
         if (!err.empty()) break;
       }
@@ -224,7 +225,8 @@ std::unique_ptr<NvlsBuffer> NvlsBuffer::create(Engine* eng, int dev, std::size_t
   }
   store_set(eng, base + "added/" + std::to_string(me), err.empty() ? "1" : "0");
   for (int p = 0; p < P; ++p)
-    if (store_get(eng, base + "added/" + std::to_string(p)) != "1") fail_here("a peer could not join the multicast object");
+    if (store_get(eng, base + "added/" + std::to_string(p)) != "1")
+      fail_here("a peer could not join the multicast object");
 
   // 3. bind this rank's memory and map it twice (unicast and multicast)
   if (err.empty()) {

@@ -263,12 +263,11 @@ class CudaPlan final : public DevicePlan {
     if (n_shared_) {
       tr_->begin_batch();
       try {
+        auto tag = [](const Msg& m) { return make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), 0, false); };
         for (auto& m : recvs)
-          if (m.mode == PlanMode::Shared)
-            shared.push_back(eng_->post_recv({m.t}, m.peer, make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), 0, false)));
+          if (m.mode == PlanMode::Shared) shared.push_back(eng_->post_recv({m.t}, m.peer, tag(m)));
         for (auto& m : sends)
-          if (m.mode == PlanMode::Shared)
-            shared.push_back(eng_->post_send({m.t}, m.peer, make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), 0, false)));
+          if (m.mode == PlanMode::Shared) shared.push_back(eng_->post_send({m.t}, m.peer, tag(m)));
       } catch (...) {
         tr_->end_batch();
         throw;
@@ -631,9 +630,8 @@ DevicePlanPtr CudaTransport::create_plan(const std::vector<at::Tensor>& recv_t, 
       pending_sends.push_back(eng_->post_send({bytes_tensor(blob.data(), blob.size())}, m.peer,
                                               make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), kPlanSub, true)));
       at::Tensor rb = at::empty({static_cast<std::int64_t>(sizeof(PlanReply))}, at::TensorOptions().dtype(at::kByte));
-      reply_recvs.push_back({plan->sends.size(),
-                             eng_->post_recv({rb}, m.peer, make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), kPlanReplySub, true)),
-                             rb});
+      const auto rtag = make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), kPlanReplySub, true);
+      reply_recvs.push_back({plan->sends.size(), eng_->post_recv({rb}, m.peer, rtag), rb});
     }
     plan->sends.push_back(std::move(m));
   }
@@ -648,9 +646,8 @@ DevicePlanPtr CudaTransport::create_plan(const std::vector<at::Tensor>& recv_t, 
       m.mode = PlanMode::Local;
     } else {
       at::Tensor db = at::empty({static_cast<std::int64_t>(wire_len)}, at::TensorOptions().dtype(at::kByte));
-      desc_recvs.push_back({plan->recvs.size(),
-                            eng_->post_recv({db}, m.peer, make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), kPlanSub, true)),
-                            db});
+      const auto dtag = make_ucp_tag(0, static_cast<std::uint32_t>(m.tag), kPlanSub, true);
+      desc_recvs.push_back({plan->recvs.size(), eng_->post_recv({db}, m.peer, dtag), db});
     }
     plan->recvs.push_back(std::move(m));
   }

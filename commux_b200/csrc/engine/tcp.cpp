@@ -296,7 +296,8 @@ bool Links::pump_peer(Peer& P, bool* want_out, bool* blocked_in) {
   bool work = false;
   auto fail = [&](const std::string& why) {
     P.dead = true;
-    if (dead_) dead_(P.p, "commux: peer rank " + std::to_string(P.p) + " failed: its TCP connection was lost (" + why + ")");
+    if (dead_)
+      dead_(P.p, "commux: peer rank " + std::to_string(P.p) + " failed: its TCP connection was lost (" + why + ")");
   };
   // outbound: whole records from the out-ring, in order
   static const char kZeros[8] = {};
@@ -325,7 +326,8 @@ bool Links::pump_peer(Peer& P, bool* want_out, bool* blocked_in) {
       int k = 0;
       std::uint64_t off = P.ioff;
       if (off < hb) {
-        iov[k++] = {const_cast<char*>(reinterpret_cast<const char*>(ir.head)) + off, static_cast<std::size_t>(hb - off)};
+        char* head = const_cast<char*>(reinterpret_cast<const char*>(ir.head));
+        iov[k++] = {head + off, static_cast<std::size_t>(hb - off)};
         off = hb;
       }
       if (off < hb + pb) {
@@ -490,7 +492,8 @@ void Links::pump() {
         const bool consumed = c->head.load(std::memory_order_acquire) == c->tail.load(std::memory_order_acquire);
         if (pe->rlen == 0 && consumed) {
           pe->dead = true;
-          if (dead_) dead_(pe->p, "commux: peer rank " + std::to_string(pe->p) + " failed: it closed its TCP connection");
+          if (dead_)
+            dead_(pe->p, "commux: peer rank " + std::to_string(pe->p) + " failed: it closed its TCP connection");
           continue;
         }
         blocked = true;  // re-check soon

@@ -39,10 +39,12 @@ Nvml& nvml() {
     if (x.lib == nullptr) return x;
     auto sym = [&](const char* a) { return dlsym(x.lib, a); };
     x.init = reinterpret_cast<nvmlReturn_t (*)()>(sym("nvmlInit_v2"));
-    x.by_bus_id = reinterpret_cast<nvmlReturn_t (*)(const char*, nvmlDevice_t*)>(sym("nvmlDeviceGetHandleByPciBusId_v2"));
+    x.by_bus_id =
+        reinterpret_cast<nvmlReturn_t (*)(const char*, nvmlDevice_t*)>(sym("nvmlDeviceGetHandleByPciBusId_v2"));
     x.by_index = reinterpret_cast<nvmlReturn_t (*)(unsigned int, nvmlDevice_t*)>(sym("nvmlDeviceGetHandleByIndex_v2"));
     x.clock = reinterpret_cast<nvmlReturn_t (*)(nvmlDevice_t, int, unsigned int*)>(sym("nvmlDeviceGetClockInfo"));
-    x.max_clock = reinterpret_cast<nvmlReturn_t (*)(nvmlDevice_t, int, unsigned int*)>(sym("nvmlDeviceGetMaxClockInfo"));
+    x.max_clock =
+        reinterpret_cast<nvmlReturn_t (*)(nvmlDevice_t, int, unsigned int*)>(sym("nvmlDeviceGetMaxClockInfo"));
     x.reasons = reinterpret_cast<nvmlReturn_t (*)(nvmlDevice_t, unsigned long long*)>(
         sym("nvmlDeviceGetCurrentClocksEventReasons"));
     if (x.reasons == nullptr)

@@ -316,8 +316,9 @@ void check_noalloc_plan(std::mt19937_64& rng, int iters) {
     std::sort(got.begin(), got.end());
     if (got != want) {
       char buf[160];
-      std::snprintf(buf, sizeof(buf), "noalloc iteration %d: %zu pairs walked, %zu expected (nd %d, elem %lld, cap %lld)",
-                    it, got.size(), want.size(), nd, static_cast<long long>(elem), static_cast<long long>(cap));
+      std::snprintf(buf, sizeof(buf),
+                    "noalloc iteration %d: %zu pairs walked, %zu expected (nd %d, elem %lld, cap %lld)", it,
+                    got.size(), want.size(), nd, static_cast<long long>(elem), static_cast<long long>(cap));
       fail(buf);
     }
   }
