@@ -48,7 +48,8 @@
 //            wrote before the barrier, local or into a peer's memory, is
 //            visible system-wide), a flag to every rank, a bounded wait for
 //            every rank's flag.
-//   nvls     (large allreduce of f32/f16/bf16), pipelined the same way:
+//   nvls     (large allreduce of f32/f16/bf16), pipelined over double-
+//            buffered chunks by two warp groups (see "warp groups" below):
 //            copy my data into my NVLS buffer, flag round, multimem.ld_reduce
 //            my segment through the multicast mapping (NVSwitch sums every
 //            rank's copy) and multimem.st the result back (the switch writes
@@ -287,10 +288,10 @@ __global__ void __launch_bounds__(kCollThreads, 2) oneshot_kernel(const __grid_c
 
 // ---- warp groups -------------------------------------------------------------
 //
-// The pipelined kernels split each CTA into two warp groups: the "link" group
-// moves data across NVLink (posted stores into peers' workspaces, or multimem
-// operations), the "local" group folds and copies within this GPU's HBM. Chunk
-// c+1 crosses NVLink while chunk c is folded and copied out. Each group syncs
+// nvls_kernel splits each CTA into two warp groups: the "link" group moves
+// data across NVLink (multimem operations through the multicast mapping), the
+// "local" group copies within this GPU's HBM. Chunk c+1 is copied in while
+// chunk c is reduced through the switch and chunk c-1 copied out. Each group syncs
 // only on its own named barrier; the groups meet through flags (global, for
 // every rank, including this one) and through a shared-memory counter polled
 // with a bounded wait, never through a barrier they must both reach, so a

@@ -177,24 +177,24 @@ class CudaPlan final : public DevicePlan {
       first.nsig = static_cast<std::uint32_t>(ready_only.size());
       for (std::size_t k = 0; k < ready_only.size(); ++k) first.sig[k] = ready_only[k];
     }
-    std::memset(&wait_, 0, sizeof(wait_));  // the "consumed" flags of the sends to other GPUs
+    std::vector<const std::uint64_t*> fins;  // the "consumed" flags of the sends to other GPUs
     for (auto& m : sends)
       if (m.mode == PlanMode::Device) {
-        TORCH_CHECK(wait_.n < static_cast<std::uint32_t>(kMaxWaitFlags), "commux plan: more than ",
+        TORCH_CHECK(fins.size() < static_cast<std::size_t>(kMaxWaitFlags), "commux plan: more than ",
                     kMaxWaitFlags, " sends to other GPUs");
-        wait_.flag[wait_.n++] = m.consumed_local;
+        fins.push_back(m.consumed_local);
       }
     // the receivers' "consumed" flags and the epoch bump ride on the last
     // launch: its last CTA waits for them and advances the epoch
-    bool flags = wait_.n > 0;
+    bool flags = !fins.empty();
     for (auto& m : recvs) flags |= m.mode == PlanMode::Device;
     PullBatch* last = !pulls_.empty() ? pulls_.back().get() : !pre_.empty() ? pre_.back().get() : nullptr;
     TORCH_CHECK(!flags || last != nullptr, "commux plan: internal error, flags without a launch");
     if (flags) {
       last->bump = epoch_d_;
       last->cta_done = cta_done_d_;
-      last->nfin = wait_.n;
-      for (std::uint32_t k = 0; k < wait_.n; ++k) last->fin[k] = wait_.flag[k];
+      last->nfin = static_cast<std::uint32_t>(fins.size());
+      for (std::size_t k = 0; k < fins.size(); ++k) last->fin[k] = fins[k];
     }
     // COMMUX_PLAN_TRACE: span of every launch of a start (earliest CTA start,
     // latest CTA end), printed after each start (which then synchronises)
@@ -493,7 +493,6 @@ class CudaPlan final : public DevicePlan {
   bool has_flags_ = false;  // some message crosses to another GPU
   std::uint32_t* counters_d_ = nullptr;
   std::vector<std::unique_ptr<PullBatch>> pre_, pulls_;
-  WaitBatch wait_{};
   cudaGraph_t graph_ = nullptr;
   cudaGraphExec_t exec_ = nullptr;
   std::int64_t nodes_ = 0;
