@@ -9,6 +9,8 @@ reported as algorithm bandwidth and bus bandwidth (allreduce: 2(P-1)/P x size
 / time; reduce/broadcast: size / time) and as the fraction of the NVLink
 roofline (bus bandwidth / 770 GB/s, the measured peer-copy rate per direction).
 NCCL runs in the same process on a second process group as the comparator.
+Each row names the device algorithm the timed commux calls took on rank 0
+(`commux_path`, from the backend's per-algorithm counters).
 
     torchrun --nproc-per-node 8 benchmarks/collectives_sweep.py --max-bytes 1073741824
 """
@@ -22,6 +24,12 @@ import os
 import sys
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+# per-algorithm call counters of the device collectives (commux.stats());
+# "gather" counts the allgather and broadcast kernels (root push, scatter +
+# allgather)
+PATHS = ("oneshot", "twoshot", "nvls", "gather", "chain")
 
 
 def main():
@@ -56,6 +64,9 @@ def main():
         groups["nccl"] = dist.new_group(backend="nccl")
     dt = {"fp32": torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}
     ops = {"sum": dist.ReduceOp.SUM, "max": dist.ReduceOp.MAX, "avg": dist.ReduceOp.AVG}
+    def path_counters():
+        return commux.stats()
+
     results = []
     size = args.min_bytes
     sizes = []
@@ -87,6 +98,7 @@ def main():
                             call()
                         torch.cuda.synchronize()
                         dist.barrier()
+                        before = path_counters() if gname == "commux" else None
                         e0 = torch.cuda.Event(enable_timing=True)
                         e1 = torch.cuda.Event(enable_timing=True)
                         e0.record()
@@ -104,6 +116,13 @@ def main():
                         # NVLink roofline: bus bandwidth against the measured
                         # 770 GB/s per direction of one GPU's links
                         row[f"{gname}_frac_of_nvlink"] = round(busbw / 770.0, 3)
+                        if before is not None:
+                            # the device algorithm(s) the timed calls took on
+                            # this rank (counter deltas); "none": no device
+                            # kernel ran (host staging, e.g. ranks sharing a GPU)
+                            after = path_counters()
+                            row["commux_path"] = "+".join(
+                                k for k in PATHS if after.get(f"coll_{k}", 0) > before.get(f"coll_{k}", 0)) or "none"
                     if rank == 0:
                         print(json.dumps(row), flush=True)
                     results.append(row)
