@@ -42,6 +42,9 @@ class _Unbuilt:
             f"Original error: {self._err}")
 
 
+# On a reload after an in-process build the module still holds the stand-in
+# of the first import; drop it so the import below finds the built module.
+globals().pop("_C", None)
 try:
     from . import _C  # noqa: F401
 except ImportError as _e:  # the build module itself imports this package

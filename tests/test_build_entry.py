@@ -61,3 +61,17 @@ def test_empty_batches_are_rejected_clearly():
     r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300,
                        env=dict(os.environ, PYTHONPATH=ROOT))
     assert r.returncode == 0 and "empty ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+def test_reload_after_in_process_build_finds_the_extension():
+    # build() imports the package before the extension exists (the package
+    # then holds a stand-in for _C) and reloads it once the build is done.
+    code = ("import importlib, commux_b200 as c\n"
+            "c._C = c._Unbuilt(ImportError('not built yet'))\n"
+            "importlib.reload(c)\n"
+            "assert not isinstance(c._C, c._Unbuilt), c._C\n"
+            "assert c.make_ucp_tag(1, 2) is not None\n"
+            "print('reload ok')\n")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300,
+                       env=dict(os.environ, PYTHONPATH=ROOT))
+    assert r.returncode == 0 and "reload ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
