@@ -1,7 +1,10 @@
 // IOContext: collective file primitives over a private commux group
 // (behaviour of reference: src/io.cpp:43-192). Error agreement is one
 // allreduce-MAX of the local errno, so every rank raises, all with the same
-// errno (the largest of those that failed); sizes and payloads travel on the collective tag namespace.
+// errno (the largest of those that failed). Sizes travel in collectives
+// (broadcast, allgather); gathered payloads are sends with tag kDataTag on
+// the context's private group (send_bytes/recv_bytes callers should keep
+// that tag free while a gather runs).
 
 #include "commux/io.hpp"
 
